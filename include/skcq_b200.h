@@ -1,0 +1,229 @@
+/*
+ * skcq_b200 -- C ABI of the B200 (sm_100a) kernels behind the SKCQ codebook
+ * build and codebook-expert forward paths.
+ *
+ * Conventions (every entry point):
+ *   - plain pointers and sizes, no framework types; all data pointers are
+ *     DEVICE pointers unless documented as host;
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy stream); calls
+ *     are stream-ordered and asynchronous;
+ *   - return 0 (SKCQ_OK) or a negative status; skcq_last_error() returns the
+ *     message of the calling thread's most recent failure. Nothing throws.
+ *
+ * The reference (levzlotnik/SKCQ) is pure Python/PyTorch; each entry point
+ * below names the reference function whose device work it replaces.
+ *
+ * Layout vocabulary for one k-means "problem set" (nblk independent
+ * problems of dimension bs, e.g. one per column block of a weight matrix):
+ *   X [nblk][n_pad][bs]  f32  assignment points (cosine: unit rows)
+ *   R [nblk][n_pad][bs]  f32  update points (cosine: raw rows; l2: = X)
+ *   C [nblk][k_pad][bs]  f32  centroids
+ *   n[nblk], k[nblk]     i32  valid points / centroids of each problem
+ *   active[nblk]         i32  1 while the problem still iterates
+ *   labels [nblk][n_pad] i32
+ * n_pad is a multiple of SKCQ_ROWS_PER_UNIT and k_pad of SKCQ_CENT_TILE.
+ * metric: 0 = cosine (maximise x.c), 1 = euclidean (minimise ||c||^2 - 2 x.c).
+ */
+#ifndef SKCQ_B200_H
+#define SKCQ_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SKCQ_OK 0
+#define SKCQ_ERR_INVALID (-1)     /* bad argument: size, alignment, null pointer */
+#define SKCQ_ERR_CUDA (-2)        /* CUDA runtime / launch error */
+#define SKCQ_ERR_DEVICE (-3)      /* a device-side check or bounded wait failed */
+#define SKCQ_ERR_FLIP_INDEX (-5)  /* spherical flip label >= block size (IndexError in the reference) */
+
+#define SKCQ_METRIC_COSINE 0
+#define SKCQ_METRIC_L2 1
+
+#define SKCQ_ROWS_PER_UNIT 256 /* rows of points one assignment work unit owns */
+#define SKCQ_CENT_TILE 128     /* centroids per tensor-core tile */
+
+/* Copies the calling thread's last error message into buf (NUL-terminated). */
+int skcq_last_error(char* buf, size_t len);
+/* ABI version of this library (bumped on any signature change). */
+int skcq_abi_version(void);
+/* Synchronises `stream`, then returns SKCQ_ERR_DEVICE (and clears the word) if
+ * any kernel recorded a device-side failure (a bounded wait that gave up, an
+ * inconsistent reseed selection), else SKCQ_OK. */
+int skcq_poll_device_error(void* stream);
+
+/* Packed operand width: tf32 columns per point/centroid for the split-precision
+ * tensor-core assignment (3*bs products, +2 bias columns for euclidean, rounded
+ * up to the tf32 MMA K of 8). Host-side helper, no device work. */
+int skcq_packed_width(int metric, int bs);
+
+/* ---- point preparation (skcq/codebook/spherical.py:243-262,
+ *      skcq/codebook/euclidean.py:455-478: block zero test and compaction) --- */
+
+/* For each problem, lists the source points whose block norm is >= thr (all
+ * points when skip_zeros == 0) in ascending order into rowmap[b][*] and their
+ * count into n_out[b]. Source point p of problem b is row p, columns
+ * [b*bs, b*bs+bs) of W (row-major, leading dimension ld); with shared != 0 there
+ * is one problem whose point p is row p / n_blocks, block p % n_blocks. */
+int skcq_compact_points(const float* W, int64_t ld, int n_rows, int bs, int n_blocks, int shared, float thr,
+                        int skip_zeros, int nblk, int npts_pad, int32_t* rowmap, int32_t* n_out, void* stream);
+
+/* Gathers the listed points: R[b][i] = point(rowmap[b][i]) and
+ * X[b][i] = normalize(R[b][i]) (normalize != 0, F.normalize eps 1e-12) or = R.
+ * Rows i >= n[b] are zero-filled. R may be NULL. */
+int skcq_gather_points(const float* W, int64_t ld, int bs, int n_blocks, int shared, int nblk, const int32_t* rowmap,
+                       const int32_t* n, int n_pad, int normalize, float* X, float* R, void* stream);
+
+/* Writes the split-tf32 tensor-core operand of the points
+ * (A[nblk][n_pad/8][kp/4][8][4], kp = skcq_packed_width). */
+int skcq_pack_points(int metric, const float* X, int nblk, int n_pad, int bs, float* A, void* stream);
+
+/* C[b][c] = X[b][perm[b][c]] for c < k[b]: the Forgy initialisation of
+ * skcq/codebook/kmeans.py:201-202 given torch.randperm's draw. */
+int skcq_init_from_points(const float* X, int n_pad, int bs, int nblk, const int64_t* perm, int64_t perm_ld,
+                          const int32_t* k, int k_pad, float* C, void* stream);
+
+/* ---- Lloyd iteration (skcq/codebook/kmeans.py:136-249) --------------------- */
+
+/* Writes the split-tf32 operand of the centroids (B[nblk][k_pad/8][kp/4][8][4];
+ * euclidean adds -||c||^2/2 as two bias columns) and cnorm[b][c] = ||c||^2
+ * (kmeans.py:59). Problems with active[b] == 0 are skipped. */
+int skcq_pack_centroids(int metric, const float* C, int nblk, int k_pad, int bs, const int32_t* k,
+                        const int32_t* active, float* B, float* cnorm, void* stream);
+
+/* Nearest centroid of every point of every active problem: assign_cosine /
+ * assign_l2 (kmeans.py:25-66). tcgen05 kind::tf32 GEMM of the split operands
+ * with the arg-max fused into the tensor-memory epilogue; the winning group of
+ * 32 centroids is re-scored in exact fp32 with the reference formula. */
+int skcq_assign(int metric, const float* A, const float* B, const float* X, const float* C, const float* cnorm,
+                int nblk, int n_pad, int k_pad, int bs, const int32_t* n, const int32_t* k, const int32_t* active,
+                int32_t* labels, void* stream);
+
+/* Same contract as skcq_assign, computed with fp32 FMAs on CUDA cores over all
+ * centroids (the reference formula everywhere). Used to cross-check. */
+int skcq_assign_exact(int metric, const float* X, const float* C, const float* cnorm, int nblk, int n_pad, int k_pad,
+                      int bs, const int32_t* n, const int32_t* k, const int32_t* active, int32_t* labels,
+                      void* stream);
+
+/* Segmented sums and counts of the update (kmeans.py:152-159 / 210-217):
+ * sums[b][labels[b][i]] += R[b][i], counts[b][labels[b][i]] += 1.
+ * sums/counts must be zero on entry (skcq_finalize leaves them zeroed). */
+int skcq_update(const float* R, const int32_t* labels, int nblk, int n_pad, int k_pad, int bs, const int32_t* n,
+                const int32_t* k, const int32_t* active, float* sums, int32_t* counts, void* stream);
+
+/* Empty-cluster reseed (kmeans.py:161-172, 219-230): for each active problem
+ * with empty clusters, the n_empty worst-fit points (cosine: lowest
+ * <x, c_label>; euclidean: largest ||x - c_label||^2; ties by point index)
+ * are written, in that order, into the sums of the empty clusters in
+ * ascending cluster order. n_empty[b] receives the count. `scratch` must hold
+ * skcq_reseed_scratch_bytes(nblk, k_pad) bytes. */
+size_t skcq_reseed_scratch_bytes(int nblk, int k_pad);
+int skcq_reseed(int metric, const float* X, const float* C, const int32_t* labels, int nblk, int n_pad, int k_pad,
+                int bs, const int32_t* n, const int32_t* k, const int32_t* active, float* sums,
+                const int32_t* counts, int32_t* n_empty, void* scratch, void* stream);
+
+/* New centroids, movement and convergence (kmeans.py:174-188, 231-244):
+ * cosine C = normalize(sums); euclidean C = sums / counts (reseeded clusters
+ * take the point). moved = ||C_new - C_old||_F; a problem whose moved < 1e-6
+ * stops (active = 0, converged = 1). Records moved_hist[iter][b] and
+ * nempty_hist[iter][b], sets iters_run[b] = iter + 1, and zeroes sums/counts. */
+int skcq_finalize(int metric, float* sums, int32_t* counts, const int32_t* n_empty, int nblk, int k_pad, int bs,
+                  const int32_t* k, int32_t* active, int32_t* converged, int32_t* iters_run, float* moved_hist,
+                  int32_t* nempty_hist, int iter, float* C, void* stream);
+
+/* ---- codec post-processing ------------------------------------------------- */
+
+/* Negative-scale flip of skcq/codebook/spherical.py:289-298: scale = <R, C[label]>;
+ * flags[b] gets bit j set when some point with a negative scale has label j
+ * (j < 63), and bit 63 when such a label is >= bs (the reference then raises
+ * IndexError: it negates *columns* of the (k, d) centroid matrix). */
+int skcq_flip_check(const float* R, const float* C, const int32_t* labels, int nblk, int n_pad, int k_pad, int bs,
+                    const int32_t* n, uint64_t* flags, void* stream);
+/* Negates dimension j of every centroid of problem b for each bit j set in
+ * flags[b] (the reference's `centroids[:, neg_labels] = -centroids[:, neg_labels]`). */
+int skcq_apply_flip(const uint64_t* flags, int nblk, int k_pad, int bs, float* C, void* stream);
+
+/* idxs (n_blocks, n_rows) int64: labels of compacted points scattered back to
+ * their source (row, block); unlisted (zero) points get label 0
+ * (spherical.py:301-302, euclidean.py:500-501, shared reshape at :159 / :398). */
+int skcq_scatter_labels(const int32_t* labels, const int32_t* rowmap, const int32_t* n, int nblk, int n_pad,
+                        int shared, int n_rows, int n_blocks, int64_t* idxs, void* stream);
+
+/* out[r] = 1 when ||W[r, :in_dim]|| < thr (the row zero mask of
+ * aqlm.py:146-147 / spherical.py:150-151), else 0. */
+int skcq_row_zero_mask(const float* W, int64_t ld, int n_rows, int in_dim, float thr, uint8_t* out, void* stream);
+
+/* Spherical scales (spherical.py:178-184): scales[r][b] = <W[r, block b], C[idx]>,
+ * 0 for rows flagged in row_zero. C is the fp32 centroid set (one problem when
+ * shared). */
+int skcq_spherical_scales(const float* W, int64_t ld, int n_rows, int bs, int n_blocks, int shared, const float* C,
+                          int k_pad, const int64_t* idxs, const uint8_t* row_zero, float* scales, void* stream);
+
+/* out[b][j][c] = bf16(C[b][c][j]) for c < K: the (n_blocks, bs, K) bf16
+ * centroid tensor of spherical.py:176,188 / euclidean.py:415,419. */
+int skcq_centroids_to_bf16(const float* C, int nblk, int k_pad, int bs, int K, uint16_t* out, void* stream);
+
+/* out[r][c] = bf16(W[r][col0 + c]) (raw remainder, spherical.py:186). */
+int skcq_copy_remainder(const float* W, int64_t ld, int n_rows, int col0, int rem, uint16_t* out, void* stream);
+
+/* SSVQ fold (skcq/codebook/ssvq.py:43-53): s = sign(w) with 0 -> +1,
+ * folded = w * s (f32), signs = s (int8), optional packed[r][w] bit (c%32) of
+ * word c/32 set when s = -1. W is f32 (w_is_bf16 = 0) or bf16 bits. */
+int skcq_ssvq_fold(const void* W, int w_is_bf16, int64_t ld, int n_rows, int in_dim, float* folded, int8_t* signs,
+                   uint32_t* packed, void* stream);
+
+/* Symmetric int<bits> fake quantisation of centroids, one scale per centroid
+ * index over all blocks and dims (spherical.py:306-315, euclidean.py:186-195).
+ * cb is the (rows = n_blocks*bs, K) bf16 tensor, updated in place. */
+int skcq_quantize_centroids(uint16_t* cb, int rows, int K, int bits, void* stream);
+
+/* int<bits> scale quantisation (spherical.py:57-69): q_scale = max|s|/levels,
+ * q = clamp(rint(s / q_scale)); out is int8 (bits <= 8) or int16. q_scale is
+ * written to *q_scale_out (device f32). When max|s| == 0 `out` is not written
+ * and q_scale is 0, as in the reference. */
+int skcq_quantize_scales(const float* scales, int64_t count, int bits, void* out, float* q_scale_out,
+                         void* stream);
+
+/* One codebook of a composite, as stored in its CWR (skcq/codebook/cwr.py). */
+typedef struct skcq_codec_desc {
+  int kind;              /* 0 spherical (scaled), 1 euclidean */
+  int bs, n_blocks, K;   /* block size, blocks covered, centroids per block */
+  int shared;            /* 1: one codebook for all blocks */
+  const uint16_t* cent;  /* bf16 (shared ? 1 : n_blocks, bs, K) */
+  const int64_t* idxs;   /* (n_blocks, idx_ld) */
+  int64_t idx_ld;
+  const void* scales;    /* (n_rows, scale_ld) or NULL */
+  int scale_dtype;       /* 0 f32, 1 bf16, 2 f16, 3 int8, 4 int16 */
+  float q_scale;         /* multiplier for int scales */
+  int64_t scale_ld;
+  const uint16_t* rem;   /* bf16 (n_rows, rem) or NULL */
+  int rem_cols;
+  const int8_t* signs;   /* int8 +-1 (n_rows, sign_ld) or NULL (SSVQ) */
+  int sign_cols;         /* signed columns: min(in_dim, signs width) */
+  int64_t sign_ld;
+} skcq_codec_desc;
+
+#define SKCQ_MAX_CODECS 8
+
+/* Composite decode (aqlm.py:137-141 over spherical.py:192-211,
+ * euclidean.py:103-120, ssvq.py:57-66): out[r][c] = sum over codecs, in order,
+ * of each codec's reconstruction; with raw != NULL, out = raw - that sum
+ * (the AQLM residual target, aqlm.py:179/189). One streaming pass. */
+int skcq_reconstruct(const skcq_codec_desc* codecs, int n_codecs, int n_rows, int in_dim, const float* raw,
+                     int64_t raw_ld, float* out, int64_t out_ld, void* stream);
+
+/* Least-squares primary scale re-fit (aqlm.py:147-179), in place on the f32
+ * scales (n_rows, scale_ld) of `primary` (kind 0; signs honoured; its `scales`
+ * field is ignored in favour of `scales`). recon is the full composite
+ * reconstruction; rows flagged in row_zero get 0. */
+int skcq_refit_scales(const skcq_codec_desc* primary, const float* raw, int64_t raw_ld, const float* recon,
+                      int64_t recon_ld, int n_rows, const uint8_t* row_zero, float* scales, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SKCQ_B200_H */

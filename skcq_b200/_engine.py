@@ -1,0 +1,349 @@
+"""Device engine: batched k-means problem sets and codec kernels.
+
+Owns the HBM layouts of the batched path and drives the C ABI
+(``include/skcq_b200.h``). One *problem set* is ``nblk`` independent k-means
+problems of dimension ``bs`` (one per column block of a weight matrix, or one
+pooled problem for a shared codebook). All problems advance together, one
+kernel per step for the whole set; a problem that converges freezes
+(``active = 0``) exactly where the reference's per-block loop would stop.
+"""
+
+from __future__ import annotations
+
+from collections.abc import Callable
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from skcq_b200 import _lib
+from skcq_b200._lib import call, ptr, stream
+
+COSINE = 0
+L2 = 1
+ROWS_PER_UNIT = 256  # SKCQ_ROWS_PER_UNIT
+CENT_TILE = 128  # SKCQ_CENT_TILE
+
+
+def round_up(x: int, m: int) -> int:
+    return (max(x, 1) + m - 1) // m * m
+
+
+def cuda_device(requested: torch.device | str | None, like: torch.Tensor) -> torch.device:
+    """The CUDA device a fit runs on: the requested one, else the input's, else
+    the current device. There is no CPU path."""
+    dev = torch.device(requested) if requested is not None else like.device
+    if dev.type == "cuda":
+        return dev
+    if not torch.cuda.is_available():
+        raise RuntimeError("skcq_b200 needs a CUDA device (B200, sm_100a); none is available")
+    return torch.device("cuda", torch.cuda.current_device())
+
+
+@dataclass
+class PointSet:
+    """Gathered points of one problem set (layouts per include/skcq_b200.h)."""
+
+    metric: int
+    nblk: int
+    bs: int
+    n_pad: int
+    n: torch.Tensor  # int32 [nblk]
+    n_host: list[int]
+    rowmap: torch.Tensor  # int32 [nblk, n_pad]
+    X: torch.Tensor  # f32 [nblk, n_pad, bs]
+    R: torch.Tensor  # f32 [nblk, n_pad, bs]; the same tensor as X for euclidean
+    _A: torch.Tensor | None = None
+
+    @property
+    def kp(self) -> int:
+        return packed_width(self.metric, self.bs)
+
+    def packed(self) -> torch.Tensor:
+        if self._A is None:
+            self._A = torch.empty(self.nblk, self.n_pad * self.kp, dtype=torch.float32, device=self.X.device)
+            call("skcq_pack_points", self.metric, ptr(self.X), self.nblk, self.n_pad, self.bs, ptr(self._A), stream())
+        return self._A
+
+
+def packed_width(metric: int, bs: int) -> int:
+    return int(_lib.load().skcq_packed_width(metric, bs))
+
+
+def gather_block_points(
+    w: torch.Tensor, bs: int, n_blocks: int, shared: bool, thr: float, skip_zeros: bool, metric: int
+) -> PointSet:
+    """Block zero test + compaction + gather (spherical.py:243-248, euclidean.py:455-460)."""
+    assert w.dtype == torch.float32 and w.is_cuda and w.stride(1) == 1
+    n_rows = w.shape[0]
+    nblk = 1 if shared else n_blocks
+    npts = n_rows * n_blocks if shared else n_rows
+    n_pad = round_up(npts, ROWS_PER_UNIT)
+    dev = w.device
+    rowmap = torch.empty(nblk, n_pad, dtype=torch.int32, device=dev)
+    n = torch.empty(nblk, dtype=torch.int32, device=dev)
+    s = stream()
+    call("skcq_compact_points", ptr(w), w.stride(0), n_rows, bs, n_blocks, int(shared), float(thr),
+         int(skip_zeros), nblk, n_pad, ptr(rowmap), ptr(n), s)
+    return _gather(w, bs, n_blocks, shared, metric, rowmap, n, n_pad)
+
+
+def _gather(w, bs, n_blocks, shared, metric, rowmap, n, n_pad) -> PointSet:
+    nblk = rowmap.shape[0]
+    dev = w.device
+    X = torch.empty(nblk, n_pad, bs, dtype=torch.float32, device=dev)
+    R = torch.empty_like(X) if metric == COSINE else None
+    call("skcq_gather_points", ptr(w), w.stride(0), bs, n_blocks, int(shared), nblk, ptr(rowmap), ptr(n), n_pad,
+         int(metric == COSINE), ptr(X), ptr(R), stream())
+    n_host = [int(v) for v in n.cpu().tolist()]
+    return PointSet(metric, nblk, bs, n_pad, n, n_host, rowmap, X, R if R is not None else X)
+
+
+def subsample_points(w, bs, n_blocks, shared, pts: PointSet, perms: list[torch.Tensor | None], m: int) -> PointSet:
+    """Training subset ``non_zero[perm[:m]]`` per problem (spherical.py:263-268)."""
+    n_train = [min(nb, m) if p is not None else nb for nb, p in zip(pts.n_host, perms, strict=True)]
+    n_pad = round_up(max(n_train), ROWS_PER_UNIT)
+    rm = torch.zeros(pts.nblk, n_pad, dtype=torch.int32, device=w.device)
+    for b, p in enumerate(perms):
+        if p is None:
+            rm[b, : pts.n_host[b]] = pts.rowmap[b, : pts.n_host[b]]
+        else:
+            rm[b, : n_train[b]] = pts.rowmap[b][p[:m].to(w.device)]
+    n = torch.tensor(n_train, dtype=torch.int32, device=w.device)
+    return _gather(w, bs, n_blocks, shared, pts.metric, rm, n, n_pad)
+
+
+@dataclass
+class KmeansRun:
+    """Result of one batched Lloyd run (skcq/codebook/kmeans.py:109-249)."""
+
+    C: torch.Tensor  # f32 [nblk, k_pad, bs]
+    k_pad: int
+    k_host: list[int]
+    labels: torch.Tensor  # int32 [nblk, n_pad] of the final assignment
+    iters_run: list[int]
+    converged: list[bool]
+    moved: np.ndarray  # [max_iters, nblk]
+    n_empty: np.ndarray  # [max_iters, nblk]
+    cnorm: torch.Tensor = field(repr=False, default=None)
+
+    def final_moved(self, b: int) -> float:
+        it = self.iters_run[b]
+        return float(self.moved[it - 1, b]) if it > 0 else 0.0
+
+
+def lloyd(
+    pts: PointSet,
+    K: int,
+    max_iters: int,
+    init_cosine: Callable[[int, int], torch.Tensor] | None = None,
+    init_perms: list[torch.Tensor | None] | None = None,
+) -> KmeansRun:
+    """Run every problem of ``pts`` to convergence or ``max_iters``.
+
+    Cosine problems start from ``init_cosine(k_eff, bs)`` (the Sobol directions
+    of kmeans.py:69-74); euclidean problems from ``X[b][init_perms[b][:k_eff]]``
+    (kmeans.py:201-202). Problems with no points are left inactive.
+    """
+    dev = pts.X.device
+    nblk, bs, n_pad, metric = pts.nblk, pts.bs, pts.n_pad, pts.metric
+    k_host = [min(K, nb) for nb in pts.n_host]
+    k_pad = round_up(max(k_host + [1]), CENT_TILE)
+    kp = pts.kp
+    s = stream()
+    k_dev = torch.tensor(k_host, dtype=torch.int32, device=dev)
+    active = (pts.n > 0).to(torch.int32)
+    C = torch.zeros(nblk, k_pad, bs, dtype=torch.float32, device=dev)
+    if metric == COSINE:
+        cache: dict[int, torch.Tensor] = {}
+        for b, kb in enumerate(k_host):
+            if kb > 0:
+                if kb not in cache:
+                    cache[kb] = init_cosine(kb, bs).to(device=dev, dtype=torch.float32)
+                C[b, :kb] = cache[kb]
+    else:
+        perm = torch.zeros(nblk, k_pad, dtype=torch.int64, device=dev)
+        for b, kb in enumerate(k_host):
+            if kb > 0:
+                perm[b, :kb] = init_perms[b][:kb].to(dev)
+        call("skcq_init_from_points", ptr(pts.X), n_pad, bs, nblk, ptr(perm), k_pad, ptr(k_dev), k_pad, ptr(C), s)
+    A = pts.packed()
+    B = torch.empty(nblk, k_pad * kp, dtype=torch.float32, device=dev)
+    cnorm = torch.empty(nblk, k_pad, dtype=torch.float32, device=dev)
+    sums = torch.zeros(nblk, k_pad, bs, dtype=torch.float32, device=dev)
+    counts = torch.zeros(nblk, k_pad, dtype=torch.int32, device=dev)
+    labels = torch.zeros(nblk, n_pad, dtype=torch.int32, device=dev)
+    n_empty = torch.zeros(nblk, dtype=torch.int32, device=dev)
+    scratch = torch.empty(int(_lib.load().skcq_reseed_scratch_bytes(nblk, k_pad)), dtype=torch.uint8, device=dev)
+    converged = torch.zeros(nblk, dtype=torch.int32, device=dev)
+    iters_run = torch.zeros(nblk, dtype=torch.int32, device=dev)
+    moved = torch.zeros(max(max_iters, 1), nblk, dtype=torch.float32, device=dev)
+    nempty_hist = torch.zeros(max(max_iters, 1), nblk, dtype=torch.int32, device=dev)
+    flag = torch.empty(1, dtype=torch.int32, pin_memory=True)
+    for it in range(max_iters):
+        call("skcq_pack_centroids", metric, ptr(C), nblk, k_pad, bs, ptr(k_dev), ptr(active), ptr(B), ptr(cnorm), s)
+        call("skcq_assign", metric, ptr(A), ptr(B), ptr(pts.X), ptr(C), ptr(cnorm), nblk, n_pad, k_pad, bs,
+             ptr(pts.n), ptr(k_dev), ptr(active), ptr(labels), s)
+        call("skcq_update", ptr(pts.R), ptr(labels), nblk, n_pad, k_pad, bs, ptr(pts.n), ptr(k_dev), ptr(active),
+             ptr(sums), ptr(counts), s)
+        call("skcq_reseed", metric, ptr(pts.X), ptr(C), ptr(labels), nblk, n_pad, k_pad, bs, ptr(pts.n), ptr(k_dev),
+             ptr(active), ptr(sums), ptr(counts), ptr(n_empty), ptr(scratch), s)
+        call("skcq_finalize", metric, ptr(sums), ptr(counts), ptr(n_empty), nblk, k_pad, bs, ptr(k_dev),
+             ptr(active), ptr(converged), ptr(iters_run), ptr(moved), ptr(nempty_hist), it, ptr(C), s)
+        flag.copy_(active.max().reshape(1), non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        if int(flag.item()) == 0:
+            break
+    _lib.poll_device_error()
+    # final assignment with the final centroids (kmeans.py:190 / 246)
+    call("skcq_pack_centroids", metric, ptr(C), nblk, k_pad, bs, ptr(k_dev), None, ptr(B), ptr(cnorm), s)
+    call("skcq_assign", metric, ptr(A), ptr(B), ptr(pts.X), ptr(C), ptr(cnorm), nblk, n_pad, k_pad, bs,
+         ptr(pts.n), ptr(k_dev), None, ptr(labels), s)
+    return KmeansRun(
+        C=C, k_pad=k_pad, k_host=k_host, labels=labels,
+        iters_run=[int(v) for v in iters_run.cpu().tolist()],
+        converged=[bool(v) for v in converged.cpu().tolist()],
+        moved=moved.cpu().numpy(), n_empty=nempty_hist.cpu().numpy(), cnorm=cnorm,
+    )
+
+
+def assign(pts: PointSet, run: KmeansRun) -> torch.Tensor:
+    """Labels of ``pts`` against the (already packed) centroids of ``run``."""
+    dev = pts.X.device
+    B = torch.empty(pts.nblk, run.k_pad * pts.kp, dtype=torch.float32, device=dev)
+    k_dev = torch.tensor(run.k_host, dtype=torch.int32, device=dev)
+    labels = torch.zeros(pts.nblk, pts.n_pad, dtype=torch.int32, device=dev)
+    s = stream()
+    call("skcq_pack_centroids", pts.metric, ptr(run.C), pts.nblk, run.k_pad, pts.bs, ptr(k_dev), None, ptr(B),
+         ptr(run.cnorm), s)
+    call("skcq_assign", pts.metric, ptr(pts.packed()), ptr(B), ptr(pts.X), ptr(run.C), ptr(run.cnorm), pts.nblk,
+         pts.n_pad, run.k_pad, pts.bs, ptr(pts.n), ptr(k_dev), None, ptr(labels), s)
+    return labels
+
+
+def scatter_labels(pts: PointSet, labels: torch.Tensor, shared: bool, n_rows: int, n_blocks: int) -> torch.Tensor:
+    idxs = torch.empty(n_blocks, n_rows, dtype=torch.int64, device=labels.device)
+    call("skcq_scatter_labels", ptr(labels), ptr(pts.rowmap), ptr(pts.n), pts.nblk, pts.n_pad, int(shared), n_rows,
+         n_blocks, ptr(idxs), stream())
+    return idxs
+
+
+def row_zero_mask(w: torch.Tensor, thr: float) -> torch.Tensor:
+    out = torch.empty(w.shape[0], dtype=torch.uint8, device=w.device)
+    call("skcq_row_zero_mask", ptr(w), w.stride(0), w.shape[0], w.shape[1], float(thr), ptr(out), stream())
+    return out
+
+
+def centroids_bf16(C: torch.Tensor, k_pad: int, bs: int, K: int) -> torch.Tensor:
+    nblk = C.shape[0]
+    out = torch.empty(nblk, bs, K, dtype=torch.bfloat16, device=C.device)
+    call("skcq_centroids_to_bf16", ptr(C), nblk, k_pad, bs, K, ptr(out), stream())
+    return out
+
+
+def remainder_bf16(w: torch.Tensor, col0: int) -> torch.Tensor | None:
+    rem = w.shape[1] - col0
+    if rem <= 0:
+        return None
+    out = torch.empty(w.shape[0], rem, dtype=torch.bfloat16, device=w.device)
+    call("skcq_copy_remainder", ptr(w), w.stride(0), w.shape[0], col0, rem, ptr(out), stream())
+    return out
+
+
+def ssvq_fold(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """(folded f32, signs int8) of ssvq.py:43-53."""
+    if w.dtype not in (torch.float32, torch.bfloat16):
+        w = w.float()
+    w = w.contiguous() if w.stride(-1) != 1 else w
+    n_rows, in_dim = w.shape
+    folded = torch.empty(n_rows, in_dim, dtype=torch.float32, device=w.device)
+    signs = torch.empty(n_rows, in_dim, dtype=torch.int8, device=w.device)
+    call("skcq_ssvq_fold", ptr(w), int(w.dtype == torch.bfloat16), w.stride(0), n_rows, in_dim, ptr(folded),
+         ptr(signs), None, stream())
+    return folded, signs
+
+
+def quantize_centroids_(cb: torch.Tensor, bits: int) -> torch.Tensor:
+    """In-place int<bits> fake quantisation of a (n_blocks, bs, K) bf16 tensor."""
+    assert cb.dtype == torch.bfloat16 and cb.is_contiguous()
+    K = cb.shape[-1]
+    call("skcq_quantize_centroids", ptr(cb), cb.numel() // K, K, int(bits), stream())
+    return cb
+
+
+def quantize_scales_int(scales: torch.Tensor, bits: int) -> tuple[torch.Tensor | None, torch.Tensor]:
+    """(quantised scales or None when max|s| == 0, q_scale 0-d f32)."""
+    s = scales.float().contiguous()
+    out = torch.empty(s.shape, dtype=torch.int8 if bits <= 8 else torch.int16, device=s.device)
+    q = torch.empty(1, dtype=torch.float32, device=s.device)
+    call("skcq_quantize_scales", ptr(s), s.numel(), int(bits), ptr(out), ptr(q), stream())
+    q_scale = q.reshape(())
+    if float(q_scale) == 0.0:
+        return None, q_scale
+    return out, q_scale
+
+
+# ---------------------------------------------------------------------------
+# Composite decode
+# ---------------------------------------------------------------------------
+
+_SCALE_CODES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2, torch.int8: 3, torch.int16: 4}
+
+
+@dataclass
+class CodecView:
+    """Device tensors of one codebook of a composite, ready for the C ABI."""
+
+    kind: int  # 0 spherical, 1 euclidean
+    bs: int
+    n_blocks: int
+    K: int
+    shared: bool
+    cent: torch.Tensor  # bf16 (n_cb, bs, K), contiguous
+    idxs: torch.Tensor  # int64 (n_blocks, >= n_rows) with unit column stride
+    scales: torch.Tensor | None = None
+    q_scale: float = 1.0
+    rem: torch.Tensor | None = None  # bf16 (n_rows, rem) contiguous
+    signs: torch.Tensor | None = None  # int8 (n_rows, >= sign_cols)
+    sign_cols: int = 0
+
+    def desc(self) -> _lib.CodecDesc:
+        d = _lib.CodecDesc()
+        d.kind, d.bs, d.n_blocks, d.K, d.shared = self.kind, self.bs, self.n_blocks, self.K, int(self.shared)
+        d.cent = ptr(self.cent)
+        d.idxs = ptr(self.idxs)
+        d.idx_ld = self.idxs.stride(0) if self.idxs.dim() == 2 and self.n_blocks > 0 else 0
+        if self.scales is not None:
+            d.scales = ptr(self.scales)
+            d.scale_dtype = _SCALE_CODES[self.scales.dtype]
+            d.q_scale = float(self.q_scale)
+            d.scale_ld = self.scales.stride(0)
+        if self.rem is not None:
+            d.rem = ptr(self.rem)
+            d.rem_cols = self.rem.shape[1]
+        if self.signs is not None:
+            d.signs = ptr(self.signs)
+            d.sign_cols = self.sign_cols
+            d.sign_ld = self.signs.stride(0)
+        return d
+
+
+def reconstruct(views: list[CodecView], n_rows: int, in_dim: int, raw: torch.Tensor | None = None,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """sum of the codecs' reconstructions, or ``raw - sum`` when raw is given."""
+    dev = views[0].cent.device
+    if out is None:
+        out = torch.empty(n_rows, in_dim, dtype=torch.float32, device=dev)
+    arr = (_lib.CodecDesc * len(views))(*[v.desc() for v in views])
+    call("skcq_reconstruct", _lib.C.cast(arr, _lib.C.c_void_p), len(views), n_rows, in_dim,
+         ptr(raw), raw.stride(0) if raw is not None else 0, ptr(out), out.stride(0), stream())
+    return out
+
+
+def refit_scales(primary: CodecView, raw: torch.Tensor, recon: torch.Tensor, row_zero: torch.Tensor,
+                 scales: torch.Tensor) -> None:
+    d = primary.desc()
+    d.scale_dtype = 0
+    d.scale_ld = scales.stride(0)
+    call("skcq_refit_scales", _lib.C.addressof(d), ptr(raw), raw.stride(0), ptr(recon), recon.stride(0),
+         raw.shape[0], ptr(row_zero), ptr(scales), stream())

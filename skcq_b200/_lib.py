@@ -1,0 +1,121 @@
+"""ctypes binding of ``libskcq_b200.so`` (the C ABI in ``include/skcq_b200.h``).
+
+Every call passes raw device pointers and the current CUDA stream; a non-zero
+status raises ``RuntimeError`` carrying ``skcq_last_error()``. There is no
+fallback: if the library is missing the import of any compute path fails.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+import torch
+
+_LIB_PATH = Path(__file__).resolve().parent / "libskcq_b200.so"
+
+P = C.c_void_p
+I = C.c_int
+L = C.c_int64
+F = C.c_float
+
+
+class CodecDesc(C.Structure):
+    """``skcq_codec_desc``: one codebook of a composite (include/skcq_b200.h)."""
+
+    _fields_ = [
+        ("kind", I), ("bs", I), ("n_blocks", I), ("K", I), ("shared", I),
+        ("cent", P), ("idxs", P), ("idx_ld", L),
+        ("scales", P), ("scale_dtype", I), ("q_scale", F), ("scale_ld", L),
+        ("rem", P), ("rem_cols", I),
+        ("signs", P), ("sign_cols", I), ("sign_ld", L),
+    ]
+
+
+# name -> argtypes (restype is int unless listed in _RESTYPES)
+_SIGS: dict[str, list] = {
+    "skcq_last_error": [C.c_char_p, C.c_size_t],
+    "skcq_abi_version": [],
+    "skcq_poll_device_error": [P],
+    "skcq_packed_width": [I, I],
+    "skcq_compact_points": [P, L, I, I, I, I, F, I, I, I, P, P, P],
+    "skcq_gather_points": [P, L, I, I, I, I, P, P, I, I, P, P, P],
+    "skcq_pack_points": [I, P, I, I, I, P, P],
+    "skcq_init_from_points": [P, I, I, I, P, L, P, I, P, P],
+    "skcq_pack_centroids": [I, P, I, I, I, P, P, P, P, P],
+    "skcq_assign": [I, P, P, P, P, P, I, I, I, I, P, P, P, P, P],
+    "skcq_assign_exact": [I, P, P, P, I, I, I, I, P, P, P, P, P],
+    "skcq_update": [P, P, I, I, I, I, P, P, P, P, P, P],
+    "skcq_reseed_scratch_bytes": [I, I],
+    "skcq_reseed": [I, P, P, P, I, I, I, I, P, P, P, P, P, P, P, P],
+    "skcq_finalize": [I, P, P, P, I, I, I, P, P, P, P, P, P, I, P, P],
+    "skcq_flip_check": [P, P, P, I, I, I, I, P, P, P],
+    "skcq_apply_flip": [P, I, I, I, P, P],
+    "skcq_scatter_labels": [P, P, P, I, I, I, I, I, P, P],
+    "skcq_row_zero_mask": [P, L, I, I, F, P, P],
+    "skcq_spherical_scales": [P, L, I, I, I, I, P, I, P, P, P, P],
+    "skcq_centroids_to_bf16": [P, I, I, I, I, P, P],
+    "skcq_copy_remainder": [P, L, I, I, I, P, P],
+    "skcq_ssvq_fold": [P, I, L, I, I, P, P, P, P],
+    "skcq_quantize_centroids": [P, I, I, I, P],
+    "skcq_quantize_scales": [P, L, I, P, P, P],
+    "skcq_reconstruct": [P, I, I, I, P, L, P, L, P],
+    "skcq_refit_scales": [P, P, L, P, L, I, P, P, P],
+}
+_RESTYPES = {"skcq_reseed_scratch_bytes": C.c_size_t}
+
+_lib: C.CDLL | None = None
+
+
+def load() -> C.CDLL:
+    """Load (once) and type the shared library; raise if it is absent."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    path = Path(os.environ.get("SKCQ_B200_LIB", _LIB_PATH))
+    if not path.exists():
+        raise RuntimeError(
+            f"skcq_b200 CUDA library not found at {path}; build it with `python -m skcq_b200.build`"
+        )
+    lib = C.CDLL(str(path))
+    for name, args in _SIGS.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = _RESTYPES.get(name, I)
+    _lib = lib
+    return lib
+
+
+def exported_symbols() -> list[str]:
+    return list(_SIGS)
+
+
+def last_error() -> str:
+    buf = C.create_string_buffer(1024)
+    load().skcq_last_error(buf, len(buf))
+    return buf.value.decode(errors="replace")
+
+
+def call(name: str, *args) -> int:
+    """Call ``name`` and raise ``RuntimeError`` on a non-zero status."""
+    rc = getattr(load(), name)(*args)
+    if rc != 0:
+        raise RuntimeError(f"{name} failed ({rc}): {last_error()}")
+    return rc
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise RuntimeError("skcq_b200 kernels take CUDA tensors")
+    return t.data_ptr()
+
+
+def stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def poll_device_error() -> None:
+    call("skcq_poll_device_error", stream())

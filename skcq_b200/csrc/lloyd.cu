@@ -1,0 +1,340 @@
+// Lloyd update, empty-cluster reseed and finalisation for the batched k-means
+// problem sets (skcq/codebook/kmeans.py:152-188 cosine, 210-244 euclidean).
+#include "common.cuh"
+
+namespace skcq {
+
+// ---------------------------------------------------------------------------
+// Update: segmented sums + counts
+// ---------------------------------------------------------------------------
+
+// Shared-memory accumulation: one CTA owns a slice of rows of one problem and
+// the whole (k x (bs+1)) accumulator; flushed with one global atomic per
+// touched entry.
+__global__ void update_smem_kernel(const float* __restrict__ R, const int32_t* __restrict__ labels, int n_pad,
+                                   int k_pad, int bs, const int32_t* __restrict__ n,
+                                   const int32_t* __restrict__ active, const int32_t* __restrict__ kvec,
+                                   int rows_per_cta, float* __restrict__ sums, int32_t* __restrict__ counts) {
+  extern __shared__ float acc[];  // [kb][bs] sums then [kb] counts (as int)
+  const int b = blockIdx.y;
+  if (active && !active[b]) return;
+  const int nb = n[b], kb = kvec[b];
+  const int i0 = blockIdx.x * rows_per_cta;
+  if (i0 >= nb) return;
+  const int i1 = min(nb, i0 + rows_per_cta);
+  int* cnt = reinterpret_cast<int*>(acc + (size_t)kb * bs);
+  for (int t = threadIdx.x; t < kb * (bs + 1); t += blockDim.x) acc[t] = 0.f;
+  __syncthreads();
+  const float* Rb = R + (int64_t)b * n_pad * bs;
+  const int32_t* Lb = labels + (int64_t)b * n_pad;
+  for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+    const int l = Lb[i];
+    const float* x = Rb + (int64_t)i * bs;
+    for (int j = 0; j < bs; ++j) atomicAdd(&acc[l * bs + j], x[j]);
+    atomicAdd(&cnt[l], 1);
+  }
+  __syncthreads();
+  float* Sb = sums + (int64_t)b * k_pad * bs;
+  int32_t* Cb = counts + (int64_t)b * k_pad;
+  for (int c = threadIdx.x; c < kb; c += blockDim.x) {
+    const int m = cnt[c];
+    if (m == 0) continue;
+    atomicAdd(&Cb[c], m);
+    for (int j = 0; j < bs; ++j) atomicAdd(&Sb[c * bs + j], acc[c * bs + j]);
+  }
+}
+
+__global__ void update_global_kernel(const float* __restrict__ R, const int32_t* __restrict__ labels, int nblk,
+                                     int n_pad, int k_pad, int bs, const int32_t* __restrict__ n,
+                                     const int32_t* __restrict__ active, float* __restrict__ sums,
+                                     int32_t* __restrict__ counts) {
+  const int64_t total = (int64_t)nblk * n_pad;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t b = t / n_pad, i = t % n_pad;
+    if (i >= n[b] || (active && !active[b])) continue;
+    const int l = labels[t];
+    const float* x = R + t * bs;
+    float* s = sums + (b * k_pad + l) * bs;
+    for (int j = 0; j < bs; ++j) atomicAdd(&s[j], x[j]);
+    atomicAdd(&counts[b * k_pad + l], 1);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Reseed: worst-fit points into empty clusters
+// ---------------------------------------------------------------------------
+
+constexpr int RS_THREADS = 1024;
+constexpr int RS_SMEM_SORT = 4096;  // sort in shared memory up to this many keys
+
+__device__ __forceinline__ uint64_t reseed_key(int metric, const float* x, const float* c, int bs, int i) {
+  uint32_t k;
+  if (metric == SKCQ_METRIC_COSINE) {
+    // kmeans.py:169-171: sims = <unit_x, c_label>, ascending
+    float s = 0.f;
+    for (int j = 0; j < bs; ++j) s = __fmaf_rn(x[j], c[j], s);
+    k = float_key(s);
+  } else {
+    // kmeans.py:227-229: dists = ||x - c_label||^2, descending
+    float s = 0.f;
+    for (int j = 0; j < bs; ++j) {
+      const float d = __fsub_rn(x[j], c[j]);
+      s = __fmaf_rn(d, d, s);
+    }
+    k = ~float_key(s);
+  }
+  return ((uint64_t)k << 32) | (uint32_t)i;
+}
+
+__device__ void bitonic_sort(uint64_t* a, int P) {
+  for (int k = 2; k <= P; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = threadIdx.x; i < P; i += blockDim.x) {
+        const int ixj = i ^ j;
+        if (ixj > i) {
+          const uint64_t x = a[i], y = a[ixj];
+          const bool up = (i & k) == 0;
+          if ((x > y) == up) {
+            a[i] = y;
+            a[ixj] = x;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+__global__ void __launch_bounds__(RS_THREADS)
+reseed_kernel(int metric, const float* __restrict__ X, const float* __restrict__ C,
+              const int32_t* __restrict__ labels, int nblk, int n_pad, int k_pad, int bs,
+              const int32_t* __restrict__ n, const int32_t* __restrict__ kvec, const int32_t* __restrict__ active,
+              float* __restrict__ sums, const int32_t* __restrict__ counts, int32_t* __restrict__ n_empty_out,
+              uint8_t* scratch, int k_pow2, int* err) {
+  __shared__ uint64_t s_sort[RS_SMEM_SORT];
+  __shared__ int s_hist[256];
+  __shared__ uint64_t s_prefix;
+  __shared__ int s_need, s_done, s_count;
+  int32_t* empty_ids = reinterpret_cast<int32_t*>(scratch + (size_t)blockIdx.x * ((size_t)k_pad * 4 + (size_t)k_pow2 * 8));
+  uint64_t* g_list = reinterpret_cast<uint64_t*>(empty_ids + k_pad);
+  for (int b = blockIdx.x; b < nblk; b += gridDim.x) {
+    if (active && !active[b]) continue;
+    const int nb = n[b], kb = kvec[b];
+    const int32_t* cnt = counts + (int64_t)b * k_pad;
+    // 1. empty clusters, ascending
+    int n_empty = 0;
+    for (int c0 = 0; c0 < kb; c0 += blockDim.x) {
+      const int c = c0 + threadIdx.x;
+      const int e = (c < kb && cnt[c] == 0) ? 1 : 0;
+      int tot;
+      const int pos = block_exclusive_scan(e, &tot);
+      if (e) empty_ids[n_empty + pos] = c;
+      n_empty += tot;
+    }
+    if (threadIdx.x == 0) n_empty_out[b] = n_empty;
+    if (n_empty == 0) continue;
+    const float* Xb = X + (int64_t)b * n_pad * bs;
+    const float* Cb = C + (int64_t)b * k_pad * bs;
+    const int32_t* Lb = labels + (int64_t)b * n_pad;
+    // 2. radix select of the n_empty smallest (score-key, point) composites
+    if (threadIdx.x == 0) {
+      s_prefix = 0;
+      s_need = n_empty;
+      s_done = 0;
+    }
+    __syncthreads();
+    uint64_t thresh = ~0ull;
+    for (int shift = 56; shift >= 0; shift -= 8) {
+      for (int t = threadIdx.x; t < 256; t += blockDim.x) s_hist[t] = 0;
+      __syncthreads();
+      const uint64_t hmask = shift == 56 ? 0ull : (~0ull << (shift + 8));
+      const uint64_t pref = s_prefix;
+      for (int i = threadIdx.x; i < nb; i += blockDim.x) {
+        const uint64_t key = reseed_key(metric, Xb + (int64_t)i * bs, Cb + (int64_t)Lb[i] * bs, bs, i);
+        if ((key & hmask) == (pref & hmask)) atomicAdd(&s_hist[(key >> shift) & 255], 1);
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        int need = s_need, cum = 0, d = 0;
+        for (; d < 255; ++d) {
+          if (cum + s_hist[d] >= need) break;
+          cum += s_hist[d];
+        }
+        need -= cum;
+        s_prefix = pref | ((uint64_t)d << shift);
+        s_need = need;
+        if (s_hist[d] == need) s_done = 1;  // every key under this prefix is selected
+      }
+      __syncthreads();
+      if (s_done) {
+        thresh = s_prefix | (shift == 0 ? 0ull : ((1ull << shift) - 1));
+        break;
+      }
+      if (shift == 0) thresh = s_prefix;
+    }
+    // 3. collect the selected composites
+    int m_pow2 = 1;
+    while (m_pow2 < n_empty) m_pow2 <<= 1;
+    uint64_t* list = m_pow2 <= RS_SMEM_SORT ? s_sort : g_list;
+    if (threadIdx.x == 0) s_count = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < m_pow2; i += blockDim.x) list[i] = ~0ull;
+    __syncthreads();
+    for (int i = threadIdx.x; i < nb; i += blockDim.x) {
+      const uint64_t key = reseed_key(metric, Xb + (int64_t)i * bs, Cb + (int64_t)Lb[i] * bs, bs, i);
+      if (key <= thresh) {
+        const int pos = atomicAdd(&s_count, 1);
+        if (pos < m_pow2) list[pos] = key;
+      }
+    }
+    __syncthreads();
+    if (s_count != n_empty) {
+      if (threadIdx.x == 0) atomicCAS(err, 0, 21);
+      __syncthreads();
+      continue;
+    }
+    // 4. order them (ascending key = worst first)
+    bitonic_sort(list, m_pow2);
+    // 5. the i-th worst point seeds the i-th empty cluster
+    float* Sb = sums + (int64_t)b * k_pad * bs;
+    for (int t = threadIdx.x; t < n_empty * bs; t += blockDim.x) {
+      const int e = t / bs, j = t - e * bs;
+      const uint32_t row = (uint32_t)(list[e] & 0xffffffffu);
+      Sb[(int64_t)empty_ids[e] * bs + j] = Xb[(int64_t)row * bs + j];
+    }
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Finalize
+// ---------------------------------------------------------------------------
+
+__global__ void finalize_kernel(int metric, float* __restrict__ sums, int32_t* __restrict__ counts,
+                                const int32_t* __restrict__ n_empty, int nblk, int k_pad, int bs,
+                                const int32_t* __restrict__ kvec, int32_t* __restrict__ active,
+                                int32_t* __restrict__ converged, int32_t* __restrict__ iters_run,
+                                float* __restrict__ moved_hist, int32_t* __restrict__ nempty_hist, int iter,
+                                float* __restrict__ C) {
+  for (int b = blockIdx.x; b < nblk; b += gridDim.x) {
+    if (!active[b]) continue;
+    const int kb = kvec[b];
+    float* Sb = sums + (int64_t)b * k_pad * bs;
+    int32_t* Nb = counts + (int64_t)b * k_pad;
+    float* Cb = C + (int64_t)b * k_pad * bs;
+    float part = 0.f;
+    for (int c = threadIdx.x; c < kb; c += blockDim.x) {
+      float* s = Sb + (int64_t)c * bs;
+      float* cc = Cb + (int64_t)c * bs;
+      const int cnt = Nb[c];
+      float den;
+      if (metric == SKCQ_METRIC_COSINE) {
+        float q = 0.f;
+        for (int j = 0; j < bs; ++j) q = __fmaf_rn(s[j], s[j], q);
+        den = fmaxf(sqrtf(q), 1e-12f);  // F.normalize
+      } else {
+        den = cnt > 0 ? (float)cnt : 1.f;  // reseeded clusters keep the point
+      }
+      for (int j = 0; j < bs; ++j) {
+        const float nv = (metric == SKCQ_METRIC_COSINE || cnt > 0) ? __fdiv_rn(s[j], den) : s[j];
+        const float d = __fsub_rn(nv, cc[j]);
+        part = __fmaf_rn(d, d, part);
+        cc[j] = nv;
+        s[j] = 0.f;
+      }
+      Nb[c] = 0;
+    }
+    const float tot = block_sum(part);
+    if (threadIdx.x == 0) {
+      const float moved = sqrtf(tot);
+      moved_hist[(int64_t)iter * nblk + b] = moved;
+      nempty_hist[(int64_t)iter * nblk + b] = n_empty[b];
+      iters_run[b] = iter + 1;
+      if (moved < 1e-6f) {
+        active[b] = 0;
+        converged[b] = 1;
+      }
+    }
+    __syncthreads();
+  }
+}
+
+}  // namespace skcq
+
+using namespace skcq;
+
+extern "C" int skcq_update(const float* R, const int32_t* labels, int nblk, int n_pad, int k_pad, int bs,
+                             const int32_t* n, const int32_t* k, const int32_t* active, float* sums,
+                             int32_t* counts, void* stream) {
+  SKCQ_REQUIRE(R && labels && n && k && sums && counts, SKCQ_ERR_INVALID, "update: null pointer");
+  SKCQ_REQUIRE(bs > 0 && bs <= 64, SKCQ_ERR_INVALID, "update: bad block size %d", bs);
+  cudaStream_t s = (cudaStream_t)stream;
+  const size_t smem = (size_t)k_pad * (bs + 1) * sizeof(float);
+  if (smem <= 160 * 1024 && nblk <= 65535) {
+    static thread_local int configured_dev = -1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (configured_dev != dev) {
+      cudaError_t e = cudaFuncSetAttribute(update_smem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+      if (e != cudaSuccess) return set_error(SKCQ_ERR_CUDA, "update: %s", cudaGetErrorString(e));
+      configured_dev = dev;
+    }
+    // enough CTAs to fill the machine, each with at least 4 rows per accumulator entry
+    int64_t rows = (int64_t)nblk * n_pad;
+    int64_t target = 148 * 2;
+    int64_t rpc = (rows + target - 1) / target;
+    int64_t min_rpc = (int64_t)k_pad * 4;
+    if (rpc < min_rpc) rpc = min_rpc;
+    if (rpc > n_pad) rpc = n_pad;
+    dim3 grid((unsigned)((n_pad + rpc - 1) / rpc), nblk);
+    update_smem_kernel<<<grid, 512, smem, s>>>(R, labels, n_pad, k_pad, bs, n, active, k, (int)rpc, sums, counts);
+    return check_launch("update (shared)");
+  }
+  int64_t work = (int64_t)nblk * n_pad;
+  int grid = (int)((work + 255) / 256);
+  if (grid > 148 * 32) grid = 148 * 32;
+  update_global_kernel<<<grid, 256, 0, s>>>(R, labels, nblk, n_pad, k_pad, bs, n, active, sums, counts);
+  return check_launch("update (global)");
+}
+
+static int pow2_at_least(int v) {
+  int p = 1;
+  while (p < v) p <<= 1;
+  return p;
+}
+
+static int reseed_grid(int nblk) { return nblk < 296 ? nblk : 296; }
+
+extern "C" size_t skcq_reseed_scratch_bytes(int nblk, int k_pad) {
+  if (nblk <= 0 || k_pad <= 0) return 0;
+  return (size_t)reseed_grid(nblk) * ((size_t)k_pad * 4 + (size_t)pow2_at_least(k_pad) * 8);
+}
+
+extern "C" int skcq_reseed(int metric, const float* X, const float* C, const int32_t* labels, int nblk, int n_pad,
+                           int k_pad, int bs, const int32_t* n, const int32_t* k, const int32_t* active, float* sums,
+                           const int32_t* counts, int32_t* n_empty, void* scratch, void* stream) {
+  SKCQ_REQUIRE(X && C && labels && n && k && sums && counts && n_empty && scratch, SKCQ_ERR_INVALID,
+               "reseed: null pointer");
+  SKCQ_REQUIRE(bs > 0 && bs <= 64, SKCQ_ERR_INVALID, "reseed: bad block size %d", bs);
+  SKCQ_REQUIRE(((uintptr_t)scratch & 7) == 0, SKCQ_ERR_INVALID, "reseed: scratch must be 8-byte aligned");
+  int* err = device_error_word();
+  SKCQ_REQUIRE(err != nullptr, SKCQ_ERR_CUDA, "reseed: no device error word");
+  cudaStream_t s = (cudaStream_t)stream;
+  cudaError_t e = cudaMemsetAsync(n_empty, 0, sizeof(int32_t) * nblk, s);
+  if (e != cudaSuccess) return set_error(SKCQ_ERR_CUDA, "reseed: %s", cudaGetErrorString(e));
+  reseed_kernel<<<reseed_grid(nblk), RS_THREADS, 0, s>>>(metric, X, C, labels, nblk, n_pad, k_pad, bs, n, k, active,
+                                                         sums, counts, n_empty, (uint8_t*)scratch,
+                                                         pow2_at_least(k_pad), err);
+  return check_launch("reseed");
+}
+
+extern "C" int skcq_finalize(int metric, float* sums, int32_t* counts, const int32_t* n_empty, int nblk, int k_pad,
+                             int bs, const int32_t* k, int32_t* active, int32_t* converged, int32_t* iters_run,
+                             float* moved_hist, int32_t* nempty_hist, int iter, float* C, void* stream) {
+  SKCQ_REQUIRE(sums && counts && n_empty && k && active && converged && iters_run && moved_hist && nempty_hist && C,
+               SKCQ_ERR_INVALID, "finalize: null pointer");
+  int grid = nblk < 1024 ? nblk : 1024;
+  finalize_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(metric, sums, counts, n_empty, nblk, k_pad, bs, k, active,
+                                                          converged, iters_run, moved_hist, nempty_hist, iter, C);
+  return check_launch("finalize");
+}

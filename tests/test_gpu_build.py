@@ -1,0 +1,227 @@
+"""GPU parity of the codebook-build path against the oracle and the reference's
+golden vectors. Every test here runs the CUDA kernels through the C ABI."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from _helpers import PermReplay, bf16_from_bits, load_golden, rel_err, sobol_np, sub
+from oracle import codecs as oc
+from oracle import kmeans as ok
+
+pytestmark = pytest.mark.gpu
+
+TIE = 1e-6  # relative top-2 gap below which labels may legitimately differ
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from skcq_b200 import _lib
+
+    _lib.load()
+
+
+def _problem(metric: int, nblk: int, n: int, bs: int, K: int, seed: int):
+    """Random problem set through the product's own gather/pack path."""
+    from skcq_b200 import _engine
+
+    g = torch.Generator().manual_seed(seed)
+    w = torch.randn(n, nblk * bs, generator=g) * 0.05
+    if metric == _engine.L2:
+        w = w * torch.rand(n, 1, generator=g)  # varied norms
+    wd = w.cuda()
+    pts = _engine.gather_block_points(wd, bs, nblk, False, 0.0, False, metric)
+    C = torch.randn(nblk, K, bs, generator=g) * 0.05
+    if metric == _engine.COSINE:
+        C = torch.nn.functional.normalize(C, dim=-1)
+    return w, pts, C
+
+
+def _labels(pts, C, exact: bool):
+    from skcq_b200 import _engine
+    from skcq_b200._lib import call, ptr, stream
+
+    nblk, K, bs = C.shape
+    k_pad = _engine.round_up(K, _engine.CENT_TILE)
+    Cd = torch.zeros(nblk, k_pad, bs, device="cuda")
+    Cd[:, :K] = C.cuda()
+    run = _engine.KmeansRun(C=Cd, k_pad=k_pad, k_host=[K] * nblk, labels=None, iters_run=[], converged=[],
+                            moved=None, n_empty=None, cnorm=torch.empty(nblk, k_pad, device="cuda"))
+    lab = _engine.assign(pts, run)
+    if exact:
+        k_dev = torch.full((nblk,), K, dtype=torch.int32, device="cuda")
+        call("skcq_assign_exact", pts.metric, ptr(pts.X), ptr(Cd), ptr(run.cnorm), nblk, pts.n_pad, k_pad, bs,
+             ptr(pts.n), ptr(k_dev), None, ptr(lab), stream())
+    torch.cuda.synchronize()
+    return lab[:, : pts.n_host[0]].cpu().numpy()
+
+
+@pytest.mark.parametrize("metric", [0, 1])
+@pytest.mark.parametrize("bs,K,n,nblk", [(4, 300, 1000, 3), (8, 256, 768, 5), (16, 4096, 2048, 2),
+                                          (6, 1000, 777, 2), (12, 129, 513, 2), (8, 4096, 4096, 2)])
+def test_assign_matches_oracle(metric, bs, K, n, nblk):
+    w, pts, C = _problem(metric, nblk, n, bs, K, seed=bs * 1000 + K + metric)
+    lab_tc = _labels(pts, C, exact=False)
+    lab_ex = _labels(pts, C, exact=True)
+    for b in range(nblk):
+        x = w[:, b * bs : (b + 1) * bs].numpy()
+        c = C[b].numpy()
+        if metric == 0:
+            s = ok.scores_cosine(ok.normalize_rows(x), c.T)
+        else:
+            s = ok.scores_l2(x, c.T)
+        maximise = metric == 0
+        ref = s.argmax(1) if maximise else s.argmin(1)
+        sm = s if maximise else -s
+        part = np.partition(sm, -2, axis=1)[:, -2:]
+        rel = (part[:, 1] - part[:, 0]) / (np.abs(part[:, 1]) + np.abs(part[:, 0]) + 1e-30)
+        m = rel > 1e-5
+        assert (lab_tc[b][m] == ref[m]).all(), f"block {b}: {(lab_tc[b][m] != ref[m]).sum()} tensor-core mismatches"
+        assert (lab_ex[b][m] == ref[m]).all()
+        assert (lab_tc[b] == ref).mean() > 0.999
+
+
+def _kmeans_case(name):
+    g = sub(load_golden("kmeans"), name + "__")
+    n, d, k, iters, is_cos = (int(v) for v in g["meta"])
+    return g, n, d, k, iters, is_cos
+
+
+@pytest.mark.parametrize("name", ["cos_a", "cos_empty", "l2_a", "l2_empty"])
+def test_kmeans_experiment_matches_reference(name, monkeypatch):
+    from skcq_b200.codebook import KmeansConfig, KmeansExperiment
+    from skcq_b200.codebook.events import KmeansDoneEvent, KmeansIterEvent
+
+    g, n, d, k, iters, is_cos = _kmeans_case(name)
+    monkeypatch.setattr(torch, "randperm", PermReplay.from_case(g).torch_patch())
+    data = torch.from_numpy(g["data"]).cuda()
+    exp = KmeansExperiment(KmeansConfig(metric="cosine" if is_cos else "euclidean", k=k, max_iters=iters,
+                                        device=torch.device("cuda"), name=name, chunk_size=64,
+                                        raw_data=data if is_cos else None))
+    its, done = [], []
+    exp.on(KmeansIterEvent, its.append)
+    exp.on(KmeansDoneEvent, done.append)
+    cent, labels = exp.fit(data)
+    # oracle on the same inputs decides whether the trajectory is tie-free
+    if is_cos:
+        _, _, log = ok.fit_cosine(g["data"], g["data"], k, iters, sobol_np(min(k, n), d))
+    else:
+        _, _, log = ok.fit_euclidean(g["data"], k, iters, PermReplay.from_case(g)(n))
+    ev = g["ev_int"]
+    if log.min_margin <= 1e-5:  # trajectory passes a near-tie: only quality must agree
+        assert abs(done[0].iters_run - ev[ev[:, 0] == 2][0][1]) <= 3
+        return
+    assert [e.n_empty for e in its] == list(ev[ev[:, 0] == 1][:, 2])
+    assert done[0].iters_run == ev[ev[:, 0] == 2][0][1]
+    assert rel_err(cent.cpu().numpy(), g["centroids"]) < 1e-5
+    assert (labels.cpu().numpy() == g["labels"]).all()
+
+
+CODEC_CASES = ["base", "single", "ssvq", "noncomm", "asym", "shared", "int8cb", "skipz", "ressign", "rem13"]
+
+
+def _product_aqlm(name):
+    from skcq_b200 import codebook as cb
+
+    kw = {
+        "base": {}, "single": {"k_list": (16,)}, "ssvq": {"sign_split": True},
+        "noncomm": {"block_size": 10, "rbs": 12}, "asym": {"k_list": (16, 8)},
+        "shared": {"shared": True}, "int8cb": {"k_list": (16, 8), "codebook_bits": 8},
+        "skipz": {"norm_threshold": 1e-5, "skip_zeros": True},
+        "ressign": {"res_sign_split": True, "k_list": (16, 16, 8)}, "rem13": {"k_list": (16,)},
+    }[name]
+    bs = kw.get("block_size", 4)
+    k_list = kw.get("k_list", (16, 16))
+    thr = kw.get("norm_threshold", 1e-9)
+    prim = cb.SphericalCodebook(cb.SphericalCodebookConfig(block_size=bs, K=k_list[0], shared=kw.get("shared", False),
+                                                           max_iters=10, norm_threshold=thr,
+                                                           skip_zeros=kw.get("skip_zeros", False)))
+    if kw.get("sign_split"):
+        prim = cb.SSVQCodebook(prim)
+    res = []
+    for kc in k_list[1:]:
+        r = cb.EuclideanCodebook(cb.EuclideanCodebookConfig(block_size=kw.get("rbs") or bs, K=kc,
+                                                            shared=kw.get("shared", False), max_iters=10,
+                                                            norm_threshold=thr, skip_zeros=False))
+        if kw.get("res_sign_split"):
+            r = cb.SSVQCodebook(r)
+        res.append(r)
+    return cb.AQLMCodebook(prim, res, cb.AQLMCodebookConfig(norm_threshold=thr,
+                                                            codebook_bits=kw.get("codebook_bits", 16)))
+
+
+@pytest.mark.parametrize("name", CODEC_CASES)
+def test_aqlm_fit_matches_reference(name, monkeypatch):
+    import test_oracle_golden as T
+
+    g = sub(load_golden("codecs"), name + "__")
+    prim, res, bits, thr = T._spec(name, int(g["meta"][2]))
+    primary, residuals, ocwr = oc.aqlm_fit(prim, res, g["w"], sobol_np, PermReplay.from_case(g),
+                                           codebook_bits=bits, norm_threshold=thr)
+    logs = [lg for c in [primary, *residuals] for lg in T.codec_logs(c)]
+    monkeypatch.setattr(torch, "randperm", PermReplay.from_case(g).torch_patch())
+    aqlm = _product_aqlm(name)
+    w = torch.from_numpy(g["w"]).cuda()
+    cwr = aqlm.fit(w)
+    recon = aqlm.reconstruct(cwr).cpu().numpy()
+    wn = g["w"].astype(np.float64)
+    e_ref = np.linalg.norm(wn - g["recon"]) / np.linalg.norm(wn)
+    e_gpu = np.linalg.norm(wn - recon) / np.linalg.norm(wn)
+    if not all(lg.min_margin > TIE for lg in logs):
+        assert abs(e_gpu - e_ref) <= 0.15 * e_ref
+        return
+    assert abs(e_gpu - e_ref) <= 1e-3 * e_ref + 1e-7
+    assert rel_err(recon, g["recon"]) < 2e-3
+
+
+def test_config1_matches_reference(monkeypatch):
+    """W 768x2048 bf16; SSVQ spherical bs=8 K=256 + euclidean bs=4 K=256, 20 iterations."""
+    from skcq_b200 import codebook as cb
+    from skcq_b200.codebook.events import KmeansDoneEvent
+
+    g = load_golden("config1")
+    monkeypatch.setattr(torch, "randperm", PermReplay.from_case(g).torch_patch())
+    w = torch.from_numpy(bf16_from_bits(g["w_bf16"]).reshape(768, 2048)).to(torch.bfloat16).cuda()
+    primary = cb.SSVQCodebook(cb.SphericalCodebook(cb.SphericalCodebookConfig(block_size=8, K=256, max_iters=20)))
+    residual = cb.EuclideanCodebook(cb.EuclideanCodebookConfig(block_size=4, K=256, max_iters=20, skip_zeros=False))
+    aqlm = cb.AQLMCodebook(primary, [residual], cb.AQLMCodebookConfig())
+    done = []
+    aqlm.on(KmeansDoneEvent, done.append)
+    cwr = aqlm.fit(w)
+    recon = aqlm.reconstruct(cwr).cpu().numpy()
+    wf = w.float().cpu().numpy()
+    rel = float(np.linalg.norm(wf - recon) / np.linalg.norm(wf))
+    assert abs(rel - g["rel_fro_err"][0]) < 1e-3 * g["rel_fro_err"][0], (rel, g["rel_fro_err"][0])
+    assert (cwr.primary.inner.idxs.cpu().numpy() == g["c0_idxs"]).mean() > 0.99
+    assert (cwr.residuals[0].idxs.cpu().numpy() == g["c1_idxs"]).mean() > 0.95
+    assert rel_err(recon[::37], g["recon_rows"]) < 5e-3
+    ev = g["ev_int"]
+    ref_iters = ev[ev[:, 0] == 2][:, 1]
+    assert len(done) == len(ref_iters)
+    assert (np.array([d.iters_run for d in done]) == ref_iters).mean() > 0.95
+
+
+def test_reconstruct_bit_exact_vs_oracle(monkeypatch):
+    """Decode is deterministic single-rounding arithmetic: identical payloads
+    decode to identical bits (aqlm.py:137-141)."""
+    g = sub(load_golden("codecs"), "ressign__")
+    monkeypatch.setattr(torch, "randperm", PermReplay.from_case(g).torch_patch())
+    aqlm = _product_aqlm("ressign")
+    cwr = aqlm.fit(torch.from_numpy(g["w"]).cuda())
+    recon = aqlm.reconstruct(cwr).cpu().numpy()
+    # oracle decode of the product's own payload
+    p = oc.Codec("spherical", oc.SphericalCfg(4, 16), centroids=aqlm.primary.directions.float().cpu().numpy())
+    parts = [oc.spherical_reconstruct(p, {"idxs": cwr.primary.idxs.cpu().numpy(),
+                                          "scales": cwr.primary.scales.cpu().numpy(), "remainder": None})]
+    for r, rc in zip(aqlm.residuals, cwr.residuals, strict=True):
+        inner = oc.Codec("euclidean", oc.EuclideanCfg(4, r.inner.K), centroids=r.inner.centroids.float().cpu().numpy())
+        x = oc.euclidean_reconstruct(inner, {"idxs": rc.inner.idxs.cpu().numpy(), "remainder": None})
+        parts.append(x * rc.signs.cpu().numpy().astype(np.float32))
+    ref = parts[0]
+    for x in parts[1:]:
+        ref = ref + x
+    assert np.array_equal(recon, ref)
