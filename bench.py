@@ -1,0 +1,408 @@
+#!/usr/bin/env python
+"""Benchmark of the SKCQ codebook build on B200.
+
+Workload (default ``layer``): one synthetic MoE layer's experts -- 128 experts x
+{gate, up: 768 x 2048; down: 2048 x 768} bf16 with Student-t(nu=5) entries
+scaled to std 0.02 -- each projection fitted with a spherical primary
+(bs=8, K=4096) and two euclidean residuals (bs=16, K=4096; bs=4, K=65536),
+25 Lloyd iterations, int8 centroids. One step = the full AQLM build of all
+three projections. Metric: k-means Mblock-iters/s = sum over codebooks of
+(non-zero blocks x iterations run) / s / 1e6, iterations taken from the
+KmeansDoneEvents.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Under torchrun (N > 1) every rank builds its own layer (different seed): the
+layer-level job farm, weak scaling, no data-path collective.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+WORKLOADS = {
+    # experts, hidden, intermediate, primary (bs, K), residuals [(bs, K)], iters, centroid bits
+    "layer": dict(experts=128, hidden=2048, inter=768, prim=(8, 4096), res=[(16, 4096), (4, 65536)], iters=25,
+                  bits=8),
+    "small": dict(experts=8, hidden=512, inter=192, prim=(8, 256), res=[(16, 256), (4, 2048)], iters=5, bits=8),
+}
+METRIC = "kmeans_mblock_iters_per_s"
+UNIT = "Mblock-iters/s"
+
+
+def projections(wl: dict) -> list[tuple[str, int, int]]:
+    """(name, rows, in_dim) of the gate/up/down expert-major matrices (quantize.py:59-61)."""
+    e, h, i = wl["experts"], wl["hidden"], wl["inter"]
+    return [("gate", e * i, h), ("up", e * i, h), ("down", e * h, i)]
+
+
+def make_weights(wl: dict, seed: int, device: str) -> dict[str, torch.Tensor]:
+    """Student-t(5) entries scaled to std 0.02 (t * 0.02 / sqrt(5/3)), bf16."""
+    gen = torch.Generator(device=device).manual_seed(seed)
+    out = {}
+    for name, rows, cols in projections(wl):
+        z = torch.randn(rows, cols, generator=gen, device=device)
+        chi2 = torch.randn(5, rows, cols, generator=gen, device=device).square_().sum(0)
+        t = z / torch.sqrt(chi2 / 5.0)
+        out[name] = (t * (0.02 / math.sqrt(5.0 / 3.0))).to(torch.bfloat16)
+        del z, chi2, t
+    return out
+
+
+def make_aqlm(wl: dict):
+    from skcq_b200 import codebook as cb
+
+    bs0, k0 = wl["prim"]
+    primary = cb.SphericalCodebook(cb.SphericalCodebookConfig(block_size=bs0, K=k0, max_iters=wl["iters"]))
+    residuals = [cb.EuclideanCodebook(cb.EuclideanCodebookConfig(block_size=bs, K=k, max_iters=wl["iters"],
+                                                                 skip_zeros=False)) for bs, k in wl["res"]]
+    return cb.AQLMCodebook(primary, residuals, cb.AQLMCodebookConfig(codebook_bits=wl["bits"]))
+
+
+class BlockIterCounter:
+    """sum(n_points * iters_run) over every k-means run seen."""
+
+    def __init__(self, aqlm) -> None:
+        from skcq_b200.codebook.events import KmeansDoneEvent, KmeansStartEvent
+
+        self.total = 0
+        self._n = 0
+        aqlm.on(KmeansStartEvent, self._start)
+        aqlm.on(KmeansDoneEvent, self._done)
+
+    def _start(self, e) -> None:
+        self._n = e.n_points
+
+    def _done(self, e) -> None:
+        self.total += self._n * e.iters_run
+
+
+def build_step(wl: dict, weights: dict[str, torch.Tensor], rel_err: bool = False):
+    """One AQLM build of every projection. Returns (block_iters, rel_errs)."""
+    total = 0
+    errs = []
+    for name, _, _ in projections(wl):
+        aqlm = make_aqlm(wl)
+        cnt = BlockIterCounter(aqlm)
+        w = weights[name]
+        cwr = aqlm.fit(w)
+        total += cnt.total
+        if rel_err:
+            wf = w.float()
+            errs.append(torch.linalg.vector_norm(wf - aqlm.reconstruct(cwr)) / torch.linalg.vector_norm(wf))
+        del cwr, aqlm
+    return total, errs
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int) -> None:
+        self.index = index
+        self.proc = None
+        self.path = Path(tempfile.mkstemp(prefix="skcq_clocks_", suffix=".csv")[1])
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        rows = []
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        self.path.unlink(missing_ok=True)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        busy = [v for v in sm if mx and v > 0.3 * max(mx)] or sm
+        return {"sm_mhz": statistics.median(busy) if busy else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def measured_peaks() -> tuple[dict, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text()), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# CPU leg: the oracle port on a bounded sample of the same workload
+# ---------------------------------------------------------------------------
+
+
+def cpu_rate(wl: dict, seconds_hint: float = 15.0) -> dict:
+    """Time one Lloyd iteration (assign + update) and one assignment of each
+    codebook kind on sampled points of one full-size block with the numpy
+    oracle, then scale to the whole layer's block-iterations."""
+    from oracle import kmeans as ok
+
+    rng = np.random.default_rng(0)
+    kinds = [("cosine", *wl["prim"])] + [("euclidean", bs, k) for bs, k in wl["res"]]
+    projs = projections(wl)
+    t_total = 0.0
+    block_iters = 0.0
+    samples = []
+    for metric, bs, K in kinds:
+        n_s = max(256, min(16384, int(2**31 // (K * 4 * 8))))
+        x = (rng.standard_t(5, size=(n_s, bs)) * 0.02 / math.sqrt(5 / 3)).astype(np.float32)
+        c = x[rng.permutation(n_s)[: min(K, n_s)]] if K > n_s else x[rng.permutation(n_s)[:K]]
+        if K > n_s:
+            c = np.concatenate([c, (rng.standard_normal((K - c.shape[0], bs)) * 0.01).astype(np.float32)])
+        ts_a, ts_u = [], []
+        for _ in range(3):
+            t0 = time.perf_counter()
+            if metric == "cosine":
+                u = ok.normalize_rows(x)
+                lab = ok.assign_cosine(u, ok.normalize_rows(c).T)
+            else:
+                lab = ok.assign_l2(x, c.T)
+            t1 = time.perf_counter()
+            ok._index_add(K, lab, x)
+            t2 = time.perf_counter()
+            ts_a.append(t1 - t0)
+            ts_u.append(t2 - t1)
+        ta, tu = statistics.median(ts_a), statistics.median(ts_u)
+        per_point_iter = (ta + tu) / n_s
+        per_point_final = ta / n_s
+        samples.append(f"{metric} bs={bs} K={K}: {n_s} pts, assign {ta * 1e3:.1f} ms, update {tu * 1e3:.1f} ms")
+        for _, rows, in_dim in projs:
+            pts = rows * (in_dim // bs)
+            t_total += pts * (wl["iters"] * per_point_iter + per_point_final)
+            block_iters += pts * wl["iters"]
+    try:
+        from threadpoolctl import threadpool_info
+
+        cores = max((i.get("num_threads", 1) for i in threadpool_info() if i.get("internal_api") == "openblas"),
+                    default=os.cpu_count())
+    except Exception:  # noqa: BLE001
+        cores = os.cpu_count()
+    return {
+        "value": block_iters / t_total / 1e6,
+        "unit": UNIT,
+        "cores": int(cores),
+        "kind": "port",
+        "sample": "numpy oracle, one Lloyd iteration + one assignment per codebook kind on sampled points of a "
+                  "full-size block, scaled to the layer; " + "; ".join(samples),
+        "est_layer_s": t_total,
+    }
+
+
+# ---------------------------------------------------------------------------
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def barrier(world: int) -> None:
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def run_reference(args, wl, world, rank) -> None:
+    if rank != 0:
+        return
+    t0 = time.perf_counter()
+    vals = []
+    for _ in range(args.warmup + args.steps):
+        vals.append(cpu_rate(wl))
+    v = vals[-args.steps:]
+    value = statistics.median(x["value"] for x in v)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.workload, **{k: (list(map(list, v)) if k == "res" else v) for k, v in wl.items()}},
+        "cpu_baseline": {k: v[-1][k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "wall_s": time.perf_counter() - t0,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="layer", choices=list(WORKLOADS))
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg")
+    args = ap.parse_args()
+    wl = WORKLOADS[args.workload]
+    world, rank, local = dist_setup(args)
+    if args.impl == "reference":
+        run_reference(args, wl, world, rank)
+        return
+
+    from skcq_b200 import _engine, _lib
+
+    _lib.load()
+    dev = f"cuda:{local}" if world > 1 else "cuda:0"
+    weights = make_weights(wl, seed=1234 + rank, device=dev)
+    torch.cuda.synchronize()
+    for _ in range(args.warmup):
+        build_step(wl, weights)
+    torch.cuda.synchronize()
+    barrier(world)
+
+    # ---- device-resident timed region -------------------------------------
+    _engine.TIMER.reset()
+    _engine.TIMER.enabled = True
+    _lib.LAUNCHES.reset()
+    _lib.LAUNCHES.enabled = True
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    block_iters = 0
+    with ClockSampler(local) as clocks:
+        torch.cuda.synchronize()
+        barrier(world)
+        start.record()
+        for _ in range(args.steps):
+            n, _ = build_step(wl, weights)
+            block_iters += n
+        end.record()
+        torch.cuda.synchronize()
+    barrier(world)
+    _lib.LAUNCHES.enabled = False
+    _engine.TIMER.enabled = False
+    ms = max_over_ranks(start.elapsed_time(end), world)
+    total_block_iters = sum_over_ranks(block_iters, world)
+    value = total_block_iters / (ms / 1e3) / 1e6
+    launches = _lib.LAUNCHES.kernels
+    ksum = _engine.TIMER.summary()
+
+    # ---- end to end through the public API with host buffers --------------
+    e2e = None
+    if not args.no_e2e:
+        host = {k: v.cpu().pin_memory() for k, v in weights.items()}
+        del weights
+        torch.cuda.empty_cache()
+        h2d = sum(t.numel() * t.element_size() for t in host.values())
+        torch.cuda.synchronize()
+        barrier(world)
+        t0 = time.perf_counter()
+        bi = 0
+        d2h = 0
+        for _ in range(args.steps):
+            dev_w = {k: v.to(dev, non_blocking=True) for k, v in host.items()}
+            n, errs = build_step(wl, dev_w, rel_err=True)
+            vals = torch.stack(errs).cpu()
+            d2h += vals.numel() * vals.element_size()
+            bi += n
+            del dev_w
+        torch.cuda.synchronize()
+        e2e_s = max_over_ranks(time.perf_counter() - t0, world)
+        e2e = {"value": sum_over_ranks(bi, world) / e2e_s / 1e6, "unit": UNIT, "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h // max(args.steps, 1), "rel_fro_err": [float(x) for x in vals]}
+
+    peaks, peak_kind = measured_peaks()
+    a = ksum.get("assign", {"ms": 0.0, "work": 0.0, "launches": 0, "padded": 0.0})
+    achieved = a["work"] / (a["ms"] / 1e3) / 1e12 if a["ms"] > 0 else 0.0
+    issued = a["padded"] / (a["ms"] / 1e3) / 1e12 if a["ms"] > 0 else 0.0
+    roofline = {
+        "bound": "tensor", "kernel": "assign_tc_kernel", "achieved": achieved,
+        "peak": peaks["bf16_tflops"], "peak_kind": f"{peak_kind} bf16 dense (burst)", "unit": "TFLOP/s",
+        "frac": achieved / peaks["bf16_tflops"], "traffic": None,
+        "issued_tf32_tflops": issued,
+        "assign_share_of_step": a["ms"] / ms if ms else None,
+        "kernel_ms": {k: round(v["ms"], 2) for k, v in ksum.items()},
+        "kernel_launches": {k: int(v["launches"]) for k, v in ksum.items()},
+    }
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": args.workload, "experts": wl["experts"], "hidden": wl["hidden"],
+                       "intermediate": wl["inter"], "primary": list(wl["prim"]),
+                       "residuals": [list(r) for r in wl["res"]], "iters": wl["iters"],
+                       "codebook_bits": wl["bits"], "step": "AQLM build of gate, up and down",
+                       "l2": "inputs larger than L2 (bf16 weights 1.2 GB per layer; split operands > 3 GB)",
+                       "parallelism": f"layer farm x{world}"},
+            "block_iters_per_step": total_block_iters / args.steps,
+            "roofline": roofline, "clocks": clocks.summary(), "gpu_launches": launches, "e2e": e2e,
+        }
+        if not args.no_cpu and world == 1:
+            line["cpu_baseline"] = {k: v for k, v in cpu_rate(wl).items() if k != "est_layer_s"}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -25,6 +25,43 @@ ROWS_PER_UNIT = 256  # SKCQ_ROWS_PER_UNIT
 CENT_TILE = 128  # SKCQ_CENT_TILE
 
 
+class KernelTimer:
+    """Optional CUDA-event timing of engine kernels on the launching stream
+    (used by the benchmark for the roofline; off by default)."""
+
+    def __init__(self) -> None:
+        self.enabled = False
+        self.records: list[tuple[str, torch.cuda.Event, torch.cuda.Event, float, float]] = []
+
+    def reset(self) -> None:
+        self.records = []
+
+    def run(self, name: str, fn, work: float = 0.0, padded: float = 0.0) -> None:
+        if not self.enabled:
+            fn()
+            return
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        self.records.append((name, s, e, work, padded))
+
+    def summary(self) -> dict[str, dict[str, float]]:
+        torch.cuda.synchronize()
+        out: dict[str, dict[str, float]] = {}
+        for name, s, e, work, padded in self.records:
+            d = out.setdefault(name, {"launches": 0, "ms": 0.0, "work": 0.0, "padded": 0.0})
+            d["launches"] += 1
+            d["ms"] += s.elapsed_time(e)
+            d["work"] += work
+            d["padded"] += padded
+        return out
+
+
+TIMER = KernelTimer()
+
+
 def round_up(x: int, m: int) -> int:
     return (max(x, 1) + m - 1) // m * m
 
@@ -68,6 +105,20 @@ class PointSet:
 
 def packed_width(metric: int, bs: int) -> int:
     return int(_lib.load().skcq_packed_width(metric, bs))
+
+
+TC_MAX_KP = 64  # widest split operand the tensor-core kernel stages (bs <= 20)
+
+
+def assign_call(pts: PointSet, B, C, cnorm, k_pad: int, k_dev, active, labels) -> None:
+    """Tensor-core assignment (+ exact re-score); blocks wider than the
+    tensor-core path stages go to the exact CUDA-core kernel."""
+    if pts.kp <= TC_MAX_KP:
+        call("skcq_assign", pts.metric, ptr(pts.packed()), ptr(B), ptr(pts.X), ptr(C), ptr(cnorm), pts.nblk,
+             pts.n_pad, k_pad, pts.bs, ptr(pts.n), ptr(k_dev), ptr(active), ptr(labels), stream())
+    else:
+        call("skcq_assign_exact", pts.metric, ptr(pts.X), ptr(C), ptr(cnorm), pts.nblk, pts.n_pad, k_pad, pts.bs,
+             ptr(pts.n), ptr(k_dev), ptr(active), ptr(labels), stream())
 
 
 def gather_block_points(
@@ -167,7 +218,6 @@ def lloyd(
             if kb > 0:
                 perm[b, :kb] = init_perms[b][:kb].to(dev)
         call("skcq_init_from_points", ptr(pts.X), n_pad, bs, nblk, ptr(perm), k_pad, ptr(k_dev), k_pad, ptr(C), s)
-    A = pts.packed()
     B = torch.empty(nblk, k_pad * kp, dtype=torch.float32, device=dev)
     cnorm = torch.empty(nblk, k_pad, dtype=torch.float32, device=dev)
     sums = torch.zeros(nblk, k_pad, bs, dtype=torch.float32, device=dev)
@@ -180,16 +230,25 @@ def lloyd(
     moved = torch.zeros(max(max_iters, 1), nblk, dtype=torch.float32, device=dev)
     nempty_hist = torch.zeros(max(max_iters, 1), nblk, dtype=torch.int32, device=dev)
     flag = torch.empty(1, dtype=torch.int32, pin_memory=True)
+    T = TIMER
+    nk = np.array(pts.n_host, dtype=np.float64) * np.array(k_host, dtype=np.float64)
     for it in range(max_iters):
-        call("skcq_pack_centroids", metric, ptr(C), nblk, k_pad, bs, ptr(k_dev), ptr(active), ptr(B), ptr(cnorm), s)
-        call("skcq_assign", metric, ptr(A), ptr(B), ptr(pts.X), ptr(C), ptr(cnorm), nblk, n_pad, k_pad, bs,
-             ptr(pts.n), ptr(k_dev), ptr(active), ptr(labels), s)
-        call("skcq_update", ptr(pts.R), ptr(labels), nblk, n_pad, k_pad, bs, ptr(pts.n), ptr(k_dev), ptr(active),
-             ptr(sums), ptr(counts), s)
-        call("skcq_reseed", metric, ptr(pts.X), ptr(C), ptr(labels), nblk, n_pad, k_pad, bs, ptr(pts.n), ptr(k_dev),
-             ptr(active), ptr(sums), ptr(counts), ptr(n_empty), ptr(scratch), s)
-        call("skcq_finalize", metric, ptr(sums), ptr(counts), ptr(n_empty), nblk, k_pad, bs, ptr(k_dev),
-             ptr(active), ptr(converged), ptr(iters_run), ptr(moved), ptr(nempty_hist), it, ptr(C), s)
+        work = padded = 0.0
+        if T.enabled:  # algorithmic work of this iteration: 2*n*k*bs flops over active problems
+            act = active.cpu().numpy().astype(bool)
+            work = 2.0 * bs * float(nk[act].sum())
+            padded = work * kp / bs
+        T.run("pack_centroids", lambda: call("skcq_pack_centroids", metric, ptr(C), nblk, k_pad, bs, ptr(k_dev),
+                                             ptr(active), ptr(B), ptr(cnorm), s))
+        T.run("assign", lambda: assign_call(pts, B, C, cnorm, k_pad, k_dev, active, labels), work, padded)
+        T.run("update", lambda: call("skcq_update", ptr(pts.R), ptr(labels), nblk, n_pad, k_pad, bs, ptr(pts.n),
+                                     ptr(k_dev), ptr(active), ptr(sums), ptr(counts), s))
+        T.run("reseed", lambda: call("skcq_reseed", metric, ptr(pts.X), ptr(C), ptr(labels), nblk, n_pad, k_pad, bs,
+                                     ptr(pts.n), ptr(k_dev), ptr(active), ptr(sums), ptr(counts), ptr(n_empty),
+                                     ptr(scratch), s))
+        T.run("finalize", lambda: call("skcq_finalize", metric, ptr(sums), ptr(counts), ptr(n_empty), nblk, k_pad,
+                                       bs, ptr(k_dev), ptr(active), ptr(converged), ptr(iters_run), ptr(moved),
+                                       ptr(nempty_hist), it, ptr(C), s))
         flag.copy_(active.max().reshape(1), non_blocking=True)
         torch.cuda.current_stream().synchronize()
         if int(flag.item()) == 0:
@@ -197,8 +256,8 @@ def lloyd(
     _lib.poll_device_error()
     # final assignment with the final centroids (kmeans.py:190 / 246)
     call("skcq_pack_centroids", metric, ptr(C), nblk, k_pad, bs, ptr(k_dev), None, ptr(B), ptr(cnorm), s)
-    call("skcq_assign", metric, ptr(A), ptr(B), ptr(pts.X), ptr(C), ptr(cnorm), nblk, n_pad, k_pad, bs,
-         ptr(pts.n), ptr(k_dev), None, ptr(labels), s)
+    work = 2.0 * bs * float(nk.sum())
+    T.run("assign", lambda: assign_call(pts, B, C, cnorm, k_pad, k_dev, None, labels), work, work * kp / bs)
     return KmeansRun(
         C=C, k_pad=k_pad, k_host=k_host, labels=labels,
         iters_run=[int(v) for v in iters_run.cpu().tolist()],
@@ -216,8 +275,7 @@ def assign(pts: PointSet, run: KmeansRun) -> torch.Tensor:
     s = stream()
     call("skcq_pack_centroids", pts.metric, ptr(run.C), pts.nblk, run.k_pad, pts.bs, ptr(k_dev), None, ptr(B),
          ptr(run.cnorm), s)
-    call("skcq_assign", pts.metric, ptr(pts.packed()), ptr(B), ptr(pts.X), ptr(run.C), ptr(run.cnorm), pts.nblk,
-         pts.n_pad, run.k_pad, pts.bs, ptr(pts.n), ptr(k_dev), None, ptr(labels), s)
+    assign_call(pts, B, run.C, run.cnorm, run.k_pad, k_dev, None, labels)
     return labels
 
 

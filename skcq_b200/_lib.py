@@ -97,11 +97,41 @@ def last_error() -> str:
     return buf.value.decode(errors="replace")
 
 
+# Kernels each entry point launches (for launch accounting by the benchmark).
+_KERNELS_PER_CALL = {
+    "skcq_compact_points": 1, "skcq_gather_points": 1, "skcq_pack_points": 1, "skcq_init_from_points": 1,
+    "skcq_pack_centroids": 1, "skcq_assign": 2, "skcq_assign_exact": 1, "skcq_update": 1, "skcq_reseed": 1,
+    "skcq_finalize": 1, "skcq_flip_check": 1, "skcq_apply_flip": 1, "skcq_scatter_labels": 1,
+    "skcq_row_zero_mask": 1, "skcq_spherical_scales": 1, "skcq_centroids_to_bf16": 1, "skcq_copy_remainder": 1,
+    "skcq_ssvq_fold": 1, "skcq_quantize_centroids": 1, "skcq_quantize_scales": 3, "skcq_reconstruct": 1,
+    "skcq_refit_scales": 1,
+}
+
+
+class LaunchCounter:
+    """Counts kernel launches made through ``call`` while enabled."""
+
+    def __init__(self) -> None:
+        self.enabled = False
+        self.kernels = 0
+        self.calls: dict[str, int] = {}
+
+    def reset(self) -> None:
+        self.kernels = 0
+        self.calls = {}
+
+
+LAUNCHES = LaunchCounter()
+
+
 def call(name: str, *args) -> int:
     """Call ``name`` and raise ``RuntimeError`` on a non-zero status."""
     rc = getattr(load(), name)(*args)
     if rc != 0:
         raise RuntimeError(f"{name} failed ({rc}): {last_error()}")
+    if LAUNCHES.enabled:
+        LAUNCHES.kernels += _KERNELS_PER_CALL.get(name, 0)
+        LAUNCHES.calls[name] = LAUNCHES.calls.get(name, 0) + 1
     return rc
 
 

@@ -139,27 +139,34 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
       : "memory");
 }
 
+// try_wait with a suspend-time hint: the thread sleeps in hardware until the
+// phase completes or ~1 ms passes, instead of spinning on issue slots.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
       : "memory");
   return ok != 0;
 }
 
-// Bounded wait: gives up after `limit` polls, sets *err and returns false.
-// Every spin in these kernels goes through this, so a lost arrival turns into
-// an error status instead of a hung GPU.
+// Bounded wait: gives up after ~4e9 SM clocks (about two seconds), sets *err
+// and returns false; also returns false as soon as another thread has recorded
+// an error. Every spin in these kernels goes through this, so a lost arrival
+// turns into an error status instead of a hung GPU. try_wait itself suspends
+// the thread in hardware until the phase flips or a short timeout passes.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
-  const uint32_t limit = 1u << 26;
-  for (uint32_t i = 0; i < limit; ++i) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (i > 64) __nanosleep(32);
-    if ((i & 1023) == 0 && *(volatile int*)err) return false;
+    if ((i & 3) == 0) {
+      if (*(volatile int*)err) return false;
+      if (clock64() - t0 > 4000000000ll) break;
+    }
   }
   atomicCAS(err, 0, code);
   return false;
