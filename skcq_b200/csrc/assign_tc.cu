@@ -3,13 +3,13 @@
 //
 // Kernel 1 -- one persistent CTA per SM, warp-specialised:
 //   warp 0      producer: 1-D bulk copies (TMA engine) of the point tile
-//               (256 points, resident for the whole centroid sweep) and a
-//               4-stage ring of centroid tiles (128 centroids each);
+//               (256 points, double buffered across work units) and a ring
+//               of centroid tiles (128 centroids each, up to 16 deep);
 //   warp 1      issues tcgen05.mma kind::tf32 (M=128, N=128, K=8) into one of
 //               two tensor-memory accumulator sets (double buffered);
-//   warps 2-9   epilogue: tcgen05.ld the 128x128 fp32 scores of one row tile
-//               and lane quarter, release the accumulator, then keep a
-//               running (best value, best group of 32 centroids) per point
+//   warps 2-17  epilogue: tcgen05.ld 64 columns of the fp32 scores of one
+//               (row tile, lane quarter), release the accumulator, then keep
+//               a running (best value, best group of 32 centroids) per point
 //               with 3-input max; the distance matrix never leaves the SM.
 // Operands are split-tf32 (hi/lo) so A.B reproduces the fp32 dot product to
 // ~2^-21 relative.
@@ -26,9 +26,9 @@ constexpr int TC_BM = 128;                       // points per MMA (TMEM lanes)
 constexpr int TC_RT = 2;                         // row tiles per work unit
 constexpr int TC_ROWS = TC_BM * TC_RT;           // points per work unit
 constexpr int TC_BN = 128;                       // centroids per tile
-constexpr int TC_STAGES = 4;                     // centroid tile ring depth (3 for the widest operands)
+constexpr int TC_STAGES = 16;                    // max centroid tile ring depth (as many as shared memory holds)
 constexpr int TC_ABUF = 2;                       // point tiles in flight (next unit loads during this one)
-constexpr int TC_EPI_WARPS = 4 * TC_RT;          // one warp per (row tile, lane quarter)
+constexpr int TC_EPI_WARPS = 8 * TC_RT;          // one warp per (row tile, lane quarter, column half)
 constexpr int TC_THREADS = (2 + TC_EPI_WARPS) * 32;
 constexpr int TC_TMEM_COLS = 2 * TC_RT * TC_BN;  // 512: two accumulator sets
 constexpr size_t TC_MIN_SMEM = 116 * 1024;       // keeps one CTA (and one TMEM owner) per SM
@@ -69,25 +69,39 @@ __device__ __forceinline__ bool unit_live(const TcParams& p, int64_t u, int upb,
   return *r0 < p.n[*b];
 }
 
+// Position in a ring of n barrier-guarded slots: slot index and the parity of
+// the slot's current use. Advancing never divides (the issuing threads are
+// single-thread critical paths).
+struct Ring {
+  uint32_t idx = 0, phase = 0;
+  __device__ __forceinline__ void next(uint32_t n) {
+    if (++idx == n) {
+      idx = 0;
+      phase ^= 1;
+    }
+  }
+};
+
 __device__ void tc_producer(const TcParams& p, const TcSmem& s) {
   const int upb = p.n_pad / TC_ROWS;
   const int64_t n_units = (int64_t)p.nblk * upb;
-  uint32_t a_cnt = 0, b_cnt = 0;
+  const uint32_t b_floats = (uint32_t)TC_BN * p.kp;
+  Ring ar, br;
   for (int64_t u = blockIdx.x; u < n_units; u += gridDim.x) {
     int b, r0;
     if (!unit_live(p, u, upb, &b, &r0)) continue;
     const int nbt = ceil_div(p.k[b], TC_BN);
-    const uint32_t as = a_cnt % TC_ABUF, ause = a_cnt / TC_ABUF;
-    if (!mbar_wait(s.a_empty + as, (ause & 1) ^ 1, p.err, 11)) return;
-    mbar_arrive_expect_tx(s.a_full + as, s.a_bytes);
-    bulk_g2s(s.a + (size_t)as * TC_ROWS * p.kp, p.A + ((int64_t)b * p.n_pad + r0) * p.kp, s.a_bytes, s.a_full + as);
-    ++a_cnt;
+    if (!mbar_wait(s.a_empty + ar.idx, ar.phase ^ 1, p.err, 11)) return;
+    mbar_arrive_expect_tx(s.a_full + ar.idx, s.a_bytes);
+    bulk_g2s(s.a + ar.idx * (TC_ROWS * p.kp), p.A + ((int64_t)b * p.n_pad + r0) * p.kp, s.a_bytes,
+             s.a_full + ar.idx);
+    ar.next(TC_ABUF);
     const float* bsrc = p.B + (int64_t)b * p.k_pad * p.kp;
-    for (int j = 0; j < nbt; ++j, ++b_cnt) {
-      const uint32_t st = b_cnt % p.stages, use = b_cnt / p.stages;
-      if (!mbar_wait(s.b_empty + st, (use & 1) ^ 1, p.err, 12)) return;
-      mbar_arrive_expect_tx(s.b_full + st, s.b_bytes);
-      bulk_g2s(s.b + (size_t)st * TC_BN * p.kp, bsrc + (int64_t)j * TC_BN * p.kp, s.b_bytes, s.b_full + st);
+    for (int j = 0; j < nbt; ++j, bsrc += b_floats) {
+      if (!mbar_wait(s.b_empty + br.idx, br.phase ^ 1, p.err, 12)) return;
+      mbar_arrive_expect_tx(s.b_full + br.idx, s.b_bytes);
+      bulk_g2s(s.b + br.idx * b_floats, bsrc, s.b_bytes, s.b_full + br.idx);
+      br.next(p.stages);
     }
   }
 }
@@ -104,34 +118,34 @@ __device__ void tc_mma(const TcParams& p, const TcSmem& s, uint32_t tmem_base) {
   const uint64_t a_rt = (uint64_t)(TC_BM * p.kp * 4) >> 4;
   const uint64_t a_buf = (uint64_t)s.a_bytes >> 4;
   const uint64_t b_st = (uint64_t)s.b_bytes >> 4;
-  uint32_t a_cnt = 0, b_cnt = 0, t_cnt = 0;
+  Ring ar, br, cr;
   for (int64_t u = blockIdx.x; u < n_units; u += gridDim.x) {
     int b, r0;
     if (!unit_live(p, u, upb, &b, &r0)) continue;
     const int nbt = ceil_div(p.k[b], TC_BN);
-    const uint32_t as = a_cnt % TC_ABUF, ause = a_cnt / TC_ABUF;
-    if (!mbar_wait(s.a_full + as, ause & 1, p.err, 13)) return;
+    if (!mbar_wait(s.a_full + ar.idx, ar.phase, p.err, 13)) return;
     tc_fence_after();
-    ++a_cnt;
-    const uint64_t a_unit = a0 + as * a_buf;
-    for (int j = 0; j < nbt; ++j, ++b_cnt, ++t_cnt) {
-      const uint32_t st = b_cnt % p.stages, use = b_cnt / p.stages;
-      const uint32_t acc = t_cnt & 1, ause = t_cnt >> 1;
-      if (!mbar_wait(s.b_full + st, use & 1, p.err, 14)) return;
-      if (!mbar_wait(s.acc_empty + acc, (ause & 1) ^ 1, p.err, 15)) return;
+    const uint64_t a_unit = a0 + ar.idx * a_buf;
+    uint64_t bd = b0 + br.idx * b_st;
+    for (int j = 0; j < nbt; ++j) {
+      if (!mbar_wait(s.b_full + br.idx, br.phase, p.err, 14)) return;
+      if (!mbar_wait(s.acc_empty + cr.idx, cr.phase ^ 1, p.err, 15)) return;
       tc_fence_after();
-      const uint64_t bd = b0 + st * b_st;
+      const uint32_t d0 = tmem_base + cr.idx * (TC_RT * TC_BN);
 #pragma unroll
       for (int rt = 0; rt < TC_RT; ++rt) {
-        const uint32_t d = tmem_base + (acc * TC_RT + rt) * TC_BN;
         const uint64_t ad = a_unit + rt * a_rt;
 #pragma unroll
-        for (int ks = 0; ks < KSTEPS; ++ks) mma_tf32(d, ad + 16 * ks, bd + 16 * ks, idesc, ks > 0 ? 1u : 0u);
+        for (int ks = 0; ks < KSTEPS; ++ks) mma_tf32(d0 + rt * TC_BN, ad + 16 * ks, bd + 16 * ks, idesc, ks > 0 ? 1u : 0u);
       }
-      tc_commit(s.b_empty + st);
-      tc_commit(s.acc_full + acc);
+      tc_commit(s.b_empty + br.idx);
+      tc_commit(s.acc_full + cr.idx);
+      cr.next(2);
+      br.next(p.stages);
+      bd = br.idx == 0 ? b0 : bd + b_st;
     }
-    tc_commit(s.a_empty + as);
+    tc_commit(s.a_empty + ar.idx);
+    ar.next(TC_ABUF);
   }
 }
 
@@ -153,42 +167,55 @@ __device__ __forceinline__ float group_max32(const float (&v)[32]) {
   return max3f(max3f(m0, m1, m2), m3, m3);
 }
 
-__device__ void tc_epilogue(const TcParams& p, const TcSmem& s, uint32_t tmem_base, int warp, int lane) {
+// Epilogue warp e = warp - 2 owns TMEM lane quarter warp % 4 (hardware rule),
+// row tile (e >> 2) & 1 and column half e >> 3 of every 128-column tile. The
+// two halves of a row keep separate (best, group) pairs, merged through shared
+// memory at the end of each work unit (larger value, then lower group, wins).
+__device__ void tc_epilogue(const TcParams& p, const TcSmem& s, uint32_t tmem_base, int warp, int lane,
+                            float* m_best, int* m_group) {
   const int upb = p.n_pad / TC_ROWS;
   const int64_t n_units = (int64_t)p.nblk * upb;
-  const int q = warp & 3;          // tensor-memory lane quarter this warp may access
-  const int rt = (warp - 2) >> 2;  // row tile handled by this warp
+  const int e = warp - 2;
+  const int q = warp & 3;
+  const int rt = (e >> 2) & 1;
+  const int half = e >> 3;
+  const int lrow = rt * TC_BM + q * 32 + lane;  // row within the unit
   const uint32_t lane_off = (uint32_t)(q * 32) << 16;
-  uint32_t t_cnt = 0;
+  Ring cr;
+  // After a failed wait a warp stops touching tensor memory but keeps joining
+  // the named barriers below, so its partner warps are never left waiting.
+  bool failed = false;
   for (int64_t u = blockIdx.x; u < n_units; u += gridDim.x) {
     int b, r0;
     if (!unit_live(p, u, upb, &b, &r0)) continue;
     const int kb = p.k[b], nb = p.n[b];
     const int nbt = ceil_div(kb, TC_BN);
     float best = -INFINITY;
-    int bestg = 0;
-    for (int j = 0; j < nbt; ++j, ++t_cnt) {
-      const uint32_t acc = t_cnt & 1, ause = t_cnt >> 1;
-      const bool ok = mbar_wait(s.acc_full + acc, ause & 1, p.err, 16);
-      if (!__all_sync(0xffffffffu, ok)) return;
+    int bestg = 0x7fffffff;
+    for (int j = 0; j < nbt; ++j) {
+      if (failed) continue;
+      const uint32_t acc = cr.idx;
+      const bool ok = mbar_wait(s.acc_full + acc, cr.phase, p.err, 16);
+      cr.next(2);
+      if (!__all_sync(0xffffffffu, ok)) {
+        failed = true;
+        continue;
+      }
       tc_fence_after();
-      const uint32_t taddr = tmem_base + lane_off + (acc * TC_RT + rt) * TC_BN;
-      float v0[32], v1[32], v2[32], v3[32];
+      const uint32_t taddr = tmem_base + lane_off + (acc * TC_RT + rt) * TC_BN + half * 64;
+      float v0[32], v1[32];
       tmem_ld32(taddr + 0, v0);
       tmem_ld32(taddr + 32, v1);
-      tmem_ld32(taddr + 64, v2);
-      tmem_ld32(taddr + 96, v3);
       tmem_wait_ld();
       tc_fence_before();
-      mbar_arrive(s.acc_empty + acc);
-      const int cbase = j * TC_BN;
-      if (cbase + TC_BN > kb) {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(s.acc_empty + acc);  // one arrival per warp
+      const int cbase = j * TC_BN + half * 64;
+      if (cbase + 64 > kb) {
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           if (cbase + i >= kb) v0[i] = -INFINITY;
           if (cbase + 32 + i >= kb) v1[i] = -INFINITY;
-          if (cbase + 64 + i >= kb) v2[i] = -INFINITY;
-          if (cbase + 96 + i >= kb) v3[i] = -INFINITY;
         }
       }
       const int g0 = cbase / GROUP;
@@ -197,13 +224,24 @@ __device__ void tc_epilogue(const TcParams& p, const TcSmem& s, uint32_t tmem_ba
       if (m > best) { best = m; bestg = g0; }
       m = group_max32(v1);
       if (m > best) { best = m; bestg = g0 + 1; }
-      m = group_max32(v2);
-      if (m > best) { best = m; bestg = g0 + 2; }
-      m = group_max32(v3);
-      if (m > best) { best = m; bestg = g0 + 3; }
     }
-    const int row = r0 + rt * TC_BM + q * 32 + lane;
-    if (row < nb) p.group[(int64_t)b * p.n_pad + row] = -(bestg + 1);  // negative: not yet refined
+    // merge the two column halves of each row (epilogue warps only: named barrier 1)
+    if (half == 1) {
+      m_best[lrow] = best;
+      m_group[lrow] = bestg;
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(TC_EPI_WARPS * 32) : "memory");
+    if (half == 0) {
+      const float ob = m_best[lrow];
+      const int og = m_group[lrow];
+      if (ob > best || (ob == best && og < bestg)) {
+        best = ob;
+        bestg = og;
+      }
+      const int row = r0 + lrow;
+      if (row < nb && !failed) p.group[(int64_t)b * p.n_pad + row] = -(bestg + 1);  // negative: not yet refined
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(TC_EPI_WARPS * 32) : "memory");
   }
 }
 
@@ -224,6 +262,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) assign_tc_kernel(TcParams p) {
   s.acc_full = s.b_empty + TC_STAGES;
   s.acc_empty = s.acc_full + 2;
   s.tmem_slot = reinterpret_cast<uint32_t*>(s.acc_empty + 2);
+  float* m_best = reinterpret_cast<float*>(s.tmem_slot + 4);  // [TC_ROWS] half-row merge
+  int* m_group = reinterpret_cast<int*>(m_best + TC_ROWS);      // [TC_ROWS]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -237,7 +277,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) assign_tc_kernel(TcParams p) {
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(s.acc_full + i, 1);
-      mbar_init(s.acc_empty + i, TC_EPI_WARPS * 32);
+      mbar_init(s.acc_empty + i, TC_EPI_WARPS);
     }
     fence_barrier_init();
   }
@@ -255,7 +295,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) assign_tc_kernel(TcParams p) {
   } else if (warp == 1) {
     if (lane == 0) tc_mma<KSTEPS>(p, s, tmem_base);
   } else {
-    tc_epilogue(p, s, tmem_base, warp, lane);
+    tc_epilogue(p, s, tmem_base, warp, lane, m_best, m_group);
   }
   tc_fence_before();
   __syncthreads();
@@ -418,7 +458,7 @@ extern "C" int skcq_assign(int metric, const float* A, const float* B, const flo
   const int kp = skcq_packed_width(metric, bs);
   SKCQ_REQUIRE(kp / 8 <= TC_MAX_KSTEPS, SKCQ_ERR_INVALID,
                "assign: block size %d too wide for the tensor-core path (use skcq_assign_exact)", bs);
-  const size_t bar_bytes = (2 * TC_ABUF + 2 * TC_STAGES + 4) * sizeof(uint64_t) + 16;
+  const size_t bar_bytes = (2 * TC_ABUF + 2 * TC_STAGES + 4) * sizeof(uint64_t) + 16 + 2 * TC_ROWS * 4;
   int stages = TC_STAGES;
   auto smem_for = [&](int st) {
     return (size_t)TC_ABUF * TC_ROWS * kp * 4 + (size_t)st * TC_BN * kp * 4 + bar_bytes;
