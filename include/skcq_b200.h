@@ -125,6 +125,22 @@ int skcq_reseed(int metric, const float* X, const float* C, const int32_t* label
                 int bs, const int32_t* n, const int32_t* k, const int32_t* active, float* sums,
                 const int32_t* counts, int32_t* n_empty, void* scratch, void* stream);
 
+/* Same result as skcq_reseed, for callers that cannot allocate device memory:
+ * hosts that give the whole device to their own allocator and forbid
+ * cudaMalloc, or plug-in interfaces that only hand over the step's inputs and
+ * outputs. No counterpart in the reference (which lets torch allocate).
+ * The scratch is a 16 MiB array compiled into the library, held by every GPU
+ * that loads it until the process exits; problems with k_pad above 1048576
+ * are rejected with SKCQ_ERR_INVALID. The first call on a device looks up the
+ * array's device address (make that first call before any stream capture).
+ * All calls share the array: the kernel writes every scratch word before
+ * reading it, so no state carries over, but calls that overlap on the GPU
+ * (e.g. on two streams) race and must be serialised by the caller. Allocates
+ * nothing (cudaMemsetAsync of n_empty only). */
+int skcq_reseed_noalloc(int metric, const float* X, const float* C, const int32_t* labels, int nblk, int n_pad,
+                        int k_pad, int bs, const int32_t* n, const int32_t* k, const int32_t* active, float* sums,
+                        const int32_t* counts, int32_t* n_empty, void* stream);
+
 /* New centroids, movement and convergence (kmeans.py:174-188, 231-244):
  * cosine C = normalize(sums); euclidean C = sums / counts (reseeded clusters
  * take the point). moved = ||C_new - C_old||_F; a problem whose moved < 1e-6

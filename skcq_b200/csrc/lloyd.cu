@@ -1,5 +1,7 @@
 // Lloyd update, empty-cluster reseed and finalisation for the batched k-means
 // problem sets (skcq/codebook/kmeans.py:152-188 cosine, 210-244 euclidean).
+#include <mutex>
+
 #include "common.cuh"
 
 namespace skcq {
@@ -337,4 +339,71 @@ extern "C" int skcq_finalize(int metric, float* sums, int32_t* counts, const int
   finalize_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(metric, sums, counts, n_empty, nblk, k_pad, bs, k, active,
                                                           converged, iters_run, moved_hist, nempty_hist, iter, C);
   return check_launch("finalize");
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free reseed
+//
+// skcq_reseed needs a caller-provided scratch buffer. Some callers cannot
+// obtain one: a host runtime that has already handed all device memory to its
+// own allocator and forbids further cudaMalloc, or a plug-in whose host
+// interface only passes it the input and output buffers of the step. For them
+// skcq_reseed_noalloc keeps the scratch in a fixed device array compiled into
+// this library (RESEED_STATIC_BYTES on every GPU that loads the library, held
+// until the process exits) and allocates nothing.
+// ---------------------------------------------------------------------------
+
+constexpr size_t RESEED_STATIC_BYTES = (size_t)16 << 20;  // 16 MiB per device
+static __device__ __align__(256) uint8_t g_reseed_scratch[RESEED_STATIC_BYTES];
+
+// Device address of g_reseed_scratch on the current device. The host-side
+// symbol is only a stand-in, so the address is looked up once per device (with
+// that device current) and cached.
+static int reseed_static_scratch(void** out) {
+  static std::mutex mu;
+  static void* addr[64] = {nullptr};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(SKCQ_ERR_CUDA, "reseed_noalloc: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return set_error(SKCQ_ERR_INVALID, "reseed_noalloc: device ordinal %d >= 64", dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_reseed_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return set_error(SKCQ_ERR_CUDA, "reseed_noalloc: cannot resolve the static scratch (%s)", cudaGetErrorString(e));
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return SKCQ_OK;
+}
+
+extern "C" int skcq_reseed_noalloc(int metric, const float* X, const float* C, const int32_t* labels, int nblk,
+                                   int n_pad, int k_pad, int bs, const int32_t* n, const int32_t* k,
+                                   const int32_t* active, float* sums, const int32_t* counts, int32_t* n_empty,
+                                   void* stream) {
+  SKCQ_REQUIRE(X && C && labels && n && k && sums && counts && n_empty, SKCQ_ERR_INVALID,
+               "reseed_noalloc: null pointer");
+  SKCQ_REQUIRE(bs > 0 && bs <= 64, SKCQ_ERR_INVALID, "reseed_noalloc: bad block size %d", bs);
+  SKCQ_REQUIRE(nblk > 0 && k_pad > 0, SKCQ_ERR_INVALID, "reseed_noalloc: empty problem set");
+  const size_t per_slot = (size_t)k_pad * 4 + (size_t)pow2_at_least(k_pad) * 8;
+  SKCQ_REQUIRE(per_slot <= RESEED_STATIC_BYTES, SKCQ_ERR_INVALID,
+               "reseed_noalloc: k_pad %d needs %zu scratch bytes per problem, over the %zu-byte static buffer "
+               "(at most 1048576 centroids per problem); use skcq_reseed with caller scratch",
+               k_pad, per_slot, RESEED_STATIC_BYTES);
+  void* scratch = nullptr;
+  int rc = reseed_static_scratch(&scratch);
+  if (rc != SKCQ_OK) return rc;
+  int* err = device_error_word();
+  SKCQ_REQUIRE(err != nullptr, SKCQ_ERR_CUDA, "reseed_noalloc: no device error word");
+  // Fewer concurrent problems when they do not all fit: CTAs stride over the set.
+  int grid = reseed_grid(nblk);
+  const int fit = (int)(RESEED_STATIC_BYTES / per_slot);
+  if (grid > fit) grid = fit;
+  cudaStream_t s = (cudaStream_t)stream;
+  cudaError_t e = cudaMemsetAsync(n_empty, 0, sizeof(int32_t) * nblk, s);
+  if (e != cudaSuccess) return set_error(SKCQ_ERR_CUDA, "reseed_noalloc: %s", cudaGetErrorString(e));
+  reseed_kernel<<<grid, RS_THREADS, 0, s>>>(metric, X, C, labels, nblk, n_pad, k_pad, bs, n, k, active, sums, counts,
+                                           n_empty, (uint8_t*)scratch, pow2_at_least(k_pad), err);
+  return check_launch("reseed_noalloc");
 }
