@@ -238,6 +238,81 @@ int skcq_reconstruct(const skcq_codec_desc* codecs, int n_codecs, int n_rows, in
 int skcq_refit_scales(const skcq_codec_desc* primary, const float* raw, int64_t raw_ld, const float* recon,
                       int64_t recon_ld, int n_rows, const uint8_t* row_zero, float* scales, void* stream);
 
+/* ---- codebook-expert forward (skcq/codebook_experts.py) -------------------- */
+
+#define SKCQ_DTYPE_F32 0
+#define SKCQ_DTYPE_BF16 1
+#define SKCQ_DTYPE_F16 2
+#define SKCQ_DTYPE_I8 3
+#define SKCQ_DTYPE_I16 4
+
+/* One codebook layer of a CodebookModule (_CodebookLayer, codebook_experts.py:77-150)
+ * in the forward's device layout. Only the primary layer carries scales
+ * (CodebookModule.forward applies p.scales only, codebook_experts.py:327-331). */
+typedef struct skcq_fwd_layer {
+  int n_blocks, bs, K;          /* bs <= 32, K <= 65536 */
+  const void* table;            /* (n_blocks, K, bs) centroid vectors (skcq_transpose_codebook) */
+  int table_dtype;              /* f32 | bf16 */
+  const uint16_t* idx16;        /* (E, n_blocks, out) assignments (skcq_pack_indices16) */
+  const void* scales;           /* (E, n_blocks, out) or NULL; f32 | bf16 | f16 | i8 | i16 */
+  int scale_dtype;
+  float q_scale;                /* multiplier for integer scales (scale_q_scale) */
+  const void* remainder;        /* (E, out, rem), f32 | bf16 */
+  int rem_dtype, rem;
+  const uint32_t* sign_mask;    /* (E, n_blocks, out) bit j: column b*bs+j negated, or NULL */
+} skcq_fwd_layer;
+
+/* out[i] = (uint16) idx[i] for the reference's int64 assignments
+ * (codebook_experts.py:95); an index outside [0, K) is stored as 0 and sets the
+ * device error (the reference's gather raises). */
+int skcq_pack_indices16(const int64_t* idx, int64_t n, int K, uint16_t* out, void* stream);
+
+/* table[b][k][j] = codebook[b][j][k]: the reference's (n_blocks, bs, K) codebook
+ * with each centroid's bs values made contiguous. dtype f32 | bf16. */
+int skcq_transpose_codebook(const void* codebook, int dtype, int n_blocks, int bs, int K, void* table, void* stream);
+
+/* mask[e][b][o] bit j = (signs[e][o][b*bs+j] < 0) for the int8 +-1 SSVQ signs
+ * (codebook_experts.py:53-55); a sign other than +-1 sets the device error. */
+int skcq_pack_sign_masks(const int8_t* signs, int E, int out, int64_t sign_ld, int n_blocks, int bs, uint32_t* mask,
+                         void* stream);
+
+/* Routing of CodebookExperts.forward (codebook_experts.py:462-470): pairs
+ * p = kpos * T + token sorted stably by expert into perm[T*k]; seg[e] ..
+ * seg[e+1] is expert e's run (seg has n_experts + 1 entries); row_of_pair[p]
+ * is the inverse permutation; active[0] is the number of experts with rows and
+ * active[1..] their ids ascending (n_experts + 1 entries). An expert id outside
+ * [0, n_experts) sets the device error (the reference's one_hot raises). */
+int skcq_route_sort(const int64_t* topk, int T, int k, int n_experts, int32_t* perm, int32_t* seg,
+                    int32_t* row_of_pair, int32_t* active, void* stream);
+
+/* CodebookModule.forward over expert segments (codebook_experts.py:325-339):
+ * for the rows r of segment s (expert seg_expert[s], or s when NULL; only the
+ * segments listed in `active` when it is not NULL), input row
+ * x[row_token[r] % T] (x[r] when row_token is NULL),
+ *   part[split][r][o] = partial sum over the split's block range of
+ *     sum_layers (scale * <x_b, signs * C_b[idx]>) + x_rem . rem_w (last split).
+ * The sum over the n_split slots is the module output (skcq_sum_splits,
+ * skcq_swiglu, skcq_combine). max_active bounds the active segments
+ * (min(n_seg, rows) is always safe). part holds n_split * P * out_dim floats. */
+int skcq_codebook_forward(const skcq_fwd_layer* layers, int n_layers, const void* x, int x_dtype, int64_t x_ld,
+                          const int32_t* row_token, int T, const int32_t* seg, const int32_t* seg_expert,
+                          const int32_t* active, int n_seg, int max_active, int in_dim, int out_dim, int n_split,
+                          float* part, int64_t P, void* stream);
+
+/* y[r][o] = sum over splits of part[split][r][o]; y f32 | bf16 with row stride y_ld. */
+int skcq_sum_splits(const float* part, int n_split, int64_t P, int out_dim, void* y, int y_dtype, int64_t y_ld,
+                    void* stream);
+
+/* out = silu(sum_s gate[s]) * sum_s up[s] over n elements per split
+ * (the SwiGLU of codebook_experts.py:427-433 with act_fn = SiLU). */
+int skcq_swiglu(const float* gate, const float* up, int n_split, int64_t n, float* out, void* stream);
+
+/* out[t] = sum over the token's k slots, in ascending (expert, kpos) order, of
+ * (sum_s part[s][row_of_pair[kpos * T + t]]) * weights[t][kpos]
+ * (codebook_experts.py:476-480). weights and out f32 | bf16. */
+int skcq_combine(const float* part, int n_split, int64_t P, const int32_t* row_of_pair, const int64_t* topk,
+                 const void* weights, int w_dtype, int T, int k, int H, void* out, int out_dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -63,6 +63,14 @@ _SIGS: dict[str, list] = {
     "skcq_quantize_scales": [P, L, I, P, P, P],
     "skcq_reconstruct": [P, I, I, I, P, L, P, L, P],
     "skcq_refit_scales": [P, P, L, P, L, I, P, P, P],
+    "skcq_pack_indices16": [P, L, I, P, P],
+    "skcq_transpose_codebook": [P, I, I, I, I, P, P],
+    "skcq_pack_sign_masks": [P, I, I, L, I, I, P, P],
+    "skcq_route_sort": [P, I, I, I, P, P, P, P, P],
+    "skcq_codebook_forward": [P, I, P, I, L, P, I, P, P, P, I, I, I, I, I, P, L, P],
+    "skcq_sum_splits": [P, I, L, I, P, I, L, P],
+    "skcq_swiglu": [P, P, I, L, P, P],
+    "skcq_combine": [P, I, L, P, P, P, I, I, I, I, P, I, P],
 }
 _RESTYPES = {"skcq_reseed_scratch_bytes": C.c_size_t}
 
@@ -105,7 +113,8 @@ _KERNELS_PER_CALL = {
     "skcq_finalize": 1, "skcq_flip_check": 1, "skcq_apply_flip": 1, "skcq_scatter_labels": 1,
     "skcq_row_zero_mask": 1, "skcq_spherical_scales": 1, "skcq_centroids_to_bf16": 1, "skcq_copy_remainder": 1,
     "skcq_ssvq_fold": 1, "skcq_quantize_centroids": 1, "skcq_quantize_scales": 3, "skcq_reconstruct": 1,
-    "skcq_refit_scales": 1,
+    "skcq_refit_scales": 1, "skcq_pack_indices16": 1, "skcq_transpose_codebook": 1, "skcq_pack_sign_masks": 1,
+    "skcq_route_sort": 1, "skcq_sum_splits": 1, "skcq_swiglu": 1, "skcq_combine": 1,
 }
 
 
@@ -131,7 +140,8 @@ def call(name: str, *args) -> int:
     if rc != 0:
         raise RuntimeError(f"{name} failed ({rc}): {last_error()}")
     if LAUNCHES.enabled:
-        LAUNCHES.kernels += _KERNELS_PER_CALL.get(name, 0)
+        # the grouped forward launches one kernel per codebook layer (argument 1)
+        LAUNCHES.kernels += args[1] if name == "skcq_codebook_forward" else _KERNELS_PER_CALL.get(name, 0)
         LAUNCHES.calls[name] = LAUNCHES.calls.get(name, 0) + 1
     return rc
 

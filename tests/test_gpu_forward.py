@@ -1,0 +1,342 @@
+"""GPU parity of the codebook-expert forward (skcq/codebook_experts.py) through
+the C ABI: CodebookModule against the oracle forward and the dense
+reconstruction, bf16 tolerance, state-dict round trip, the reference's failure
+modes, and CodebookExperts against the oracle and the reference's outputs."""
+
+from __future__ import annotations
+
+import io
+
+import numpy as np
+import pytest
+import torch
+
+from _helpers import PermReplay, load_golden, rel_err, sub
+from oracle import forward as of
+
+pytestmark = pytest.mark.gpu
+
+FWD_CASES = ["base", "single", "ssvq", "noncomm", "asym"]
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+
+
+def _fit(name, monkeypatch):
+    import test_gpu_build as B
+
+    g = sub(load_golden("codecs"), name + "__")
+    monkeypatch.setattr(torch, "randperm", PermReplay.from_case(g).torch_patch())
+    aqlm = B._product_aqlm(name)
+    cwr = aqlm.fit(torch.from_numpy(g["w"]).cuda())
+    return g, aqlm, cwr
+
+
+def _oracle_layers(mod):
+    """The module's own buffers as oracle layer dicts (f32, scales dequantised)."""
+    out = []
+    for lay in mod.layers:
+        s = None
+        if lay.scales is not None:
+            s = lay.scales.detach().float().cpu().numpy()
+            if not lay.scales.is_floating_point():
+                s = s * float(lay.scale_q_scale)
+        out.append({
+            "codebook": lay.codebook.detach().float().cpu().numpy(),
+            "assignments": lay.assignments.cpu().numpy(),
+            "scales": s,
+            "remainder": lay.remainder.float().cpu().numpy(),
+            "signs": lay.signs.cpu().numpy() if lay.signs is not None else None,
+            "block_size": lay.block_size,
+            "forward_mode": lay.forward_mode,
+        })
+    return out
+
+
+@pytest.mark.parametrize("name", FWD_CASES)
+def test_module_matches_oracle_and_reconstruction(name, monkeypatch):
+    """forward == oracle module forward on the same buffers, and
+    == hidden @ reconstruct(cwr)[e].T (tests/test_codebook.py:74-122)."""
+    from skcq_b200.codebook_experts import CodebookModule
+
+    g, aqlm, cwr = _fit(name, monkeypatch)
+    mod = CodebookModule.from_cwr(aqlm, cwr, out_dim=8).to(torch.float32).cuda()
+    hidden = torch.from_numpy(g["hidden"]).cuda()
+    layers = _oracle_layers(mod)
+    w = aqlm.reconstruct(cwr).double().cpu()
+    w = w.reshape(-1, 8, w.shape[1])
+    outs = []
+    for e in range(w.shape[0]):
+        out = mod(hidden, expert_idx=e)
+        assert out.dtype == torch.float32 and out.shape == (hidden.shape[0], 8)
+        out = out.double().cpu()
+        outs.append(out.numpy())
+        assert rel_err(out.numpy(), of.module_forward(layers, g["hidden"], e)) < 1e-6, f"expert {e}"
+        assert np.allclose(out.numpy(), g["hidden"].astype(np.float64) @ w[e].numpy().T, atol=1e-5, rtol=1e-5)
+    # where the fit itself reproduces the reference's, so does the forward
+    if rel_err(aqlm.reconstruct(cwr).cpu().numpy(), g["recon"]) < 2e-3:
+        assert rel_err(np.stack(outs), g["fwd"]) < 2e-3
+
+
+def test_module_on_reference_payload():
+    """The reference's own fitted payload (golden, 'base') loaded into the module
+    reproduces the reference module's outputs, independent of any fit."""
+    from _helpers import bf16_from_bits
+    from skcq_b200.codebook_experts import CodebookModule
+
+    g = sub(load_golden("codecs"), "base__")
+    rows, in_dim = int(g["meta"][0]), int(g["meta"][1])
+    E, out_dim, bs = rows // 8, 8, 4
+    nb = in_dim // bs
+    mod = CodebookModule.empty(nb, bs, out_dim, [16, 16], E)
+    sd = mod.state_dict()
+    for c in range(2):
+        cent = bf16_from_bits(g[f"c{c}_cent_bf16"]).reshape(nb, bs, 16)
+        sd[f"layers.{c}.codebook"] = torch.from_numpy(cent).float()
+        idx = g[f"c{c}_idxs"].reshape(nb, E, out_dim).transpose(1, 0, 2)
+        sd[f"layers.{c}.assignments"] = torch.from_numpy(np.ascontiguousarray(idx)).long()
+    sc = g["c0_scales"].reshape(E, out_dim, nb).transpose(0, 2, 1)
+    sd["layers.0.scales"] = torch.from_numpy(np.ascontiguousarray(sc)).float()
+    mod = mod.to(torch.float32)
+    mod.load_state_dict(sd)
+    mod = mod.cuda()
+    hidden = torch.from_numpy(g["hidden"]).cuda()
+    out = np.stack([mod(hidden, expert_idx=e).cpu().numpy() for e in range(E)])
+    # centroids are stored as bf16 in the fixture; the reference ran on f32 ones
+    assert rel_err(out, g["fwd"]) < 1e-2
+    ref = np.stack([of.module_forward(_oracle_layers(mod), g["hidden"], e) for e in range(E)])
+    assert rel_err(out, ref) < 1e-6
+
+
+def test_bf16_module_within_bf16_tolerance(monkeypatch):
+    from skcq_b200.codebook_experts import CodebookModule
+
+    g, aqlm, cwr = _fit("base", monkeypatch)
+    mod32 = CodebookModule.from_cwr(aqlm, cwr, out_dim=8).to(torch.float32).cuda()
+    mod16 = CodebookModule.from_cwr(aqlm, cwr, out_dim=8).to(torch.bfloat16).cuda()
+    hidden = torch.from_numpy(g["hidden"]).cuda()
+    for e in range(4):
+        a = mod32(hidden, e).double()
+        b16 = mod16(hidden.to(torch.bfloat16), e)
+        assert b16.dtype == torch.bfloat16
+        b = b16.double()
+        cos = torch.nn.functional.cosine_similarity(a.flatten(), b.flatten(), dim=0).item()
+        # tolerance: bf16 inputs, codebook and output (8 mantissa bits)
+        assert (a - b).abs().max().item() <= 2e-2 * a.abs().max().item() + 1e-3
+        assert cos >= 0.999
+
+
+def test_state_dict_round_trip(monkeypatch):
+    """tests/test_codebook.py:294-324: save, load, identical outputs."""
+    from skcq_b200.codebook_experts import CodebookModule
+
+    g, aqlm, cwr = _fit("ssvq", monkeypatch)
+    mod = CodebookModule.from_cwr(aqlm, cwr, out_dim=8).to(torch.bfloat16).cuda()
+    hidden = torch.randn(6, 12, generator=torch.Generator().manual_seed(3)).to(torch.bfloat16).cuda()
+    before = mod(hidden, expert_idx=2)
+    buf = io.BytesIO()
+    torch.save(mod.state_dict_with_meta(), buf)
+    buf.seek(0)
+    loaded = CodebookModule.load(buf).cuda()
+    assert loaded.primary.signs is not None
+    assert torch.equal(before, loaded(hidden, expert_idx=2))
+
+
+def test_shared_codebook_fails_like_reference(monkeypatch):
+    """A shared codebook cannot drive the per-expert forward: the reference's
+    gather fails (codebook_experts.py:49); so does this one, loudly."""
+    from skcq_b200.codebook_experts import CodebookModule
+
+    g, aqlm, cwr = _fit("shared", monkeypatch)
+    mod = CodebookModule.from_cwr(aqlm, cwr, out_dim=8).to(torch.float32).cuda()
+    with pytest.raises(RuntimeError):
+        mod(torch.randn(3, 12).cuda(), 0)
+
+
+def test_experts_forward_matches_oracle(monkeypatch):
+    """CodebookExperts.forward (codebook_experts.py:454-481) on a 4-expert top-2 MoE."""
+    from skcq_b200 import codebook as cb
+    from skcq_b200.codebook_experts import CodebookExperts, CodebookModule
+
+    g = load_golden("experts")
+    monkeypatch.setattr(torch, "randperm", PermReplay.from_case(g).torch_patch())
+    mods = []
+    for w, out_dim in ((g["wg"], 8), (g["wu"], 8), (g["wd"], 12)):
+        prim = cb.SphericalCodebook(cb.SphericalCodebookConfig(block_size=4, K=16, max_iters=10,
+                                                               norm_threshold=1e-9, skip_zeros=False))
+        res = [cb.EuclideanCodebook(cb.EuclideanCodebookConfig(block_size=4, K=8, max_iters=10,
+                                                               norm_threshold=1e-9, skip_zeros=False))]
+        aqlm = cb.AQLMCodebook(prim, res, cb.AQLMCodebookConfig(norm_threshold=1e-9))
+        cwr = aqlm.fit(torch.from_numpy(w).cuda())
+        mods.append(CodebookModule.from_cwr(aqlm, cwr, out_dim=out_dim).to(torch.float32).cuda())
+    ex = CodebookExperts(mods[0], mods[1], mods[2], 4, torch.nn.functional.silu)
+    hidden = torch.from_numpy(g["hidden"]).cuda()
+    y = ex(hidden, torch.from_numpy(g["topi"]).cuda(), torch.from_numpy(g["topw"]).cuda())
+    assert y.dtype == torch.float32 and y.shape == hidden.shape
+    y = y.cpu().numpy()
+    ref = of.experts_forward(*[_oracle_layers(m) for m in mods], 4, g["hidden"], g["topi"], g["topw"])
+    assert rel_err(y, ref) < 1e-6
+    assert rel_err(y, g["y"]) < 2e-3
+
+
+def test_experts_generic_activation_and_unrouted_expert(monkeypatch):
+    """A non-SiLU act_fn goes through the module's own activation; an expert
+    that no token selects contributes nothing (codebook_experts.py:465-467)."""
+    from skcq_b200.codebook_experts import CodebookExperts
+
+    E, H, I, T = 4, 32, 16, 10
+    gate = _random_module(E, I, H, [(4, 16, True), (4, 8, False)], seed=11)
+    up = _random_module(E, I, H, [(4, 16, True), (4, 8, False)], seed=12)
+    down = _random_module(E, H, I, [(4, 16, True), (4, 8, False)], seed=13)
+    gen = torch.Generator().manual_seed(14)
+    hidden = torch.randn(T, H, generator=gen)
+    topi = torch.randint(0, 3, (T, 2), generator=gen)  # expert 3 never routed
+    topi[:, 1] = (topi[:, 0] + 1) % 3
+    topw = torch.rand(T, 2, generator=gen)
+    ex = CodebookExperts(gate, up, down, E, torch.nn.functional.gelu)
+    y = ex(hidden.cuda(), topi.cuda(), topw.cuda()).cpu().numpy()
+    ref = np.zeros((T, H), np.float64)
+    Wg, Wu, Wd = ([_dense_from_module(m, e).numpy() for e in range(E)] for m in (gate, up, down))
+    hd = hidden.double().numpy()
+    for t in range(T):
+        for j in range(2):
+            e = int(topi[t, j])
+            gt = torch.nn.functional.gelu(torch.from_numpy(hd[t] @ Wg[e].T)).numpy()
+            ref[t] += float(topw[t, j]) * ((gt * (hd[t] @ Wu[e].T)) @ Wd[e].T)
+    assert rel_err(y, ref) < 1e-5
+
+
+def _random_module(E, out_dim, in_dim, specs, seed, dtype=torch.float32):
+    """CodebookModule with random buffers: specs = [(bs, K, scaled)]."""
+    from skcq_b200.codebook_experts import CodebookModule, _CodebookLayer
+
+    g = torch.Generator().manual_seed(seed)
+    layers = []
+    for bs, K, scaled in specs:
+        nb = in_dim // bs
+        rem = in_dim - nb * bs
+        layers.append(_CodebookLayer(
+            (torch.randn(nb, bs, K, generator=g) * 0.05).to(dtype),
+            torch.randint(0, K, (E, nb, out_dim), generator=g),
+            nb, bs, out_dim, K,
+            remainder=(torch.randn(E, out_dim, rem, generator=g) * 0.02).to(dtype) if rem else None,
+            scales=(torch.rand(E, nb, out_dim, generator=g) * 0.1).to(dtype) if scaled else None,
+        ))
+    return CodebookModule(torch.nn.ModuleList(layers), len(layers), out_dim).cuda()
+
+
+def _dense_from_module(mod, e):
+    """W_e (out, in) f64 from the module's own buffers (the math of _codebook_pass)."""
+    out_dim = mod.out_dim
+    parts = []
+    for lay in mod.layers:
+        cb = lay.codebook.detach().double().cpu()
+        a = lay.assignments[e].cpu()
+        nb, bs = lay.n_blocks, lay.block_size
+        w = torch.zeros(out_dim, nb * bs + lay.rem, dtype=torch.float64)
+        cols = torch.gather(cb, 2, a[:, None, :].expand(nb, bs, out_dim))  # (nb, bs, out)
+        if lay.scales is not None:
+            cols = cols * lay.scales[e].detach().double().cpu()[:, None, :]
+        w[:, : nb * bs] = cols.permute(2, 0, 1).reshape(out_dim, nb * bs)
+        if lay.rem:
+            w[:, nb * bs:] = lay.remainder[e].double().cpu()
+        parts.append(w)
+    width = max(p.shape[1] for p in parts)
+    return sum(torch.nn.functional.pad(p, (0, width - p.shape[1])) for p in parts)
+
+
+def test_decode_shapes_match_dense():
+    """Production codebook shapes (bs 8/16/4, K 4096/4096/65536; 16-bit indices
+    above 32767) on 4 experts of 768 x 2048 with a 13-column remainder on the
+    last codebook, decode batch of 8 tokens."""
+    mod = _random_module(4, 768, 2061, [(8, 4096, True), (16, 4096, False), (4, 65536, False)], seed=5)
+    x = torch.randn(8, 2061, generator=torch.Generator().manual_seed(6)).cuda()
+    for e in (0, 3):
+        out = mod(x, e).double().cpu()
+        ref = x.double().cpu() @ _dense_from_module(mod, e).t()
+        assert rel_err(out.numpy(), ref.numpy()) < 1e-5
+
+
+def test_grouped_segments_match_per_expert():
+    """run_segments over all experts at once equals per-expert calls
+    (prefill: 300 rows routed unevenly to 8 experts, one expert empty)."""
+    mod = _random_module(8, 96, 256, [(8, 256, True), (4, 256, False)], seed=21)
+    gen = torch.Generator().manual_seed(22)
+    counts = [40, 0, 100, 7, 1, 52, 60, 40]
+    rows = torch.randn(sum(counts), 256, generator=gen).cuda()
+    seg = torch.tensor(np.concatenate([[0], np.cumsum(counts)]), dtype=torch.int32).cuda()
+    for n_split in (1, 3):
+        part, S = mod.run_segments(rows, seg, None, 8, n_split=n_split)
+        assert S == n_split and part.shape == (n_split, rows.shape[0], 96)
+        y = part.sum(0).cpu()
+        start = 0
+        for e, c in enumerate(counts):
+            if c:
+                ye = mod(rows[start:start + c], e).cpu()
+                assert rel_err(y[start:start + c].numpy(), ye.numpy()) < 1e-6
+            start += c
+
+
+def test_invalid_routing_raises():
+    """An expert id outside [0, num_experts) raises, as the reference's one_hot does."""
+    from skcq_b200.codebook_experts import CodebookExperts
+
+    gate = _random_module(4, 8, 16, [(4, 16, True)], seed=31)
+    up = _random_module(4, 8, 16, [(4, 16, True)], seed=32)
+    down = _random_module(4, 16, 8, [(4, 16, True)], seed=33)
+    ex = CodebookExperts(gate, up, down, 4, torch.nn.functional.silu)
+    topi = torch.tensor([[0, 1], [2, 4]]).cuda()
+    with pytest.raises(RuntimeError):
+        ex(torch.randn(2, 16).cuda(), topi, torch.ones(2, 2).cuda())
+    # the device stays usable and valid routing works afterwards
+    y = ex(torch.randn(2, 16).cuda(), torch.tensor([[0, 1], [2, 3]]).cuda(), torch.ones(2, 2).cuda())
+    assert torch.isfinite(y).all()
+
+
+def test_out_of_range_assignment_raises():
+    from skcq_b200.codebook_experts import CodebookModule, _CodebookLayer
+
+    lay = _CodebookLayer(torch.randn(2, 4, 16), torch.full((1, 2, 8), 16, dtype=torch.long), 2, 4, 8, 16)
+    mod = CodebookModule(torch.nn.ModuleList([lay]), 1, 8).cuda()
+    with pytest.raises(RuntimeError):
+        mod(torch.randn(3, 8).cuda(), 0)
+
+
+def test_expert_index_semantics():
+    mod = _random_module(3, 8, 16, [(4, 16, True)], seed=41)
+    x = torch.randn(2, 16).cuda()
+    assert torch.equal(mod(x, -1), mod(x, 2))
+    with pytest.raises(IndexError):
+        mod(x, 3)
+
+
+def test_large_batch_route_sort_order():
+    """Route sort of 4096 tokens x top-8 over 128 experts (chunked warp-ranking
+    path) and over 300 experts (owner-scan path): the grouped result equals
+    the per-token reference order."""
+    from skcq_b200.codebook_experts import CodebookExperts
+
+    for E in (128, 300):
+        T, H, I = 512 if E == 300 else 4096, 32, 16
+        gen = torch.Generator().manual_seed(E)
+        gate = _random_module(E, I, H, [(8, 32, True)], seed=51)
+        up = _random_module(E, I, H, [(8, 32, True)], seed=52)
+        down = _random_module(E, H, I, [(8, 32, True)], seed=53)
+        hidden = torch.randn(T, H, generator=gen)
+        topi = torch.rand(T, E, generator=gen).argsort(-1)[:, :8]
+        topw = torch.rand(T, 8, generator=gen)
+        y = CodebookExperts(gate, up, down, E, torch.nn.functional.silu)(hidden.cuda(), topi.cuda(), topw.cuda())
+        # reference loop on the GPU modules (codebook_experts.py:462-480)
+        ref = torch.zeros(T, H).cuda()
+        mask = torch.nn.functional.one_hot(topi.cuda(), E).permute(2, 1, 0)
+        for e in range(E):
+            pos, tok = torch.where(mask[e])
+            if tok.numel() == 0:
+                continue
+            xs = hidden.cuda()[tok]
+            inter = torch.nn.functional.silu(gate(xs, e)) * up(xs, e)
+            ref.index_add_(0, tok, down(inter, e) * topw.cuda()[tok, pos, None])
+        assert rel_err(y.cpu().numpy(), ref.cpu().numpy()) < 1e-5
