@@ -141,6 +141,22 @@ int skcq_reseed_noalloc(int metric, const float* X, const float* C, const int32_
                         int k_pad, int bs, const int32_t* n, const int32_t* k, const int32_t* active, float* sums,
                         const int32_t* counts, int32_t* n_empty, void* stream);
 
+/* Reseed for row-sharded problems (each rank holds a slice of every problem's
+ * points; sums/counts already summed over ranks). For each active problem
+ * with empty clusters (from the global `counts`), writes this rank's
+ * min(n_empty, n[b]) worst-fit points, worst first, using the reseed order of
+ * skcq_reseed with the point's global index gofs[b] + i breaking ties:
+ * keys[b][e] = (score key << 32 | global index) ^ 2^63 (so signed int64 order
+ * is the selection order) and vecs[b][e][:] = X[b][i]. keys must be
+ * pre-filled with INT64_MAX and vecs with 0 ([nblk][m_max] / [nblk][m_max][bs],
+ * m_max >= every n_empty); n_empty[b] receives the count. Merging the ranks'
+ * lists and taking the n_empty smallest keys gives the single-process choice.
+ * scratch as for skcq_reseed. */
+int skcq_reseed_candidates(int metric, const float* X, const float* C, const int32_t* labels, int nblk, int n_pad,
+                           int k_pad, int bs, const int32_t* n, const int32_t* k, const int32_t* active,
+                           const int32_t* counts, const int64_t* gofs, int m_max, int64_t* keys, float* vecs,
+                           int32_t* n_empty, void* scratch, void* stream);
+
 /* New centroids, movement and convergence (kmeans.py:174-188, 231-244):
  * cosine C = normalize(sums); euclidean C = sums / counts (reseeded clusters
  * take the point). moved = ||C_new - C_old||_F; a problem whose moved < 1e-6

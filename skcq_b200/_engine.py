@@ -189,21 +189,30 @@ def lloyd(
     max_iters: int,
     init_cosine: Callable[[int, int], torch.Tensor] | None = None,
     init_perms: list[torch.Tensor | None] | None = None,
+    shard=None,
+    n_global: torch.Tensor | None = None,
+    gofs: torch.Tensor | None = None,
 ) -> KmeansRun:
     """Run every problem of ``pts`` to convergence or ``max_iters``.
 
     Cosine problems start from ``init_cosine(k_eff, bs)`` (the Sobol directions
     of kmeans.py:69-74); euclidean problems from ``X[b][init_perms[b][:k_eff]]``
     (kmeans.py:201-202). Problems with no points are left inactive.
+
+    With ``shard`` (a ``distributed.RowShard``), ``pts`` holds this rank's
+    slice of every problem: ``n_global`` points in all, this rank's first at
+    global index ``gofs``; sums and counts are summed over ranks each
+    iteration and the reseed merges every rank's candidates.
     """
     dev = pts.X.device
     nblk, bs, n_pad, metric = pts.nblk, pts.bs, pts.n_pad, pts.metric
-    k_host = [min(K, nb) for nb in pts.n_host]
+    n_all = [int(v) for v in n_global.tolist()] if shard is not None else pts.n_host
+    k_host = [min(K, nb) for nb in n_all]
     k_pad = round_up(max(k_host + [1]), CENT_TILE)
     kp = pts.kp
     s = stream()
     k_dev = torch.tensor(k_host, dtype=torch.int32, device=dev)
-    active = (pts.n > 0).to(torch.int32)
+    active = (torch.tensor(n_all, device=dev) > 0).to(torch.int32)
     C = torch.zeros(nblk, k_pad, bs, dtype=torch.float32, device=dev)
     if metric == COSINE:
         cache: dict[int, torch.Tensor] = {}
@@ -217,7 +226,14 @@ def lloyd(
         for b, kb in enumerate(k_host):
             if kb > 0:
                 perm[b, :kb] = init_perms[b][:kb].to(dev)
-        call("skcq_init_from_points", ptr(pts.X), n_pad, bs, nblk, ptr(perm), k_pad, ptr(k_dev), k_pad, ptr(C), s)
+        if shard is None:
+            call("skcq_init_from_points", ptr(pts.X), n_pad, bs, nblk, ptr(perm), k_pad, ptr(k_dev), k_pad, ptr(C),
+                 s)
+        else:
+            from skcq_b200 import distributed
+
+            C.copy_(distributed.owned_init(pts.X, perm, k_dev, gofs.to(dev), pts.n))
+            shard.all_reduce_sum_(C)
     B = torch.empty(nblk, k_pad * kp, dtype=torch.float32, device=dev)
     cnorm = torch.empty(nblk, k_pad, dtype=torch.float32, device=dev)
     sums = torch.zeros(nblk, k_pad, bs, dtype=torch.float32, device=dev)
@@ -243,9 +259,12 @@ def lloyd(
         T.run("assign", lambda: assign_call(pts, B, C, cnorm, k_pad, k_dev, active, labels), work, padded)
         T.run("update", lambda: call("skcq_update", ptr(pts.R), ptr(labels), nblk, n_pad, k_pad, bs, ptr(pts.n),
                                      ptr(k_dev), ptr(active), ptr(sums), ptr(counts), s))
-        T.run("reseed", lambda: call("skcq_reseed", metric, ptr(pts.X), ptr(C), ptr(labels), nblk, n_pad, k_pad, bs,
-                                     ptr(pts.n), ptr(k_dev), ptr(active), ptr(sums), ptr(counts), ptr(n_empty),
-                                     ptr(scratch), s))
+        if shard is None:
+            T.run("reseed", lambda: call("skcq_reseed", metric, ptr(pts.X), ptr(C), ptr(labels), nblk, n_pad, k_pad,
+                                         bs, ptr(pts.n), ptr(k_dev), ptr(active), ptr(sums), ptr(counts),
+                                         ptr(n_empty), ptr(scratch), s))
+        else:
+            _sharded_reseed(shard, pts, C, labels, k_pad, k_dev, active, sums, counts, n_empty, scratch, gofs)
         T.run("finalize", lambda: call("skcq_finalize", metric, ptr(sums), ptr(counts), ptr(n_empty), nblk, k_pad,
                                        bs, ptr(k_dev), ptr(active), ptr(converged), ptr(iters_run), ptr(moved),
                                        ptr(nempty_hist), it, ptr(C), s))
@@ -264,6 +283,30 @@ def lloyd(
         converged=[bool(v) for v in converged.cpu().tolist()],
         moved=moved.cpu().numpy(), n_empty=nempty_hist.cpu().numpy(), cnorm=cnorm,
     )
+
+
+def _sharded_reseed(shard, pts: PointSet, C, labels, k_pad, k_dev, active, sums, counts, n_empty, scratch,
+                    gofs) -> None:
+    """Sum sums/counts over ranks, then reseed empty clusters from the merged
+    worst-fit candidates of all ranks (same choice as skcq_reseed on the
+    unsharded problem)."""
+    from skcq_b200 import distributed
+
+    shard.all_reduce_sum_(sums)
+    shard.all_reduce_sum_(counts)
+    empty = distributed.empty_clusters(counts, k_dev, active)
+    ne = empty.sum(1)
+    n_empty.copy_(ne.to(torch.int32))
+    m_max = int(ne.max().item()) if ne.numel() else 0
+    if m_max == 0:
+        return
+    dev = pts.X.device
+    keys = torch.full((pts.nblk, m_max), distributed.INT64_MAX, dtype=torch.int64, device=dev)
+    vecs = torch.zeros(pts.nblk, m_max, pts.bs, dtype=torch.float32, device=dev)
+    call("skcq_reseed_candidates", pts.metric, ptr(pts.X), ptr(C), ptr(labels), pts.nblk, pts.n_pad, k_pad, pts.bs,
+         ptr(pts.n), ptr(k_dev), ptr(active), ptr(counts), ptr(gofs.to(dev)), m_max, ptr(keys), ptr(vecs),
+         ptr(n_empty), ptr(scratch), stream())
+    distributed.merge_reseed(shard.all_gather(keys), shard.all_gather(vecs), empty, sums)
 
 
 def assign(pts: PointSet, run: KmeansRun) -> torch.Tensor:

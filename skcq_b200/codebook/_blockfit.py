@@ -12,7 +12,7 @@ from dataclasses import dataclass
 
 import torch
 
-from skcq_b200 import _engine
+from skcq_b200 import _engine, distributed
 from skcq_b200.codebook.events import Experiment
 from skcq_b200.codebook.kmeans import emit_run_events, sobol_first_orthant
 
@@ -45,12 +45,20 @@ def fit_blocks(
     dev = raw.device
     n_rows, in_dim = raw.shape
     n_blocks = in_dim // bs
+    shard = distributed.current()
+    if shard is not None and shared:
+        raise NotImplementedError("row-sharded fits support per-block codebooks only (shared=False)")
     pts = _engine.gather_block_points(raw, bs, n_blocks, shared, norm_threshold, skip_zeros, metric)
     nblk = pts.nblk
+    n_global = gofs = None
+    n_all = pts.n_host
+    if shard is not None:
+        n_global, gofs = distributed.global_counts(shard, pts.n)
+        n_all = [int(v) for v in n_global.tolist()]
     # Centroid count each block would stack (spherical.py:250-256, euclidean.py:462-468):
     # empty blocks give min(K, 1) (spherical) or K (euclidean) zero centroids.
     empty_k = min(K, 1) if metric == _engine.COSINE else K
-    k_each = [min(K, nb) if nb > 0 else empty_k for nb in pts.n_host]
+    k_each = [min(K, nb) if nb > 0 else empty_k for nb in n_all]
     if len(set(k_each)) != 1:
         raise RuntimeError(
             f"stack expects each tensor to be equal size, but blocks have {sorted(set(k_each))} centroids"
@@ -61,9 +69,11 @@ def fit_blocks(
     sub_perms: list[torch.Tensor | None] = []
     init_perms: list[torch.Tensor | None] = []
     any_sub = False
-    for nb in pts.n_host:
+    for nb in n_all:
         sp = None
         if nb > 0 and max_train_samples > 0 and nb > max_train_samples:
+            if shard is not None:
+                raise NotImplementedError("row-sharded fits do not subsample (max_train_samples)")
             sp = torch.randperm(nb, device=dev)
             any_sub = True
         sub_perms.append(sp)
@@ -73,24 +83,25 @@ def fit_blocks(
         else:
             init_perms.append(None)
     train = _engine.subsample_points(raw, bs, n_blocks, shared, pts, sub_perms, max_train_samples) if any_sub else pts
-    if max(pts.n_host) == 0:
+    if max(n_all) == 0:
         run = None
         labels = torch.zeros(nblk, pts.n_pad, dtype=torch.int32, device=dev)
     else:
         run = _engine.lloyd(
             train, K, max_iters,
             init_cosine=lambda k, d: sobol_first_orthant(k, d, dev),
-            init_perms=init_perms,
+            init_perms=init_perms, shard=shard, n_global=n_global, gofs=gofs,
         )
         labels = _engine.assign(pts, run) if any_sub else run.labels
         metric_name = "cosine" if metric == _engine.COSINE else "euclidean"
+        n_train = n_all if shard is not None else train.n_host
         for b in range(nblk):
-            if pts.n_host[b] == 0:
+            if n_all[b] == 0:
                 continue
             emit_run_events(
                 owner, run, b,
                 name if shared else f"{name} blk={b}",
-                metric_name, max_iters, train.n_host[b],
+                metric_name, max_iters, n_train[b],
                 0 if shared else b, 1 if shared else n_blocks,
             )
     idxs = _engine.scatter_labels(pts, labels, shared, n_rows, n_blocks)

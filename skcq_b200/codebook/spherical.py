@@ -11,7 +11,7 @@ from dataclasses import dataclass
 
 import torch
 
-from skcq_b200 import _engine
+from skcq_b200 import _engine, distributed
 from skcq_b200._lib import call, ptr, stream
 from skcq_b200.codebook._blockfit import fit_blocks, stacked_centroids
 from skcq_b200.codebook.base import WeightsCodebookBase
@@ -150,6 +150,9 @@ class SphericalCodebook(WeightsCodebookBase[SphericalCWR], Experiment):
         flags = torch.empty(pts.nblk, dtype=torch.int64, device=run.C.device)
         call("skcq_flip_check", ptr(pts.R), ptr(run.C), ptr(fit.labels), pts.nblk, pts.n_pad, run.k_pad, bs,
              ptr(pts.n), ptr(flags), stream())
+        shard = distributed.current()
+        if shard is not None:  # the flip names labels of any rank's points
+            flags = distributed.or_over_ranks(shard, flags)
         host = [int(v) & 0xFFFFFFFFFFFFFFFF for v in flags.cpu().tolist()]
         if any(h >> 63 for h in host):
             raise IndexError(f"index out of range in the negative-scale flip: a label >= block size {bs}")

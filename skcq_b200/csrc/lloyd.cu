@@ -107,12 +107,23 @@ __device__ void bitonic_sort(uint64_t* a, int P) {
   }
 }
 
+// Candidate mode (keys != NULL, row-sharded problems): instead of seeding, the
+// min(n_empty, n) worst local points are written, worst first, as
+// (key ^ 2^63, vector) with the point's global index (gofs[b] + i) in the key,
+// for a cross-rank merge.
+struct ReseedCand {
+  const int64_t* gofs;
+  int m_max;
+  int64_t* keys;  // [nblk][m_max], pre-filled with INT64_MAX
+  float* vecs;    // [nblk][m_max][bs]
+};
+
 __global__ void __launch_bounds__(RS_THREADS)
 reseed_kernel(int metric, const float* __restrict__ X, const float* __restrict__ C,
               const int32_t* __restrict__ labels, int nblk, int n_pad, int k_pad, int bs,
               const int32_t* __restrict__ n, const int32_t* __restrict__ kvec, const int32_t* __restrict__ active,
               float* __restrict__ sums, const int32_t* __restrict__ counts, int32_t* __restrict__ n_empty_out,
-              uint8_t* scratch, int k_pow2, int* err) {
+              uint8_t* scratch, int k_pow2, int* err, ReseedCand cand) {
   __shared__ uint64_t s_sort[RS_SMEM_SORT];
   __shared__ int s_hist[256];
   __shared__ uint64_t s_prefix;
@@ -134,14 +145,16 @@ reseed_kernel(int metric, const float* __restrict__ X, const float* __restrict__
       n_empty += tot;
     }
     if (threadIdx.x == 0) n_empty_out[b] = n_empty;
-    if (n_empty == 0) continue;
+    const int n_sel = cand.keys ? min(n_empty, nb) : n_empty;
+    if (n_sel == 0) continue;
+    const uint32_t gofs = cand.keys ? (uint32_t)cand.gofs[b] : 0u;
     const float* Xb = X + (int64_t)b * n_pad * bs;
     const float* Cb = C + (int64_t)b * k_pad * bs;
     const int32_t* Lb = labels + (int64_t)b * n_pad;
     // 2. radix select of the n_empty smallest (score-key, point) composites
     if (threadIdx.x == 0) {
       s_prefix = 0;
-      s_need = n_empty;
+      s_need = n_sel;
       s_done = 0;
     }
     __syncthreads();
@@ -152,7 +165,7 @@ reseed_kernel(int metric, const float* __restrict__ X, const float* __restrict__
       const uint64_t hmask = shift == 56 ? 0ull : (~0ull << (shift + 8));
       const uint64_t pref = s_prefix;
       for (int i = threadIdx.x; i < nb; i += blockDim.x) {
-        const uint64_t key = reseed_key(metric, Xb + (int64_t)i * bs, Cb + (int64_t)Lb[i] * bs, bs, i);
+        const uint64_t key = reseed_key(metric, Xb + (int64_t)i * bs, Cb + (int64_t)Lb[i] * bs, bs, gofs + i);
         if ((key & hmask) == (pref & hmask)) atomicAdd(&s_hist[(key >> shift) & 255], 1);
       }
       __syncthreads();
@@ -176,27 +189,37 @@ reseed_kernel(int metric, const float* __restrict__ X, const float* __restrict__
     }
     // 3. collect the selected composites
     int m_pow2 = 1;
-    while (m_pow2 < n_empty) m_pow2 <<= 1;
+    while (m_pow2 < n_sel) m_pow2 <<= 1;
     uint64_t* list = m_pow2 <= RS_SMEM_SORT ? s_sort : g_list;
     if (threadIdx.x == 0) s_count = 0;
     __syncthreads();
     for (int i = threadIdx.x; i < m_pow2; i += blockDim.x) list[i] = ~0ull;
     __syncthreads();
     for (int i = threadIdx.x; i < nb; i += blockDim.x) {
-      const uint64_t key = reseed_key(metric, Xb + (int64_t)i * bs, Cb + (int64_t)Lb[i] * bs, bs, i);
+      const uint64_t key = reseed_key(metric, Xb + (int64_t)i * bs, Cb + (int64_t)Lb[i] * bs, bs, gofs + i);
       if (key <= thresh) {
         const int pos = atomicAdd(&s_count, 1);
         if (pos < m_pow2) list[pos] = key;
       }
     }
     __syncthreads();
-    if (s_count != n_empty) {
+    if (s_count != n_sel) {
       if (threadIdx.x == 0) atomicCAS(err, 0, 21);
       __syncthreads();
       continue;
     }
     // 4. order them (ascending key = worst first)
     bitonic_sort(list, m_pow2);
+    if (cand.keys) {
+      for (int t = threadIdx.x; t < n_sel * bs; t += blockDim.x) {
+        const int e = t / bs, j = t - e * bs;
+        const uint32_t row = (uint32_t)(list[e] & 0xffffffffu) - gofs;
+        cand.vecs[((int64_t)b * cand.m_max + e) * bs + j] = Xb[(int64_t)row * bs + j];
+        if (j == 0) cand.keys[(int64_t)b * cand.m_max + e] = (int64_t)(list[e] ^ (1ull << 63));
+      }
+      __syncthreads();
+      continue;
+    }
     // 5. the i-th worst point seeds the i-th empty cluster
     float* Sb = sums + (int64_t)b * k_pad * bs;
     for (int t = threadIdx.x; t < n_empty * bs; t += blockDim.x) {
@@ -326,8 +349,28 @@ extern "C" int skcq_reseed(int metric, const float* X, const float* C, const int
   if (e != cudaSuccess) return set_error(SKCQ_ERR_CUDA, "reseed: %s", cudaGetErrorString(e));
   reseed_kernel<<<reseed_grid(nblk), RS_THREADS, 0, s>>>(metric, X, C, labels, nblk, n_pad, k_pad, bs, n, k, active,
                                                          sums, counts, n_empty, (uint8_t*)scratch,
-                                                         pow2_at_least(k_pad), err);
+                                                         pow2_at_least(k_pad), err, ReseedCand{});
   return check_launch("reseed");
+}
+
+extern "C" int skcq_reseed_candidates(int metric, const float* X, const float* C, const int32_t* labels, int nblk,
+                                      int n_pad, int k_pad, int bs, const int32_t* n, const int32_t* k,
+                                      const int32_t* active, const int32_t* counts, const int64_t* gofs, int m_max,
+                                      int64_t* keys, float* vecs, int32_t* n_empty, void* scratch, void* stream) {
+  SKCQ_REQUIRE(X && C && labels && n && k && counts && gofs && keys && vecs && n_empty && scratch, SKCQ_ERR_INVALID,
+               "reseed_candidates: null pointer");
+  SKCQ_REQUIRE(bs > 0 && bs <= 64 && m_max > 0, SKCQ_ERR_INVALID, "reseed_candidates: bs %d, m_max %d", bs, m_max);
+  SKCQ_REQUIRE(((uintptr_t)scratch & 7) == 0, SKCQ_ERR_INVALID, "reseed_candidates: scratch must be 8-byte aligned");
+  int* err = device_error_word();
+  SKCQ_REQUIRE(err != nullptr, SKCQ_ERR_CUDA, "reseed_candidates: no device error word");
+  cudaStream_t s = (cudaStream_t)stream;
+  cudaError_t e = cudaMemsetAsync(n_empty, 0, sizeof(int32_t) * nblk, s);
+  if (e != cudaSuccess) return set_error(SKCQ_ERR_CUDA, "reseed_candidates: %s", cudaGetErrorString(e));
+  reseed_kernel<<<reseed_grid(nblk), RS_THREADS, 0, s>>>(metric, X, C, labels, nblk, n_pad, k_pad, bs, n, k, active,
+                                                         nullptr, counts, n_empty, (uint8_t*)scratch,
+                                                         pow2_at_least(k_pad), err,
+                                                         ReseedCand{gofs, m_max, keys, vecs});
+  return check_launch("reseed_candidates");
 }
 
 extern "C" int skcq_finalize(int metric, float* sums, int32_t* counts, const int32_t* n_empty, int nblk, int k_pad,
@@ -404,6 +447,6 @@ extern "C" int skcq_reseed_noalloc(int metric, const float* X, const float* C, c
   cudaError_t e = cudaMemsetAsync(n_empty, 0, sizeof(int32_t) * nblk, s);
   if (e != cudaSuccess) return set_error(SKCQ_ERR_CUDA, "reseed_noalloc: %s", cudaGetErrorString(e));
   reseed_kernel<<<grid, RS_THREADS, 0, s>>>(metric, X, C, labels, nblk, n_pad, k_pad, bs, n, k, active, sums, counts,
-                                           n_empty, (uint8_t*)scratch, pow2_at_least(k_pad), err);
+                                           n_empty, (uint8_t*)scratch, pow2_at_least(k_pad), err, ReseedCand{});
   return check_launch("reseed_noalloc");
 }
