@@ -92,8 +92,9 @@ class BlockIterCounter:
         self.total += self._n * e.iters_run
 
 
-def build_step(wl: dict, weights: dict[str, torch.Tensor], rel_err: bool = False):
-    """One AQLM build of every projection. Returns (block_iters, rel_errs)."""
+def build_step(wl: dict, weights: dict[str, torch.Tensor], rel_err: bool = False, keep: dict | None = None):
+    """One AQLM build of every projection. Returns (block_iters, rel_errs);
+    ``keep`` receives {name: (aqlm, cwr)} when given."""
     total = 0
     errs = []
     for name, _, _ in projections(wl):
@@ -105,8 +106,142 @@ def build_step(wl: dict, weights: dict[str, torch.Tensor], rel_err: bool = False
         if rel_err:
             wf = w.float()
             errs.append(torch.linalg.vector_norm(wf - aqlm.reconstruct(cwr)) / torch.linalg.vector_norm(wf))
+        if keep is not None:
+            keep[name] = (aqlm, cwr)
         del cwr, aqlm
     return total, errs
+
+
+# ---------------------------------------------------------------------------
+# Forward: the fitted layer as CodebookExperts, decode and prefill
+# ---------------------------------------------------------------------------
+
+
+def _route(T: int, E: int, k: int, gen: torch.Generator, dev: str, zipf: float | None = None):
+    """Top-k routing. Decode: softmax of N(0,1) logits, top-k, renormalised
+    (Qwen-style). Prefill: expert popularity p_e ~ rank^-zipf over a seeded
+    permutation of ranks, top-k without replacement by Gumbel-top-k on log p."""
+    if zipf is None:
+        logits = torch.randn(T, E, generator=gen, device=dev)
+    else:
+        ranks = torch.randperm(E, generator=gen, device=dev).float() + 1.0
+        logp = -zipf * torch.log(ranks)
+        u = torch.rand(T, E, generator=gen, device=dev).clamp_(1e-20, 1.0)
+        logits = logp[None, :] - torch.log(-torch.log(u))
+    w, idx = torch.topk(torch.softmax(logits, -1), k, dim=-1)
+    return idx, (w / w.sum(-1, keepdim=True)).float()
+
+
+def _dense_experts(W: dict, E: int, H: int):
+    """Dense bf16 experts of the same weights (W = reconstruct, bf16): tokens
+    sorted by expert and one library grouped GEMM per projection (the dense
+    comparator)."""
+
+    def fwd(x, topi, topw):
+        T, k = topi.shape
+        flat = topi.t().reshape(-1)
+        order = torch.sort(flat, stable=True).indices
+        offs = torch.cumsum(torch.bincount(flat, minlength=E), 0).to(torch.int32)
+        tok = order % T
+        xs = x[tok]
+        g = torch._grouped_mm(xs, W["gate"], offs=offs)
+        u = torch._grouped_mm(xs, W["up"], offs=offs)
+        inter = (torch.nn.functional.silu(g.float()) * u.float()).to(torch.bfloat16)
+        d = torch._grouped_mm(inter, W["down"], offs=offs).float()
+        out = torch.zeros(T, H, device=x.device)
+        out.index_add_(0, tok, d * topw.t().reshape(-1)[order][:, None])
+        return out.to(torch.bfloat16)
+
+    return fwd
+
+
+def _time_ms(fn, iters: int, flush: torch.Tensor) -> float:
+    """Median device time of fn over iters runs, L2 flushed before each."""
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(iters):
+        flush.zero_()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        torch.cuda.synchronize()
+        ts.append(s.elapsed_time(e))
+    return statistics.median(ts)
+
+
+def _decode_bytes(ex, topi: torch.Tensor) -> float:
+    """Algorithmic bytes of one decode forward: packed indices and scales of
+    the active experts, the centroid vectors they touch (unique), x and y."""
+    act = torch.unique(topi)
+    total = 0.0
+    for mod in (ex.gate, ex.up, ex.down):
+        for i, lay in enumerate(mod.layers):
+            L = lay._layout(topi.device)
+            idx = L["idx16"][act].to(torch.int64) & 0xFFFF  # (A, nb, out)
+            nb, K, bs = L["table"].shape
+            total += idx.numel() * 2
+            if i == 0 and L["scales"] is not None:
+                total += idx.numel() * L["scales"].element_size()
+            keys = idx + torch.arange(nb, device=idx.device)[None, :, None] * K
+            total += torch.unique(keys).numel() * bs * L["table"].element_size()
+    T = topi.shape[0]
+    return total + T * ex.gate.layers[0].n_blocks * ex.gate.layers[0].block_size * 2 * 2
+
+
+def forward_bench(wl: dict, fits: dict, dev: str, peaks: dict) -> dict:
+    from skcq_b200.codebook_experts import CodebookExperts, CodebookModule
+
+    E, H, I = wl["experts"], wl["hidden"], wl["inter"]
+    outs = {"gate": I, "up": I, "down": H}
+    mods, dense = {}, {}
+    for name, (aqlm, cwr) in fits.items():
+        mods[name] = CodebookModule.from_cwr(aqlm, cwr, out_dim=outs[name]).to(torch.bfloat16)
+        w = aqlm.reconstruct(cwr).to(torch.bfloat16)
+        dense[name] = w.reshape(E, outs[name], w.shape[1]).transpose(1, 2)  # (E, in, out) view
+        del w
+    ex = CodebookExperts(mods["gate"], mods["up"], mods["down"], E, torch.nn.functional.silu)
+    ex.check_errors = False
+    dfwd = _dense_experts(dense, E, H)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    gen = torch.Generator(device=dev).manual_seed(4321)
+    res = {"decode": [], "prefill": None}
+    for T in (1, 8, 64):
+        x = torch.randn(T, H, generator=gen, device=dev).to(torch.bfloat16)
+        topi, topw = _route(T, E, 8, gen, dev)
+        y, yd = ex(x, topi, topw).float(), dfwd(x, topi, topw).float()
+        cos = torch.nn.functional.cosine_similarity(y.flatten(), yd.flatten(), dim=0).item()
+        ms = _time_ms(lambda: ex(x, topi, topw), 20, flush)
+        md = _time_ms(lambda: dfwd(x, topi, topw), 20, flush)
+        nbytes = _decode_bytes(ex, topi)
+        n_act = int(torch.unique(topi).numel())
+        res["decode"].append({
+            "tokens": T, "active_experts": n_act, "tokens_per_s": T / (ms / 1e3), "ms": ms,
+            "dense_bf16_tokens_per_s": T / (md / 1e3), "dense_ms": md, "cos_vs_dense": cos,
+            "algorithmic_bytes": nbytes, "achieved_gbs": nbytes / (ms / 1e3) / 1e9,
+            "frac_hbm": nbytes / (ms / 1e3) / 1e9 / peaks["hbm_gbs"],
+            "dense_bytes": n_act * 3 * H * I * 2,
+        })
+    T = 16384
+    x = torch.randn(T, H, generator=gen, device=dev).to(torch.bfloat16)
+    topi, topw = _route(T, E, 8, gen, dev, zipf=1.1)
+    y, yd = ex(x, topi, topw).float(), dfwd(x, topi, topw).float()
+    cos = torch.nn.functional.cosine_similarity(y.flatten(), yd.flatten(), dim=0).item()
+    ms = _time_ms(lambda: ex(x, topi, topw), 3, flush)
+    md = _time_ms(lambda: dfwd(x, topi, topw), 5, flush)
+    flops = 2.0 * T * 8 * 3 * H * I
+    counts = torch.bincount(topi.flatten(), minlength=E)
+    res["prefill"] = {
+        "tokens": T, "pairs": T * 8, "max_rows_per_expert": int(counts.max()), "tokens_per_s": T / (ms / 1e3),
+        "ms": ms, "dense_bf16_tokens_per_s": T / (md / 1e3), "dense_ms": md, "cos_vs_dense": cos,
+        "achieved_tflops": flops / (ms / 1e3) / 1e12, "frac_bf16": flops / (ms / 1e3) / 1e12 / peaks["bf16_tflops"],
+    }
+    from skcq_b200 import _lib
+
+    _lib.poll_device_error()
+    return res
 
 
 class ClockSampler:
@@ -301,6 +436,9 @@ def main() -> None:
     ap.add_argument("--workload", default="layer", choices=list(WORKLOADS))
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg")
+    ap.add_argument("--no-forward", action="store_true", help="skip the codebook-expert forward leg")
+    ap.add_argument("--mode", default="farm", choices=["farm", "rows"],
+                    help="N > 1: farm = one layer per rank (weak scaling); rows = one layer row-sharded (strong)")
     args = ap.parse_args()
     wl = WORKLOADS[args.workload]
     world, rank, local = dist_setup(args)
@@ -312,10 +450,32 @@ def main() -> None:
 
     _lib.load()
     dev = f"cuda:{local}" if world > 1 else "cuda:0"
-    weights = make_weights(wl, seed=1234 + rank, device=dev)
+    rows_mode = args.mode == "rows" and world > 1
+    if rows_mode:
+        # one layer, expert-major rows split over the ranks (row-sharded k-means)
+        from skcq_b200 import distributed
+
+        full = make_weights(wl, seed=1234, device=dev)
+        weights = {}
+        for name, rows, _ in projections(wl):
+            r0, r1 = distributed.expert_row_range(wl["experts"], rows // wl["experts"], world, rank)
+            weights[name] = full[name][r0:r1].contiguous()
+        del full
+        shard_ctx = distributed.row_sharded
+    else:
+        weights = make_weights(wl, seed=1234 + rank, device=dev)
+        shard_ctx = None
+
+    def step(ws, **kw):
+        if shard_ctx is None:
+            return build_step(wl, ws, **kw)
+        with shard_ctx():
+            torch.manual_seed(99)  # identical Forgy draws on every rank
+            return build_step(wl, ws, **kw)
+
     torch.cuda.synchronize()
     for _ in range(args.warmup):
-        build_step(wl, weights)
+        step(weights)
     torch.cuda.synchronize()
     barrier(world)
 
@@ -331,7 +491,7 @@ def main() -> None:
         barrier(world)
         start.record()
         for _ in range(args.steps):
-            n, _ = build_step(wl, weights)
+            n, _ = step(weights)
             block_iters += n
         end.record()
         torch.cuda.synchronize()
@@ -339,13 +499,15 @@ def main() -> None:
     _lib.LAUNCHES.enabled = False
     _engine.TIMER.enabled = False
     ms = max_over_ranks(start.elapsed_time(end), world)
-    total_block_iters = sum_over_ranks(block_iters, world)
+    # row-sharded ranks share each problem: count it once
+    total_block_iters = block_iters if rows_mode else sum_over_ranks(block_iters, world)
     value = total_block_iters / (ms / 1e3) / 1e6
     launches = _lib.LAUNCHES.kernels
     ksum = _engine.TIMER.summary()
 
     # ---- end to end through the public API with host buffers --------------
     e2e = None
+    fits: dict = {}
     if not args.no_e2e:
         host = {k: v.cpu().pin_memory() for k, v in weights.items()}
         del weights
@@ -358,17 +520,23 @@ def main() -> None:
         d2h = 0
         for _ in range(args.steps):
             dev_w = {k: v.to(dev, non_blocking=True) for k, v in host.items()}
-            n, errs = build_step(wl, dev_w, rel_err=True)
+            fits.clear()
+            n, errs = step(dev_w, rel_err=True, keep=fits)
             vals = torch.stack(errs).cpu()
             d2h += vals.numel() * vals.element_size()
             bi += n
             del dev_w
         torch.cuda.synchronize()
         e2e_s = max_over_ranks(time.perf_counter() - t0, world)
-        e2e = {"value": sum_over_ranks(bi, world) / e2e_s / 1e6, "unit": UNIT, "h2d_bytes_per_step": h2d,
+        e2e = {"value": (bi if rows_mode else sum_over_ranks(bi, world)) / e2e_s / 1e6, "unit": UNIT,
+               "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h // max(args.steps, 1), "rel_fro_err": [float(x) for x in vals]}
 
     peaks, peak_kind = measured_peaks()
+    fwd = None
+    if not args.no_forward and not args.no_e2e and fits and not rows_mode:
+        fwd = forward_bench(wl, fits, dev, peaks)
+        fits.clear()
     a = ksum.get("assign", {"ms": 0.0, "work": 0.0, "launches": 0, "padded": 0.0})
     achieved = a["work"] / (a["ms"] / 1e3) / 1e12 if a["ms"] > 0 else 0.0
     issued = a["padded"] / (a["ms"] / 1e3) / 1e12 if a["ms"] > 0 else 0.0
@@ -384,16 +552,19 @@ def main() -> None:
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "strong" if rows_mode else "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": args.workload, "experts": wl["experts"], "hidden": wl["hidden"],
                        "intermediate": wl["inter"], "primary": list(wl["prim"]),
                        "residuals": [list(r) for r in wl["res"]], "iters": wl["iters"],
                        "codebook_bits": wl["bits"], "step": "AQLM build of gate, up and down",
                        "l2": "inputs larger than L2 (bf16 weights 1.2 GB per layer; split operands > 3 GB)",
-                       "parallelism": f"layer farm x{world}"},
+                       "parallelism": f"row-sharded k-means x{world} (NCCL all-reduce of sums/counts)"
+                       if rows_mode else f"layer farm x{world}"},
             "block_iters_per_step": total_block_iters / args.steps,
             "roofline": roofline, "clocks": clocks.summary(), "gpu_launches": launches, "e2e": e2e,
+            "forward": fwd,
         }
         if not args.no_cpu and world == 1:
             line["cpu_baseline"] = {k: v for k, v in cpu_rate(wl).items() if k != "est_layer_s"}

@@ -329,6 +329,42 @@ int skcq_swiglu(const float* gate, const float* up, int n_split, int64_t n, floa
 int skcq_combine(const float* part, int n_split, int64_t P, const int32_t* row_of_pair, const int64_t* topk,
                  const void* weights, int w_dtype, int T, int k, int H, void* out, int out_dtype, void* stream);
 
+/* ---- prefill forward on the tensor cores ------------------------------------
+ * For large batches (many rows per expert) the active experts' weights are
+ * decoded once into bf16 and multiplied on tcgen05 (kind::f16, fp32
+ * accumulate). Operands live in the tcgen05 shared-memory image: A chunks of
+ * 128 rows x 64 k (16 KB), W chunks of 256 outputs x 64 k (32 KB), K padded to
+ * a multiple of 64 with zeros. KC = ceil(in_dim / 64), NT = ceil(out / 256).
+ * Row tiles: 128 consecutive sorted rows of one expert. */
+
+/* tiles[0] = number of row tiles; tile t = (row0, row1, slot) at
+ * tiles[1 + 3t ..], slot = the expert's index in the active list of
+ * skcq_route_sort. tiles holds 1 + 3 * max_tiles ints; max_tiles >=
+ * ceil(rows / 128) + active experts. */
+int skcq_prefill_plan(const int32_t* seg, int n_experts, int max_tiles, int32_t* tiles, void* stream);
+
+/* A[t][kc] (max_tiles * KC * 16 KB, 16-byte aligned): mode 0, row r of tile t
+ * is x[row_token[r] % T] (x[r] when row_token is NULL; x f32 | bf16); mode 1,
+ * it is silu(x[r]) * up[r] (x and up f32: the SwiGLU of gate and up outputs).
+ * Rows past a tile's end are zero. */
+int skcq_prefill_pack(int mode, const void* x, int x_dtype, int64_t x_ld, const int32_t* row_token, int T,
+                      const float* up, int64_t up_ld, int in_dim, const int32_t* tiles, int max_tiles, void* A,
+                      void* stream);
+
+/* W[slot][nt][kc] (max_slots * NT * KC * 32 KB, 16-byte aligned) for the
+ * experts active[1 + slot] (slot < active[0]; expert = slot when active is
+ * NULL): bf16 of sum over layers of (primary scale) * sign * centroid values
+ * plus raw remainder columns, i.e. the module's dense expert weight
+ * (codebook_experts.py:48-56, :325-339). col_group: a multiple of 8 and of
+ * every layer's block size, one of 8, 16, 24, 32, 48, 64. */
+int skcq_prefill_dequant(const skcq_fwd_layer* layers, int n_layers, const int32_t* active, int max_slots,
+                         int out_dim, int in_dim, int col_group, void* W, void* stream);
+
+/* y[r][o] = sum_k A[r][k] * W_slot(r)[o][k] for the rows of every planned
+ * tile (f32 out, row stride y_ld; rows outside tiles untouched). */
+int skcq_prefill_gemm(const void* A, const void* W, const int32_t* tiles, int max_tiles, int in_dim, int out_dim,
+                      float* y, int64_t y_ld, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -11,6 +11,7 @@ reference's expert order.
 
 from __future__ import annotations
 
+import math
 from collections.abc import Callable
 from typing import Any, Literal
 
@@ -340,6 +341,31 @@ class CodebookModule(nn.Module):
              x.shape[1], self.out_dim, S, ptr(part), P, stream())
         return part, S
 
+    def col_group(self) -> int | None:
+        """Columns one dequant thread decodes: lcm(8, block sizes), if the
+        prefill decoder supports it."""
+        g = 8
+        for layer in self.layers:
+            g = g * layer.block_size // math.gcd(g, layer.block_size)
+        return g if g in (8, 16, 24, 32, 48, 64) and all(la.block_size <= 32 for la in self.layers) else None
+
+    def prefill(self, A: torch.Tensor, tiles: torch.Tensor, max_tiles: int, active: torch.Tensor | None,
+                max_slots: int, n_rows: int, in_dim: int) -> torch.Tensor:
+        """Tensor-core forward of packed rows ``A`` (skcq_prefill_pack layout):
+        decode the active experts' weights once, then one grouped GEMM.
+        Returns (n_rows, out_dim) f32."""
+        dev = A.device
+        descs = [layer.descriptor(dev, primary=(i == 0)) for i, layer in enumerate(self.layers)]
+        arr = (FwdLayer * len(descs))(*descs)
+        KC, NT = -(-in_dim // 64), -(-self.out_dim // 256)
+        W = torch.empty(max_slots * NT * KC * 16384, dtype=torch.bfloat16, device=dev)
+        call("skcq_prefill_dequant", _lib.C.cast(arr, _lib.C.c_void_p), len(descs), ptr(active), max_slots,
+             self.out_dim, in_dim, self.col_group(), ptr(W), stream())
+        y = torch.empty(n_rows, self.out_dim, dtype=torch.float32, device=dev)
+        call("skcq_prefill_gemm", ptr(A), ptr(W), ptr(tiles), max_tiles, in_dim, self.out_dim, ptr(y), y.stride(0),
+             stream())
+        return y
+
     def forward(self, hidden_states: torch.Tensor, expert_idx: int) -> torch.Tensor:
         """codebook_experts.py:325-339 for one expert; output in the input dtype
         on the input's device."""
@@ -412,6 +438,9 @@ class CodebookExperts(nn.Module):
     ``[0, num_experts)`` raises like the reference's ``one_hot``."""
 
     check_errors: bool = True
+    # bf16 batches with at least this many (token, slot) rows per expert on
+    # average take the tensor-core prefill path
+    prefill_min_rows: int = 32
 
     def __init__(self, gate: CodebookModule, up: CodebookModule, down: CodebookModule, num_experts: int,
                  act_fn: Callable[[torch.Tensor], torch.Tensor]) -> None:
@@ -443,6 +472,11 @@ class CodebookExperts(nn.Module):
         call("skcq_route_sort", ptr(topk), T, k, E, ptr(perm), ptr(seg), ptr(inv), ptr(active), stream())
         max_active = min(E, P)
         I = self.gate.out_dim
+        if self._use_prefill(h, P, max_active):
+            out = self._forward_prefill(h, topk, w, perm, seg, inv, active, T, k, E, P, max_active)
+            if self.check_errors:
+                _lib.poll_device_error()
+            return out.to(device=hidden_states.device, dtype=hidden_states.dtype)
         S = _choose_splits(max_active, I, min(self.gate.min_blocks, self.up.min_blocks), P)
         seg_kw = {"active": active, "max_active": max_active, "n_rows": P}
         g, _ = self.gate.run_segments(h, seg, None, E, row_token=perm, T=T, n_split=S, **seg_kw)
@@ -460,3 +494,41 @@ class CodebookExperts(nn.Module):
         if self.check_errors:
             _lib.poll_device_error()
         return out.to(device=hidden_states.device, dtype=hidden_states.dtype)
+
+    def _use_prefill(self, h: torch.Tensor, P: int, max_active: int) -> bool:
+        mods = (self.gate, self.up, self.down)
+        return (h.dtype == torch.bfloat16 and P >= self.prefill_min_rows * max(1, max_active)
+                and all(m.col_group() is not None for m in mods)
+                and all(la.codebook.dtype == torch.bfloat16 for m in mods for la in m.layers))
+
+    def _forward_prefill(self, h, topk, w, perm, seg, inv, active, T, k, E, P, max_active) -> torch.Tensor:
+        """Tensor-core path: plan 128-row tiles per expert, pack the routed
+        rows once for gate and up, decode each projection's active experts and
+        run the grouped tcgen05 GEMM; SwiGLU is fused into packing the down
+        projection's rows."""
+        dev = h.device
+        H = h.shape[1]
+        I = self.gate.out_dim
+        max_tiles = -(-P // 128) + max_active
+        tiles = torch.empty(1 + 3 * max_tiles, dtype=torch.int32, device=dev)
+        call("skcq_prefill_plan", ptr(seg), E, max_tiles, ptr(tiles), stream())
+        A = torch.empty(max_tiles * (-(-H // 64)) * 8192, dtype=torch.bfloat16, device=dev)
+        call("skcq_prefill_pack", 0, ptr(h), _DTYPE[h.dtype], h.stride(0), ptr(perm), T, None, 0, H, ptr(tiles),
+             max_tiles, ptr(A), stream())
+        g = self.gate.prefill(A, tiles, max_tiles, active, max_active, P, H)
+        u = self.up.prefill(A, tiles, max_tiles, active, max_active, P, H)
+        del A
+        A2 = torch.empty(max_tiles * (-(-I // 64)) * 8192, dtype=torch.bfloat16, device=dev)
+        if _is_silu(self.intermediate.act_fn):
+            call("skcq_prefill_pack", 1, ptr(g), _DTYPE[torch.float32], g.stride(0), None, 0, ptr(u), u.stride(0), I,
+                 ptr(tiles), max_tiles, ptr(A2), stream())
+        else:
+            inter = self.intermediate(g, u).float().contiguous()
+            call("skcq_prefill_pack", 0, ptr(inter), _DTYPE[torch.float32], inter.stride(0), None, 0, None, 0, I,
+                 ptr(tiles), max_tiles, ptr(A2), stream())
+        del g, u
+        d = self.down.prefill(A2, tiles, max_tiles, active, max_active, P, I)
+        out = torch.empty(T, H, dtype=h.dtype, device=dev)
+        call("skcq_combine", ptr(d), 1, P, ptr(inv), ptr(topk), ptr(w), _DTYPE[w.dtype], T, k, H, ptr(out),
+             _DTYPE[out.dtype], stream())
+        return out

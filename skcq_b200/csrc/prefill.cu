@@ -1,0 +1,480 @@
+// Prefill forward of the codebook experts on the 5th-generation tensor cores
+// (skcq/codebook_experts.py:30-61 gather_matmul mode, batched over experts).
+//
+// For large batches every active expert's weight is needed by many rows, so
+// the weight is decoded once per forward instead of once per row:
+//   1. plan:    128-row tiles of each expert's run of sorted (token, slot) rows;
+//   2. pack:    the rows, gathered by token (or SwiGLU of gate/up), as bf16 in
+//               the tcgen05 no-swizzle K-major shared-memory image, one
+//               16 KB chunk (128 rows x 64 k) after another;
+//   3. dequant: each active expert's W[out][in] = sum over codebooks of
+//               scale * sign * C_b[idx] (+ raw remainder columns), bf16, in the
+//               same image layout, 32 KB chunks of 256 outputs x 64 k;
+//   4. gemm:    one CTA per (row tile, 256-output tile): a producer warp
+//               streams A and B chunks with 1-D bulk copies into a 4-stage
+//               ring, one thread issues tcgen05.mma kind::f16 (M=128, N=256,
+//               K=16 per instruction) into a TMEM accumulator, four warps read
+//               it back with tcgen05.ld and store fp32 rows.
+// Because the packer and the decoder write the exact shared-memory image, no
+// tensor map is needed: each stage is two contiguous bulk copies.
+#include <cuda_bf16.h>
+
+#include "common.cuh"
+#include "fwd_common.cuh"
+
+namespace skcq {
+
+constexpr int PF_BM = 128;
+constexpr int PF_BN = 256;
+constexpr int PF_BK = 64;
+constexpr int PF_STAGES = 4;
+constexpr uint32_t PF_A_BYTES = PF_BM * PF_BK * 2;  // 16 KB
+constexpr uint32_t PF_B_BYTES = PF_BN * PF_BK * 2;  // 32 KB
+constexpr int PF_THREADS = 192;                     // producer, MMA, 4 epilogue warps
+constexpr size_t PF_SMEM = (size_t)PF_STAGES * (PF_A_BYTES + PF_B_BYTES) + 2048;  // + alignment pad and barriers
+
+// Instruction descriptor: kind::f16 with bf16 A and B (K-major), f32 D, M x N.
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// 16-byte unit index of (row r, k-group kg) in a rows x 64 chunk: core matrices
+// of 8 rows x 8 bf16, K-adjacent ones 128 B apart, 8-row groups 1 KB apart.
+__device__ __forceinline__ int canon_unit(int r, int kg) { return ((r >> 3) * 8 + kg) * 8 + (r & 7); }
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// ---------------------------------------------------------------------------
+// 1. plan: tiles[0] = n_tiles; tile t at tiles[1 + 3t ..]: (row0, row1, slot)
+// ---------------------------------------------------------------------------
+__global__ void prefill_plan_kernel(const int32_t* __restrict__ seg, int E, int max_tiles, int32_t* __restrict__ tiles,
+                                    int* err) {
+  __shared__ int s_base, s_sbase;
+  if (threadIdx.x == 0) {
+    s_base = 0;
+    s_sbase = 0;
+  }
+  __syncthreads();
+  for (int e0 = 0; e0 < E; e0 += 1024) {
+    const int e = e0 + threadIdx.x;
+    const int cnt = e < E ? seg[e + 1] - seg[e] : 0;
+    int tot, stot;
+    const int nt = (cnt + PF_BM - 1) / PF_BM;
+    const int off = block_exclusive_scan(nt, &tot);
+    const int soff = block_exclusive_scan(cnt > 0 ? 1 : 0, &stot);
+    const int base = s_base + off, sbase = s_sbase + soff;
+    if (e < E) {
+      for (int t = 0; t < nt; ++t) {
+        const int id = base + t;
+        if (id >= max_tiles) {
+          atomicCAS(err, 0, 44);
+          break;
+        }
+        tiles[1 + 3 * id] = seg[e] + t * PF_BM;
+        tiles[2 + 3 * id] = min(seg[e] + (t + 1) * PF_BM, seg[e + 1]);
+        tiles[3 + 3 * id] = sbase;
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      s_base += tot;
+      s_sbase += stot;
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) tiles[0] = min(s_base, max_tiles);
+}
+
+// ---------------------------------------------------------------------------
+// 2. pack rows: A[t][kc] chunks (128 x 64 bf16 image)
+// mode 0: row r reads x[row_token[r] % T] (f32 | bf16); mode 1: silu(g[r]) * u[r]
+// ---------------------------------------------------------------------------
+__global__ void prefill_pack_kernel(int mode, const void* __restrict__ x, int x_dtype, int64_t x_ld,
+                                    const int32_t* __restrict__ row_token, int T, const float* __restrict__ u,
+                                    int64_t u_ld, int in_dim, int KC, const int32_t* __restrict__ tiles,
+                                    int max_tiles, uint4* __restrict__ A) {
+  const int n_tiles = tiles[0];
+  const int64_t units = (int64_t)max_tiles * KC * 1024;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < units; i += (int64_t)gridDim.x * blockDim.x) {
+    const int t = (int)(i / ((int64_t)KC * 1024));
+    if (t >= n_tiles) break;  // tiles are outermost: the rest of this thread's units are past n_tiles too
+    const int rem = (int)(i - (int64_t)t * KC * 1024);
+    const int kc = rem >> 10, unit = rem & 1023;
+    const int rg = unit >> 6, kg = (unit >> 3) & 7, r = rg * 8 + (unit & 7);
+    const int row = tiles[1 + 3 * t] + r, row1 = tiles[2 + 3 * t];
+    const int k0 = kc * PF_BK + kg * 8;
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = 0.f;
+    if (row < row1) {
+      if (mode == 0) {
+        const int64_t tok = row_token ? (int64_t)(row_token[row] % T) : (int64_t)row;
+        if (x_dtype == SKCQ_DTYPE_BF16) {
+          const uint16_t* p = static_cast<const uint16_t*>(x) + tok * x_ld + k0;
+          if (k0 + 8 <= in_dim && ((reinterpret_cast<uintptr_t>(p) & 15) == 0)) {
+            const uint4 q = *reinterpret_cast<const uint4*>(p);
+            A[i] = q;
+            continue;
+          }
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            if (k0 + j < in_dim) v[j] = __uint_as_float((uint32_t)p[j] << 16);
+        } else {
+          const float* p = static_cast<const float*>(x) + tok * x_ld + k0;
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            if (k0 + j < in_dim) v[j] = p[j];
+        }
+      } else {
+        const float* g = static_cast<const float*>(x) + (int64_t)row * x_ld + k0;
+        const float* uu = u + (int64_t)row * u_ld + k0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (k0 + j < in_dim) {
+            const float a = g[j];
+            v[j] = __fdiv_rn(a, 1.0f + expf(-a)) * uu[j];
+          }
+      }
+    }
+    A[i] = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
+                      pack_bf16x2(v[6], v[7]));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// 3. dequant: W[slot][nt][kc] chunks (256 x 64 bf16 image) of active experts
+// ---------------------------------------------------------------------------
+struct DqSet {
+  skcq_fwd_layer l[SKCQ_MAX_CODECS];
+  int n;
+};
+
+// acc[0..CW) += the layer's contribution to columns [c0, c0 + CW) of row o.
+template <int BS, int CW, typename T>
+__device__ __forceinline__ void dq_layer(const skcq_fwd_layer& L, bool primary, int e, int o, int out, int c0,
+                                         float (&acc)[CW]) {
+  const int nb = L.n_blocks;
+  const int cov = nb * BS;
+#pragma unroll
+  for (int bb = 0; bb < CW / BS; ++bb) {
+    const int b = c0 / BS + bb;
+    if (b < nb) {
+      const int64_t eb = ((int64_t)e * nb + b) * out + o;
+      const int idx = __ldg(L.idx16 + eb);
+      float w[BS];
+      load_centroid<BS, T>(static_cast<const T*>(L.table) + ((int64_t)b * L.K + idx) * BS, w);
+      const uint32_t m = L.sign_mask ? __ldg(L.sign_mask + eb) : 0u;
+      const float sc = (primary && L.scales) ? ld_scale(L.scales, eb, L.scale_dtype, L.q_scale) : 1.f;
+#pragma unroll
+      for (int j = 0; j < BS; ++j) {
+        const float v = (m >> j & 1u) ? -w[j] : w[j];
+        acc[bb * BS + j] = (primary && L.scales) ? __fmaf_rn(v, sc, acc[bb * BS + j]) : acc[bb * BS + j] + v;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < BS; ++j) {
+        const int col = c0 + bb * BS + j - cov;
+        if (col >= 0 && col < L.rem) acc[bb * BS + j] += ld_any(L.remainder, ((int64_t)e * out + o) * L.rem + col,
+                                                               L.rem_dtype);
+      }
+    }
+  }
+}
+
+template <int CW, typename T>
+__device__ __forceinline__ void dq_layer_any(const skcq_fwd_layer& L, bool primary, int e, int o, int out, int c0,
+                                             float (&acc)[CW]) {
+  switch (L.bs) {
+    case 4: if constexpr (CW % 4 == 0) { dq_layer<4, CW, T>(L, primary, e, o, out, c0, acc); return; } break;
+    case 6: if constexpr (CW % 6 == 0) { dq_layer<6, CW, T>(L, primary, e, o, out, c0, acc); return; } break;
+    case 8: if constexpr (CW % 8 == 0) { dq_layer<8, CW, T>(L, primary, e, o, out, c0, acc); return; } break;
+    case 12: if constexpr (CW % 12 == 0) { dq_layer<12, CW, T>(L, primary, e, o, out, c0, acc); return; } break;
+    case 16: if constexpr (CW % 16 == 0) { dq_layer<16, CW, T>(L, primary, e, o, out, c0, acc); return; } break;
+    default: break;
+  }
+  // any other block size dividing CW: element by element
+  const int nb = L.n_blocks, bs = L.bs, cov = nb * bs;
+  const T* table = static_cast<const T*>(L.table);
+#pragma unroll
+  for (int j = 0; j < CW; ++j) {
+    const int c = c0 + j, b = c / bs;
+    if (b < nb) {
+      const int64_t eb = ((int64_t)e * nb + b) * out + o;
+      const int idx = L.idx16[eb];
+      const int jj = c - b * bs;
+      float v;
+      if constexpr (sizeof(T) == 4)
+        v = reinterpret_cast<const float*>(table)[((int64_t)b * L.K + idx) * bs + jj];
+      else
+        v = __uint_as_float((uint32_t) reinterpret_cast<const uint16_t*>(table)[((int64_t)b * L.K + idx) * bs + jj]
+                            << 16);
+      if (L.sign_mask && (L.sign_mask[eb] >> jj & 1u)) v = -v;
+      acc[j] = (primary && L.scales) ? __fmaf_rn(v, ld_scale(L.scales, eb, L.scale_dtype, L.q_scale), acc[j])
+                                     : acc[j] + v;
+    } else if (c - cov < L.rem) {
+      acc[j] += ld_any(L.remainder, ((int64_t)e * out + o) * L.rem + (c - cov), L.rem_dtype);
+    }
+  }
+}
+
+// thread = (slot, column group, output o), o fastest
+template <int CW>
+__global__ void prefill_dequant_kernel(DqSet set, const int32_t* __restrict__ active, int max_slots, int out,
+                                       int in_dim, int NT, int KC, uint4* __restrict__ W) {
+  const int n_slots = active ? active[0] : max_slots;
+  const int groups = (KC * PF_BK + CW - 1) / CW;
+  const int64_t total = (int64_t)max_slots * groups * out;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int o = (int)(i % out);
+    const int64_t sg = i / out;
+    const int g = (int)(sg % groups), slot = (int)(sg / groups);
+    if (slot >= n_slots) break;  // slots are outermost
+    const int e = active ? active[1 + slot] : slot;
+    const int c0 = g * CW;
+    float acc[CW];
+#pragma unroll
+    for (int j = 0; j < CW; ++j) acc[j] = 0.f;
+    if (c0 < in_dim) {
+      for (int li = 0; li < set.n; ++li) {
+        const skcq_fwd_layer& L = set.l[li];
+        if (L.table_dtype == SKCQ_DTYPE_BF16)
+          dq_layer_any<CW, __nv_bfloat16>(L, li == 0, e, o, out, c0, acc);
+        else
+          dq_layer_any<CW, float>(L, li == 0, e, o, out, c0, acc);
+      }
+#pragma unroll
+      for (int j = 0; j < CW; ++j)
+        if (c0 + j >= in_dim) acc[j] = 0.f;
+    }
+    const int nt = o / PF_BN, rr = o % PF_BN;
+    uint4* chunk0 = W + (((int64_t)slot * NT + nt) * KC) * (PF_B_BYTES / 16);
+#pragma unroll
+    for (int q = 0; q < CW / 8; ++q) {
+      const int c = c0 + q * 8;
+      if (c >= KC * PF_BK) break;  // a group may run past the padded width (CW not dividing 64)
+      const int kc = c / PF_BK, kg = (c % PF_BK) / 8;
+      chunk0[(int64_t)kc * (PF_B_BYTES / 16) + canon_unit(rr, kg)] =
+          make_uint4(pack_bf16x2(acc[q * 8], acc[q * 8 + 1]), pack_bf16x2(acc[q * 8 + 2], acc[q * 8 + 3]),
+                     pack_bf16x2(acc[q * 8 + 4], acc[q * 8 + 5]), pack_bf16x2(acc[q * 8 + 6], acc[q * 8 + 7]));
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// 4. grouped GEMM on tcgen05
+// ---------------------------------------------------------------------------
+struct GemmArgs {
+  const uint8_t* A;  // [max_tiles][KC] 16 KB chunks
+  const uint8_t* W;  // [slots][NT][KC] 32 KB chunks
+  const int32_t* tiles;
+  int KC, NT, out;
+  float* y;
+  int64_t y_ld;
+  int* err;
+};
+
+__global__ void __launch_bounds__(PF_THREADS, 1) prefill_gemm_kernel(GemmArgs g) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  const int t = blockIdx.x, nt = blockIdx.y;
+  if (t >= g.tiles[0]) return;
+  const int row0 = g.tiles[1 + 3 * t], row1 = g.tiles[2 + 3 * t], slot = g.tiles[3 + 3 * t];
+  uint8_t* base = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  uint8_t* sa = base;
+  uint8_t* sb = base + PF_STAGES * PF_A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sb + PF_STAGES * PF_B_BYTES);
+  uint64_t* empty = full + PF_STAGES;
+  uint64_t* acc_full = empty + PF_STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < PF_STAGES; ++i) {
+      mbar_init(full + i, 1);
+      mbar_init(empty + i, 1);
+    }
+    mbar_init(acc_full, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, PF_BN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int KC = g.KC;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint8_t* a_src = g.A + (size_t)t * KC * PF_A_BYTES;
+      const uint8_t* b_src = g.W + ((size_t)slot * g.NT + nt) * KC * PF_B_BYTES;
+      for (int kc = 0; kc < KC; ++kc) {
+        const int s = kc % PF_STAGES;
+        if (kc >= PF_STAGES && !mbar_wait(empty + s, ((kc / PF_STAGES) - 1) & 1, g.err, 51)) break;
+        mbar_arrive_expect_tx(full + s, PF_A_BYTES + PF_B_BYTES);
+        bulk_g2s(sa + s * PF_A_BYTES, a_src + (size_t)kc * PF_A_BYTES, PF_A_BYTES, full + s);
+        bulk_g2s(sb + s * PF_B_BYTES, b_src + (size_t)kc * PF_B_BYTES, PF_B_BYTES, full + s);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16(PF_BM, PF_BN);
+      bool ok = true;
+      for (int kc = 0; kc < KC; ++kc) {
+        const int s = kc % PF_STAGES;
+        if (!mbar_wait(full + s, (kc / PF_STAGES) & 1, g.err, 52)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a0 = smem_u32(sa + s * PF_A_BYTES), b0 = smem_u32(sb + s * PF_B_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < PF_BK / 16; ++kk)
+          mma_bf16(tmem, smem_desc(a0 + kk * 256, 128, 1024), smem_desc(b0 + kk * 256, 128, 1024), idesc,
+                   (kc | kk) != 0 ? 1u : 0u);
+        tc_commit(empty + s);
+      }
+      if (ok) tc_commit(acc_full);
+    }
+  } else {
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    if (mbar_wait(acc_full, 0, g.err, 53)) {
+      tc_fence_after();
+      const int r = q * 32 + lane;
+      const int row = row0 + r;
+      float* yr = g.y + (int64_t)row * g.y_ld + (int64_t)nt * PF_BN;
+      const int ncol = min(PF_BN, g.out - nt * PF_BN);
+      for (int j = 0; j < PF_BN / 32; ++j) {
+        float v[32];
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + j * 32, v);
+        tmem_wait_ld();
+        if (row < row1) {
+          if (j * 32 + 32 <= ncol && (g.y_ld & 3) == 0) {
+#pragma unroll
+            for (int c = 0; c < 32; c += 4)
+              *reinterpret_cast<float4*>(yr + j * 32 + c) = make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]);
+          } else {
+            for (int c = 0; c < 32; ++c)
+              if (j * 32 + c < ncol) yr[j * 32 + c] = v[c];
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, PF_BN);
+  }
+}
+
+}  // namespace skcq
+
+using namespace skcq;
+
+extern "C" int skcq_prefill_plan(const int32_t* seg, int n_experts, int max_tiles, int32_t* tiles, void* stream) {
+  SKCQ_REQUIRE(seg && tiles, SKCQ_ERR_INVALID, "prefill_plan: null pointer");
+  SKCQ_REQUIRE(n_experts > 0 && max_tiles > 0, SKCQ_ERR_INVALID, "prefill_plan: %d experts, %d tiles", n_experts,
+               max_tiles);
+  int* err = device_error_word();
+  SKCQ_REQUIRE(err != nullptr, SKCQ_ERR_CUDA, "prefill_plan: no device error word");
+  prefill_plan_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(seg, n_experts, max_tiles, tiles, err);
+  return check_launch("prefill_plan");
+}
+
+extern "C" int skcq_prefill_pack(int mode, const void* x, int x_dtype, int64_t x_ld, const int32_t* row_token, int T,
+                                 const float* up, int64_t up_ld, int in_dim, const int32_t* tiles, int max_tiles,
+                                 void* A, void* stream) {
+  SKCQ_REQUIRE(x && tiles && A, SKCQ_ERR_INVALID, "prefill_pack: null pointer");
+  SKCQ_REQUIRE(mode == 0 || (mode == 1 && up), SKCQ_ERR_INVALID, "prefill_pack: mode %d", mode);
+  SKCQ_REQUIRE(mode == 1 || x_dtype == SKCQ_DTYPE_F32 || x_dtype == SKCQ_DTYPE_BF16, SKCQ_ERR_INVALID,
+               "prefill_pack: x dtype %d", x_dtype);
+  SKCQ_REQUIRE(row_token == nullptr || T > 0, SKCQ_ERR_INVALID, "prefill_pack: token map without tokens");
+  SKCQ_REQUIRE(in_dim > 0 && max_tiles > 0 && ((uintptr_t)A & 15) == 0, SKCQ_ERR_INVALID, "prefill_pack: bad sizes");
+  const int KC = ceil_div(in_dim, PF_BK);
+  const int64_t units = (int64_t)max_tiles * KC * 1024;
+  int64_t grid = (units + 255) / 256;
+  if (grid > 148 * 64) grid = 148 * 64;
+  prefill_pack_kernel<<<(int)grid, 256, 0, (cudaStream_t)stream>>>(mode, x, mode == 1 ? SKCQ_DTYPE_F32 : x_dtype,
+                                                                    x_ld, row_token, T, up, up_ld, in_dim, KC, tiles,
+                                                                    max_tiles, static_cast<uint4*>(A));
+  return check_launch("prefill_pack");
+}
+
+extern "C" int skcq_prefill_dequant(const skcq_fwd_layer* layers, int n_layers, const int32_t* active, int max_slots,
+                                    int out_dim, int in_dim, int col_group, void* W, void* stream) {
+  SKCQ_REQUIRE(layers && W, SKCQ_ERR_INVALID, "prefill_dequant: null pointer");
+  SKCQ_REQUIRE(n_layers >= 1 && n_layers <= SKCQ_MAX_CODECS, SKCQ_ERR_INVALID, "prefill_dequant: %d layers",
+               n_layers);
+  SKCQ_REQUIRE(((uintptr_t)W & 15) == 0 && out_dim > 0 && in_dim > 0 && max_slots >= 0, SKCQ_ERR_INVALID,
+               "prefill_dequant: bad sizes");
+  DqSet set;
+  set.n = n_layers;
+  for (int i = 0; i < n_layers; ++i) {
+    const skcq_fwd_layer& L = layers[i];
+    SKCQ_REQUIRE(L.table && L.idx16 && L.bs > 0 && L.bs <= 32 && L.K > 0 && col_group % L.bs == 0, SKCQ_ERR_INVALID,
+                 "prefill_dequant: layer %d (bs %d) does not fit column groups of %d", i, L.bs, col_group);
+    SKCQ_REQUIRE(L.table_dtype == SKCQ_DTYPE_F32 || L.table_dtype == SKCQ_DTYPE_BF16, SKCQ_ERR_INVALID,
+                 "prefill_dequant: layer %d table dtype %d", i, L.table_dtype);
+    SKCQ_REQUIRE(L.n_blocks * L.bs + L.rem <= in_dim && (L.rem == 0 || L.remainder), SKCQ_ERR_INVALID,
+                 "prefill_dequant: layer %d coverage", i);
+    set.l[i] = L;
+  }
+  if (max_slots == 0) return SKCQ_OK;
+  const int KC = ceil_div(in_dim, PF_BK), NT = ceil_div(out_dim, PF_BN);
+  SKCQ_REQUIRE(out_dim <= NT * PF_BN, SKCQ_ERR_INVALID, "prefill_dequant: out");
+  cudaStream_t s = (cudaStream_t)stream;
+  // rows of the last 256-output tile past out_dim stay as the caller left them;
+  // they only feed accumulator columns that the GEMM never stores
+  const int64_t total = (int64_t)max_slots * ((KC * PF_BK + col_group - 1) / col_group) * out_dim;
+  int64_t grid = (total + 127) / 128;
+  if (grid > 148 * 64) grid = 148 * 64;
+  uint4* w = static_cast<uint4*>(W);
+  switch (col_group) {
+    case 8: prefill_dequant_kernel<8><<<(int)grid, 128, 0, s>>>(set, active, max_slots, out_dim, in_dim, NT, KC, w); break;
+    case 16: prefill_dequant_kernel<16><<<(int)grid, 128, 0, s>>>(set, active, max_slots, out_dim, in_dim, NT, KC, w); break;
+    case 24: prefill_dequant_kernel<24><<<(int)grid, 128, 0, s>>>(set, active, max_slots, out_dim, in_dim, NT, KC, w); break;
+    case 32: prefill_dequant_kernel<32><<<(int)grid, 128, 0, s>>>(set, active, max_slots, out_dim, in_dim, NT, KC, w); break;
+    case 48: prefill_dequant_kernel<48><<<(int)grid, 128, 0, s>>>(set, active, max_slots, out_dim, in_dim, NT, KC, w); break;
+    case 64: prefill_dequant_kernel<64><<<(int)grid, 128, 0, s>>>(set, active, max_slots, out_dim, in_dim, NT, KC, w); break;
+    default: return set_error(SKCQ_ERR_INVALID, "prefill_dequant: column group %d not in {8, 16, 24, 32, 48, 64}", col_group);
+  }
+  return check_launch("prefill_dequant");
+}
+
+extern "C" int skcq_prefill_gemm(const void* A, const void* W, const int32_t* tiles, int max_tiles, int in_dim,
+                                 int out_dim, float* y, int64_t y_ld, void* stream) {
+  SKCQ_REQUIRE(A && W && tiles && y, SKCQ_ERR_INVALID, "prefill_gemm: null pointer");
+  SKCQ_REQUIRE(((uintptr_t)A & 15) == 0 && ((uintptr_t)W & 15) == 0, SKCQ_ERR_INVALID,
+               "prefill_gemm: operands must be 16-byte aligned");
+  SKCQ_REQUIRE(max_tiles > 0 && in_dim > 0 && out_dim > 0, SKCQ_ERR_INVALID, "prefill_gemm: bad sizes");
+  int* err = device_error_word();
+  SKCQ_REQUIRE(err != nullptr, SKCQ_ERR_CUDA, "prefill_gemm: no device error word");
+  static thread_local int configured_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_dev != dev) {
+    cudaError_t e = cudaFuncSetAttribute(prefill_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PF_SMEM);
+    if (e != cudaSuccess) return set_error(SKCQ_ERR_CUDA, "prefill_gemm: %s", cudaGetErrorString(e));
+    configured_dev = dev;
+  }
+  GemmArgs g{static_cast<const uint8_t*>(A), static_cast<const uint8_t*>(W), tiles, ceil_div(in_dim, PF_BK),
+             ceil_div(out_dim, PF_BN), out_dim, y, y_ld, err};
+  dim3 grid((unsigned)max_tiles, (unsigned)g.NT);
+  prefill_gemm_kernel<<<grid, PF_THREADS, PF_SMEM, (cudaStream_t)stream>>>(g);
+  return check_launch("prefill_gemm");
+}

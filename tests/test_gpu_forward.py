@@ -340,3 +340,94 @@ def test_large_batch_route_sort_order():
             inter = torch.nn.functional.silu(gate(xs, e)) * up(xs, e)
             ref.index_add_(0, tok, down(inter, e) * topw.cuda()[tok, pos, None])
         assert rel_err(y.cpu().numpy(), ref.cpu().numpy()) < 1e-5
+
+
+# ---- tensor-core prefill path --------------------------------------------------
+
+
+def _prefill_case(E, H, I, T, k, specs_gu, specs_d, seed, signs=False):
+    from skcq_b200.codebook_experts import CodebookExperts
+
+    gate = _random_module(E, I, H, specs_gu, seed=seed, dtype=torch.bfloat16)
+    up = _random_module(E, I, H, specs_gu, seed=seed + 1, dtype=torch.bfloat16)
+    down = _random_module(E, H, I, specs_d, seed=seed + 2, dtype=torch.bfloat16)
+    if signs:
+        g = torch.Generator().manual_seed(seed + 3)
+        lay = gate.layers[0]
+        sg = torch.where(torch.rand(E, I, lay.n_blocks * lay.block_size, generator=g) < 0.5, -1, 1).to(torch.int8)
+        lay.register_buffer("signs", sg.cuda())
+        lay.sign_cov = sg.shape[-1]
+    ex = CodebookExperts(gate, up, down, E, torch.nn.functional.silu)
+    gen = torch.Generator().manual_seed(seed + 4)
+    hidden = torch.randn(T, H, generator=gen).to(torch.bfloat16)
+    topi = torch.rand(T, E, generator=gen).argsort(-1)[:, :k]
+    topw = torch.rand(T, k, generator=gen)
+    return ex, hidden.cuda(), topi.cuda(), topw.cuda()
+
+
+@pytest.mark.parametrize("case", ["base", "ragged", "bs12", "signs"])
+def test_prefill_tensor_core_path_matches_gather_path(case):
+    """The tcgen05 prefill path (decode weights once, grouped bf16 GEMM) agrees
+    with the fp32 gather path within bf16 tolerance (max rel 1e-2, cos 0.9999)."""
+    from skcq_b200 import _lib
+
+    cfg = {
+        "base": (8, 256, 128, 512, 2, [(8, 64, True), (16, 64, False), (4, 256, False)], [(8, 64, True), (4, 64, False)]),
+        # in/out not multiples of 64/256, remainder columns, uneven expert load
+        "ragged": (5, 200, 300, 333, 3, [(8, 32, True), (4, 16, False)], [(4, 32, True), (8, 16, False)]),
+        "bs12": (4, 384, 96, 300, 2, [(12, 64, True), (6, 32, False)], [(12, 32, True), (6, 32, False)]),
+        "signs": (6, 128, 64, 256, 2, [(8, 32, True), (16, 32, False)], [(8, 32, True)]),
+    }[case]
+    E, H, I, T, k, sgu, sd = cfg
+    seed = {"base": 101, "ragged": 202, "bs12": 303, "signs": 404}[case]
+    ex, x, topi, topw = _prefill_case(E, H, I, T, k, sgu, sd, seed=seed, signs=(case == "signs"))
+    assert ex._use_prefill(x, T * k, min(E, T * k))
+    _lib.LAUNCHES.reset()
+    _lib.LAUNCHES.enabled = True
+    y_tc = ex(x, topi, topw)
+    _lib.LAUNCHES.enabled = False
+    assert _lib.LAUNCHES.calls.get("skcq_prefill_gemm") == 3
+    ex.prefill_min_rows = 1 << 30
+    _lib.LAUNCHES.reset()
+    _lib.LAUNCHES.enabled = True
+    y_ref = ex(x, topi, topw)
+    _lib.LAUNCHES.enabled = False
+    assert "skcq_prefill_gemm" not in _lib.LAUNCHES.calls
+    a, b = y_tc.double(), y_ref.double()
+    cos = torch.nn.functional.cosine_similarity(a.flatten(), b.flatten(), dim=0).item()
+    assert cos >= 0.9999, cos
+    assert (a - b).abs().max().item() <= 1e-2 * b.abs().max().item(), (a - b).abs().max().item()
+
+
+def test_prefill_gemm_exact_on_bf16_operands():
+    """With bf16-exact weights and inputs the GEMM result equals an fp64
+    matmul of the same operands to fp32 accumulation accuracy."""
+    from skcq_b200 import _lib
+    from skcq_b200._lib import call, ptr, stream
+
+    E, H, I, T, k = 4, 192, 320, 400, 2
+    ex, x, topi, topw = _prefill_case(E, H, I, T, k, [(8, 16, False)], [(8, 16, False)], seed=77)
+    P = T * k
+    route = torch.empty(2 * P + 2 * (E + 1), dtype=torch.int32, device="cuda")
+    perm, inv, seg, active = route[:P], route[P:2 * P], route[2 * P:2 * P + E + 1], route[2 * P + E + 1:]
+    call("skcq_route_sort", ptr(topi.contiguous()), T, k, E, ptr(perm), ptr(seg), ptr(inv), ptr(active), stream())
+    max_tiles = -(-P // 128) + E
+    tiles = torch.empty(1 + 3 * max_tiles, dtype=torch.int32, device="cuda")
+    call("skcq_prefill_plan", ptr(seg), E, max_tiles, ptr(tiles), stream())
+    A = torch.empty(max_tiles * 3 * 8192, dtype=torch.bfloat16, device="cuda")
+    call("skcq_prefill_pack", 0, ptr(x), 1, x.stride(0), ptr(perm), T, None, 0, H, ptr(tiles), max_tiles, ptr(A),
+         stream())
+    y = ex.gate.prefill(A, tiles, max_tiles, active, E, P, H)
+    _lib.poll_device_error()
+    # reference: per row, its token's x (bf16) against the expert's decoded weight rounded to bf16
+    seg_h = seg.cpu().tolist()
+    perm_h = perm.cpu()
+    for e in range(E):
+        r0, r1 = seg_h[e], seg_h[e + 1]
+        if r0 == r1:
+            continue
+        W = _dense_from_module(ex.gate, e).to(torch.bfloat16).double()  # (I, H)
+        xs = x.cpu()[perm_h[r0:r1] % T].double()
+        ref = xs @ W.t()
+        got = y[r0:r1].double().cpu()
+        assert torch.allclose(got, ref, rtol=1e-4, atol=1e-4 * ref.abs().max().item()), e
