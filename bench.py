@@ -135,13 +135,14 @@ def _route(T: int, E: int, k: int, gen: torch.Generator, dev: str, zipf: float |
 def _dense_experts(W: dict, E: int, H: int):
     """Dense bf16 experts of the same weights (W = reconstruct, bf16): tokens
     sorted by expert and one library grouped GEMM per projection (the dense
-    comparator)."""
+    comparator; graph-capturable)."""
 
     def fwd(x, topi, topw):
         T, k = topi.shape
         flat = topi.t().reshape(-1)
         order = torch.sort(flat, stable=True).indices
-        offs = torch.cumsum(torch.bincount(flat, minlength=E), 0).to(torch.int32)
+        counts = torch.zeros(E, dtype=torch.int64, device=x.device).scatter_add_(0, flat, torch.ones_like(flat))
+        offs = torch.cumsum(counts, 0).to(torch.int32)
         tok = order % T
         xs = x[tok]
         g = torch._grouped_mm(xs, W["gate"], offs=offs)
@@ -208,18 +209,37 @@ def forward_bench(wl: dict, fits: dict, dev: str, peaks: dict) -> dict:
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     gen = torch.Generator(device=dev).manual_seed(4321)
     res = {"decode": [], "prefill": None}
+    from skcq_b200.codebook_experts import GraphedExperts
+
     for T in (1, 8, 64):
         x = torch.randn(T, H, generator=gen, device=dev).to(torch.bfloat16)
         topi, topw = _route(T, E, 8, gen, dev)
         y, yd = ex(x, topi, topw).float(), dfwd(x, topi, topw).float()
         cos = torch.nn.functional.cosine_similarity(y.flatten(), yd.flatten(), dim=0).item()
-        ms = _time_ms(lambda: ex(x, topi, topw), 20, flush)
-        md = _time_ms(lambda: dfwd(x, topi, topw), 20, flush)
+        ms_eager = _time_ms(lambda: ex(x, topi, topw), 20, flush)
+        gex = GraphedExperts(ex, T, 8)
+        yg = gex(x, topi, topw).float()
+        graph_exact = bool(torch.equal(yg, y))
+        ms = _time_ms(lambda: gex(x, topi, topw), 20, flush)
+        md_eager = _time_ms(lambda: dfwd(x, topi, topw), 20, flush)
+        try:  # the dense comparator gets the same launch-overhead treatment
+            sx, si, sw = x.clone(), topi.clone(), topw.clone()
+            dfwd(sx, si, sw)
+            torch.cuda.synchronize()
+            dg = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(dg, capture_error_mode="relaxed"):
+                dfwd(sx, si, sw)
+            md = _time_ms(dg.replay, 20, flush)
+            dense_graph = True
+        except Exception:  # noqa: BLE001
+            md, dense_graph = md_eager, False
         nbytes = _decode_bytes(ex, topi)
         n_act = int(torch.unique(topi).numel())
         res["decode"].append({
-            "tokens": T, "active_experts": n_act, "tokens_per_s": T / (ms / 1e3), "ms": ms,
-            "dense_bf16_tokens_per_s": T / (md / 1e3), "dense_ms": md, "cos_vs_dense": cos,
+            "tokens": T, "active_experts": n_act, "tokens_per_s": T / (ms / 1e3), "ms": ms, "ms_eager": ms_eager,
+            "cuda_graph": True, "graph_matches_eager": graph_exact,
+            "dense_bf16_tokens_per_s": T / (md / 1e3), "dense_ms": md, "dense_ms_eager": md_eager,
+            "dense_cuda_graph": dense_graph, "cos_vs_dense": cos,
             "algorithmic_bytes": nbytes, "achieved_gbs": nbytes / (ms / 1e3) / 1e9,
             "frac_hbm": nbytes / (ms / 1e3) / 1e9 / peaks["hbm_gbs"],
             "dense_bytes": n_act * 3 * H * I * 2,

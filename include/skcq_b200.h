@@ -309,11 +309,13 @@ int skcq_route_sort(const int64_t* topk, int T, int k, int n_experts, int32_t* p
  *     sum_layers (scale * <x_b, signs * C_b[idx]>) + x_rem . rem_w (last split).
  * The sum over the n_split slots is the module output (skcq_sum_splits,
  * skcq_swiglu, skcq_combine). max_active bounds the active segments
- * (min(n_seg, rows) is always safe). part holds n_split * P * out_dim floats. */
+ * (min(n_seg, rows) is always safe). rows_hint: expected rows per segment
+ * (performance only; any segment length is computed correctly). part holds
+ * n_split * P * out_dim floats. */
 int skcq_codebook_forward(const skcq_fwd_layer* layers, int n_layers, const void* x, int x_dtype, int64_t x_ld,
                           const int32_t* row_token, int T, const int32_t* seg, const int32_t* seg_expert,
                           const int32_t* active, int n_seg, int max_active, int in_dim, int out_dim, int n_split,
-                          float* part, int64_t P, void* stream);
+                          int rows_hint, float* part, int64_t P, void* stream);
 
 /* y[r][o] = sum over splits of part[split][r][o]; y f32 | bf16 with row stride y_ld. */
 int skcq_sum_splits(const float* part, int n_split, int64_t P, int out_dim, void* y, int y_dtype, int64_t y_ld,
@@ -355,15 +357,25 @@ int skcq_prefill_pack(int mode, const void* x, int x_dtype, int64_t x_ld, const 
  * experts active[1 + slot] (slot < active[0]; expert = slot when active is
  * NULL): bf16 of sum over layers of (primary scale) * sign * centroid values
  * plus raw remainder columns, i.e. the module's dense expert weight
- * (codebook_experts.py:48-56, :325-339). col_group: a multiple of 8 and of
- * every layer's block size, one of 8, 16, 24, 32, 48, 64. */
+ * (codebook_experts.py:48-56, :325-339); block sizes up to 32. half = -1: tiles of
+ * 256 outputs (NT = ceil(out / 256)); half = 0 | 1: tiles of 128 features
+ * (NT = ceil(out / 128)) with this module's rows at [128 half, 128 half + 128)
+ * of each 256-row chunk, so gate (0) and up (1) share one buffer. */
 int skcq_prefill_dequant(const skcq_fwd_layer* layers, int n_layers, const int32_t* active, int max_slots,
-                         int out_dim, int in_dim, int col_group, void* W, void* stream);
+                         int out_dim, int in_dim, int half, void* W, void* stream);
 
 /* y[r][o] = sum_k A[r][k] * W_slot(r)[o][k] for the rows of every planned
  * tile (f32 out, row stride y_ld; rows outside tiles untouched). */
 int skcq_prefill_gemm(const void* A, const void* W, const int32_t* tiles, int max_tiles, int in_dim, int out_dim,
                       float* y, int64_t y_ld, void* stream);
+
+/* Gate and up in one GEMM (W_gate_up from skcq_prefill_dequant with half 0 and
+ * 1): for every planned tile, silu(x W_gate^T) * (x W_up^T) as bf16 rows in
+ * the A image of the down projection (A_out: max_tiles * ceil(inter/64) *
+ * 16 KB), zero past each tile's rows and past inter_dim (the SwiGLU of
+ * codebook_experts.py:427-433 fused into the epilogue). */
+int skcq_prefill_gemm_swiglu(const void* A, const void* W_gate_up, const int32_t* tiles, int max_tiles, int in_dim,
+                             int inter_dim, void* A_out, void* stream);
 
 #ifdef __cplusplus
 }

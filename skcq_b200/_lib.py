@@ -68,7 +68,7 @@ _SIGS: dict[str, list] = {
     "skcq_transpose_codebook": [P, I, I, I, I, P, P],
     "skcq_pack_sign_masks": [P, I, I, L, I, I, P, P],
     "skcq_route_sort": [P, I, I, I, P, P, P, P, P],
-    "skcq_codebook_forward": [P, I, P, I, L, P, I, P, P, P, I, I, I, I, I, P, L, P],
+    "skcq_codebook_forward": [P, I, P, I, L, P, I, P, P, P, I, I, I, I, I, I, P, L, P],
     "skcq_sum_splits": [P, I, L, I, P, I, L, P],
     "skcq_swiglu": [P, P, I, L, P, P],
     "skcq_combine": [P, I, L, P, P, P, I, I, I, I, P, I, P],
@@ -76,6 +76,7 @@ _SIGS: dict[str, list] = {
     "skcq_prefill_pack": [I, P, I, L, P, I, P, L, I, P, I, P, P],
     "skcq_prefill_dequant": [P, I, P, I, I, I, I, P, P],
     "skcq_prefill_gemm": [P, P, P, I, I, I, P, L, P],
+    "skcq_prefill_gemm_swiglu": [P, P, P, I, I, I, P, P],
 }
 _RESTYPES = {"skcq_reseed_scratch_bytes": C.c_size_t}
 
@@ -121,6 +122,7 @@ _KERNELS_PER_CALL = {
     "skcq_refit_scales": 1, "skcq_pack_indices16": 1, "skcq_transpose_codebook": 1, "skcq_pack_sign_masks": 1,
     "skcq_route_sort": 1, "skcq_sum_splits": 1, "skcq_swiglu": 1, "skcq_combine": 1,
     "skcq_prefill_plan": 1, "skcq_prefill_pack": 1, "skcq_prefill_dequant": 1, "skcq_prefill_gemm": 1,
+    "skcq_prefill_gemm_swiglu": 1,
 }
 
 

@@ -11,7 +11,6 @@ reference's expert order.
 
 from __future__ import annotations
 
-import math
 from collections.abc import Callable
 from typing import Any, Literal
 
@@ -201,8 +200,8 @@ def _as_rows(x: torch.Tensor) -> torch.Tensor:
     return x
 
 
-# CTAs the split-K decode aims for (4 per SM on 148 SMs)
-_TARGET_CTAS = 4 * 148
+# CTAs the split-K decode aims for (8 per SM on 148 SMs)
+_TARGET_CTAS = 8 * 148
 _MAX_SPLITS = 64
 
 
@@ -321,7 +320,8 @@ class CodebookModule(nn.Module):
     def run_segments(self, x: torch.Tensor, seg: torch.Tensor, seg_expert: torch.Tensor | None,
                      n_seg: int, *, row_token: torch.Tensor | None = None, T: int = 0,
                      active: torch.Tensor | None = None, max_active: int | None = None,
-                     n_rows: int | None = None, n_split: int | None = None) -> tuple[torch.Tensor, int]:
+                     n_rows: int | None = None, n_split: int | None = None,
+                     rows_hint: int | None = None) -> tuple[torch.Tensor, int]:
         """Grouped forward over expert segments of rows (device tensors).
 
         Row r of segment s (expert ``seg_expert[s]``, or s) reads
@@ -336,18 +336,21 @@ class CodebookModule(nn.Module):
         descs = [layer.descriptor(dev, primary=(i == 0)) for i, layer in enumerate(self.layers)]
         arr = (FwdLayer * len(descs))(*descs)
         part = torch.empty(S, P, self.out_dim, dtype=torch.float32, device=dev)
+        hint = rows_hint if rows_hint is not None else -(-P // max(1, max_active))
         call("skcq_codebook_forward", _lib.C.cast(arr, _lib.C.c_void_p), len(descs), ptr(x), _DTYPE[x.dtype],
              x.stride(0), ptr(row_token), T, ptr(seg), ptr(seg_expert), ptr(active), n_seg, max_active,
-             x.shape[1], self.out_dim, S, ptr(part), P, stream())
+             x.shape[1], self.out_dim, S, hint, ptr(part), P, stream())
         return part, S
 
-    def col_group(self) -> int | None:
-        """Columns one dequant thread decodes: lcm(8, block sizes), if the
-        prefill decoder supports it."""
-        g = 8
-        for layer in self.layers:
-            g = g * layer.block_size // math.gcd(g, layer.block_size)
-        return g if g in (8, 16, 24, 32, 48, 64) and all(la.block_size <= 32 for la in self.layers) else None
+    def dequant_into(self, W: torch.Tensor, active: torch.Tensor | None, max_slots: int, in_dim: int,
+                     half: int = -1) -> None:
+        """Decode the active experts' dense weights into ``W`` (the tcgen05
+        operand image of skcq_prefill_dequant)."""
+        dev = W.device
+        descs = [layer.descriptor(dev, primary=(i == 0)) for i, layer in enumerate(self.layers)]
+        arr = (FwdLayer * len(descs))(*descs)
+        call("skcq_prefill_dequant", _lib.C.cast(arr, _lib.C.c_void_p), len(descs), ptr(active), max_slots,
+             self.out_dim, in_dim, half, ptr(W), stream())
 
     def prefill(self, A: torch.Tensor, tiles: torch.Tensor, max_tiles: int, active: torch.Tensor | None,
                 max_slots: int, n_rows: int, in_dim: int) -> torch.Tensor:
@@ -355,12 +358,9 @@ class CodebookModule(nn.Module):
         decode the active experts' weights once, then one grouped GEMM.
         Returns (n_rows, out_dim) f32."""
         dev = A.device
-        descs = [layer.descriptor(dev, primary=(i == 0)) for i, layer in enumerate(self.layers)]
-        arr = (FwdLayer * len(descs))(*descs)
         KC, NT = -(-in_dim // 64), -(-self.out_dim // 256)
         W = torch.empty(max_slots * NT * KC * 16384, dtype=torch.bfloat16, device=dev)
-        call("skcq_prefill_dequant", _lib.C.cast(arr, _lib.C.c_void_p), len(descs), ptr(active), max_slots,
-             self.out_dim, in_dim, self.col_group(), ptr(W), stream())
+        self.dequant_into(W, active, max_slots, in_dim)
         y = torch.empty(n_rows, self.out_dim, dtype=torch.float32, device=dev)
         call("skcq_prefill_gemm", ptr(A), ptr(W), ptr(tiles), max_tiles, in_dim, self.out_dim, ptr(y), y.stride(0),
              stream())
@@ -478,7 +478,8 @@ class CodebookExperts(nn.Module):
                 _lib.poll_device_error()
             return out.to(device=hidden_states.device, dtype=hidden_states.dtype)
         S = _choose_splits(max_active, I, min(self.gate.min_blocks, self.up.min_blocks), P)
-        seg_kw = {"active": active, "max_active": max_active, "n_rows": P}
+        # rows per expert: at most T when a token's k experts are distinct
+        seg_kw = {"active": active, "max_active": max_active, "n_rows": P, "rows_hint": min(T, 8)}
         g, _ = self.gate.run_segments(h, seg, None, E, row_token=perm, T=T, n_split=S, **seg_kw)
         u, _ = self.up.run_segments(h, seg, None, E, row_token=perm, T=T, n_split=S, **seg_kw)
         inter = torch.empty(P, I, dtype=torch.float32, device=dev)
@@ -498,7 +499,6 @@ class CodebookExperts(nn.Module):
     def _use_prefill(self, h: torch.Tensor, P: int, max_active: int) -> bool:
         mods = (self.gate, self.up, self.down)
         return (h.dtype == torch.bfloat16 and P >= self.prefill_min_rows * max(1, max_active)
-                and all(m.col_group() is not None for m in mods)
                 and all(la.codebook.dtype == torch.bfloat16 for m in mods for la in m.layers))
 
     def _forward_prefill(self, h, topk, w, perm, seg, inv, active, T, k, E, P, max_active) -> torch.Tensor:
@@ -515,20 +515,68 @@ class CodebookExperts(nn.Module):
         A = torch.empty(max_tiles * (-(-H // 64)) * 8192, dtype=torch.bfloat16, device=dev)
         call("skcq_prefill_pack", 0, ptr(h), _DTYPE[h.dtype], h.stride(0), ptr(perm), T, None, 0, H, ptr(tiles),
              max_tiles, ptr(A), stream())
-        g = self.gate.prefill(A, tiles, max_tiles, active, max_active, P, H)
-        u = self.up.prefill(A, tiles, max_tiles, active, max_active, P, H)
-        del A
         A2 = torch.empty(max_tiles * (-(-I // 64)) * 8192, dtype=torch.bfloat16, device=dev)
-        if _is_silu(self.intermediate.act_fn):
-            call("skcq_prefill_pack", 1, ptr(g), _DTYPE[torch.float32], g.stride(0), None, 0, ptr(u), u.stride(0), I,
-                 ptr(tiles), max_tiles, ptr(A2), stream())
+        if _is_silu(self.intermediate.act_fn) and self.up.out_dim == I:
+            # gate and up share one weight image; the GEMM epilogue applies SwiGLU
+            # and writes the down projection's packed rows
+            Wgu = torch.empty(max_active * (-(-I // 128)) * (-(-H // 64)) * 16384, dtype=torch.bfloat16, device=dev)
+            self.gate.dequant_into(Wgu, active, max_active, H, half=0)
+            self.up.dequant_into(Wgu, active, max_active, H, half=1)
+            call("skcq_prefill_gemm_swiglu", ptr(A), ptr(Wgu), ptr(tiles), max_tiles, H, I, ptr(A2), stream())
+            del Wgu
         else:
+            g = self.gate.prefill(A, tiles, max_tiles, active, max_active, P, H)
+            u = self.up.prefill(A, tiles, max_tiles, active, max_active, P, H)
             inter = self.intermediate(g, u).float().contiguous()
+            del g, u
             call("skcq_prefill_pack", 0, ptr(inter), _DTYPE[torch.float32], inter.stride(0), None, 0, None, 0, I,
                  ptr(tiles), max_tiles, ptr(A2), stream())
-        del g, u
+        del A
         d = self.down.prefill(A2, tiles, max_tiles, active, max_active, P, I)
         out = torch.empty(T, H, dtype=h.dtype, device=dev)
         call("skcq_combine", ptr(d), 1, P, ptr(inv), ptr(topk), ptr(w), _DTYPE[w.dtype], T, k, H, ptr(out),
              _DTYPE[out.dtype], stream())
         return out
+
+
+class GraphedExperts:
+    """CUDA-graph replay of ``CodebookExperts.forward`` for one batch shape.
+
+    Decode steps are launch-bound (route, three layers per projection, SwiGLU,
+    combine); capturing them once and replaying removes the per-launch host
+    cost. Inputs are copied into static buffers, the graph is replayed and the
+    static output tensor is returned (overwritten by the next call). Device-side
+    checks (an expert id out of range) are recorded and can be read with
+    ``skcq_b200._lib.poll_device_error()``.
+    """
+
+    def __init__(self, experts: CodebookExperts, n_tokens: int, top_k: int, dtype: torch.dtype = torch.bfloat16,
+                 weights_dtype: torch.dtype = torch.float32, device: torch.device | None = None) -> None:
+        dev = device or _cuda_of(experts.gate.primary.codebook)
+        H = experts.down.out_dim
+        self.experts = experts
+        self.x = torch.zeros(n_tokens, H, dtype=dtype, device=dev)
+        self.topi = torch.arange(top_k, device=dev).remainder(experts.num_experts).expand(n_tokens, top_k).contiguous()
+        self.topw = torch.full((n_tokens, top_k), 1.0 / top_k, dtype=weights_dtype, device=dev)
+        check = experts.check_errors
+        experts.check_errors = False
+        try:
+            side = torch.cuda.Stream(device=dev)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(side):
+                for _ in range(2):  # builds device layouts and configures kernels outside the capture
+                    experts(self.x, self.topi, self.topw)
+            torch.cuda.current_stream(dev).wait_stream(side)
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph, capture_error_mode="relaxed"):
+                self.out = experts(self.x, self.topi, self.topw)
+        finally:
+            experts.check_errors = check
+
+    def __call__(self, hidden_states: torch.Tensor, top_k_index: torch.Tensor,
+                 top_k_weights: torch.Tensor) -> torch.Tensor:
+        self.x.copy_(hidden_states, non_blocking=True)
+        self.topi.copy_(top_k_index, non_blocking=True)
+        self.topw.copy_(top_k_weights, non_blocking=True)
+        self.graph.replay()
+        return self.out

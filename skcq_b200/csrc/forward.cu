@@ -188,8 +188,13 @@ __global__ void __launch_bounds__(RT_THREADS) route_sort_kernel(const int64_t* _
 // ---------------------------------------------------------------------------
 
 constexpr int FW_THREADS = 128;  // outputs per CTA
-constexpr int FW_ROWS = 8;       // rows per shared-memory chunk
-constexpr int FW_UNROLL = 4;     // blocks whose loads are issued together
+constexpr int FW_ROWS = 8;       // most rows per shared-memory chunk (the kernel's R is 1, 2, 4 or 8)
+
+// blocks whose centroid loads are issued together (more for small vectors)
+template <int BS>
+__host__ __device__ constexpr int fw_unroll() {
+  return BS <= 4 ? 8 : (BS <= 8 ? 4 : 2);
+}
 
 struct FwdArgs {
   const void* x;
@@ -211,7 +216,7 @@ struct FwdArgs {
 // acc[r] += scale * <xs[r][col0 + 0..BS), w> for the R rows of the chunk.
 template <int BS, int R>
 __device__ __forceinline__ void block_rows(const float* __restrict__ xs, int ld, int col0, const float (&w)[BS],
-                                           bool scaled, float sc, float (&acc)[FW_ROWS]) {
+                                           bool scaled, float sc, float (&acc)[R]) {
 #pragma unroll
   for (int r = 0; r < R; ++r) {
     float d = 0.f;
@@ -223,7 +228,8 @@ __device__ __forceinline__ void block_rows(const float* __restrict__ xs, int ld,
 
 template <int BS, typename T, int R>
 __device__ __forceinline__ void layer_rows(const skcq_fwd_layer& L, int e, int o, int out, int b0, int b1,
-                                           const float* __restrict__ xs, int ld, bool last, float (&acc)[FW_ROWS]) {
+                                           const float* __restrict__ xs, int ld, bool last, float (&acc)[R]) {
+  constexpr int FW_UNROLL = fw_unroll<BS>();
   const int nb = L.n_blocks;
   const T* table = static_cast<const T*>(L.table);
   const uint16_t* ix = L.idx16 + (int64_t)e * nb * out + o;
@@ -277,14 +283,14 @@ __device__ __forceinline__ void layer_rows(const skcq_fwd_layer& L, int e, int o
 // Generic block size (runtime bs <= 32): same arithmetic, scalar loads.
 template <typename T, int R>
 __device__ __forceinline__ void layer_rows_any(const skcq_fwd_layer& L, int e, int o, int out, int b0, int b1,
-                                               const float* __restrict__ xs, int ld, bool last, float (&acc)[FW_ROWS]) {
+                                               const float* __restrict__ xs, int ld, bool last, float (&acc)[R]) {
   const int nb = L.n_blocks, bs = L.bs;
   const T* table = static_cast<const T*>(L.table);
   for (int b = b0; b < b1; ++b) {
     const int idx = L.idx16[((int64_t)e * nb + b) * out + o];
     const uint32_t m = L.sign_mask ? L.sign_mask[((int64_t)e * nb + b) * out + o] : 0u;
     const T* cp = table + ((int64_t)b * L.K + idx) * bs;
-    float d[FW_ROWS];
+    float d[R];
 #pragma unroll
     for (int r = 0; r < R; ++r) d[r] = 0.f;
     for (int j = 0; j < bs; ++j) {
@@ -318,7 +324,7 @@ __device__ __forceinline__ void layer_rows_any(const skcq_fwd_layer& L, int e, i
 
 template <int BS, typename T, int R>
 __device__ __forceinline__ void rows_dispatch(const skcq_fwd_layer& L, int e, int o, int out, int b0, int b1,
-                                              const float* xs, int ld, bool last, float (&acc)[FW_ROWS]) {
+                                              const float* xs, int ld, bool last, float (&acc)[R]) {
   if constexpr (BS == 0)
     layer_rows_any<T, R>(L, e, o, out, b0, b1, xs, ld, last, acc);
   else
@@ -326,7 +332,10 @@ __device__ __forceinline__ void rows_dispatch(const skcq_fwd_layer& L, int e, in
 }
 
 // grid.x = n_split * (segments) * tiles, split slowest. BS == 0: runtime bs.
-template <int BS, typename T>
+// R rows per shared-memory chunk: the host picks the smallest of 1, 2, 4, 8
+// covering the expected rows per segment (decode: the batch size), so a
+// single-token step runs a kernel with one accumulator per thread.
+template <int BS, typename T, int R>
 __global__ void __launch_bounds__(FW_THREADS) fwd_layer_kernel(FwdArgs a, skcq_fwd_layer L) {
   extern __shared__ float xs[];
   const int out = a.out_dim;
@@ -351,52 +360,71 @@ __global__ void __launch_bounds__(FW_THREADS) fwd_layer_kernel(FwdArgs a, skcq_f
   const int cov = nb * bs;
   const int o = tile * FW_THREADS + threadIdx.x;
   const bool live = o < out;
-  for (int rc = r0; rc < r1; rc += FW_ROWS) {
-    const int nr = min(FW_ROWS, r1 - rc);
+  for (int rc = r0; rc < r1; rc += R) {
+    const int nr = min(R, r1 - rc);
     __syncthreads();
-    for (int i = threadIdx.x; i < nr * ncols; i += FW_THREADS) {
+    for (int i = threadIdx.x; i < R * ncols; i += FW_THREADS) {
       const int rr = i / ncols, c = i - rr * ncols;
-      const int col = c < nblk_cols ? b0 * bs + c : cov + (c - nblk_cols);
-      const int row = rc + rr;
-      const int64_t tok = a.row_token ? (int64_t)(a.row_token[row] % a.T) : (int64_t)row;
-      xs[i] = ld_any(a.x, tok * a.x_ld + col, a.x_dtype);
+      float v = 0.f;
+      if (rr < nr) {
+        const int col = c < nblk_cols ? b0 * bs + c : cov + (c - nblk_cols);
+        const int row = rc + rr;
+        const int64_t tok = a.row_token ? (int64_t)(a.row_token[row] % a.T) : (int64_t)row;
+        v = ld_any(a.x, tok * a.x_ld + col, a.x_dtype);
+      }
+      xs[i] = v;
     }
     __syncthreads();
     if (!live) continue;
-    float acc[FW_ROWS];
+    float acc[R];
 #pragma unroll
-    for (int r = 0; r < FW_ROWS; ++r) acc[r] = 0.f;
-    if (nr == 1)
-      rows_dispatch<BS, T, 1>(L, e, o, out, b0, b1, xs, ncols, last, acc);
-    else if (nr == 2)
-      rows_dispatch<BS, T, 2>(L, e, o, out, b0, b1, xs, ncols, last, acc);
-    else if (nr <= 4)
-      rows_dispatch<BS, T, 4>(L, e, o, out, b0, b1, xs, ncols, last, acc);
-    else
-      rows_dispatch<BS, T, FW_ROWS>(L, e, o, out, b0, b1, xs, ncols, last, acc);
+    for (int r = 0; r < R; ++r) acc[r] = 0.f;
+    rows_dispatch<BS, T, R>(L, e, o, out, b0, b1, xs, ncols, last, acc);
     float* dst = a.part + ((int64_t)split * a.P + rc) * out + o;
-    for (int r = 0; r < nr; ++r) {
-      float v = acc[r];
-      if (a.accumulate) v += dst[(int64_t)r * out];
-      dst[(int64_t)r * out] = v;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      if (r < nr) {
+        float v = acc[r];
+        if (a.accumulate) v += dst[(int64_t)r * out];
+        dst[(int64_t)r * out] = v;
+      }
     }
   }
 }
 
-template <int BS>
-void launch_layer(const FwdArgs& a, const skcq_fwd_layer& L, int grid, size_t smem, cudaStream_t s) {
+template <int BS, int R>
+void launch_layer_r(const FwdArgs& a, const skcq_fwd_layer& L, int grid, size_t smem, cudaStream_t s) {
   if (L.table_dtype == SKCQ_DTYPE_BF16)
-    fwd_layer_kernel<BS, __nv_bfloat16><<<grid, FW_THREADS, smem, s>>>(a, L);
+    fwd_layer_kernel<BS, __nv_bfloat16, R><<<grid, FW_THREADS, smem, s>>>(a, L);
   else
-    fwd_layer_kernel<BS, float><<<grid, FW_THREADS, smem, s>>>(a, L);
+    fwd_layer_kernel<BS, float, R><<<grid, FW_THREADS, smem, s>>>(a, L);
+}
+
+template <int BS>
+void launch_layer(const FwdArgs& a, const skcq_fwd_layer& L, int R, int grid, size_t smem, cudaStream_t s) {
+  switch (R) {
+    case 1: launch_layer_r<BS, 1>(a, L, grid, smem, s); break;
+    case 2: launch_layer_r<BS, 2>(a, L, grid, smem, s); break;
+    case 4: launch_layer_r<BS, 4>(a, L, grid, smem, s); break;
+    default: launch_layer_r<BS, 8>(a, L, grid, smem, s); break;
+  }
+}
+
+template <int BS, int R>
+cudaError_t allow_smem_r() {
+  cudaError_t e = cudaFuncSetAttribute(fwd_layer_kernel<BS, __nv_bfloat16, R>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(fwd_layer_kernel<BS, float, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  return e;
 }
 
 template <int BS>
 cudaError_t allow_smem() {
-  cudaError_t e = cudaFuncSetAttribute(fwd_layer_kernel<BS, __nv_bfloat16>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(fwd_layer_kernel<BS, float>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  cudaError_t e = allow_smem_r<BS, 1>();
+  if (e == cudaSuccess) e = allow_smem_r<BS, 2>();
+  if (e == cudaSuccess) e = allow_smem_r<BS, 4>();
+  if (e == cudaSuccess) e = allow_smem_r<BS, 8>();
   return e;
 }
 
@@ -431,33 +459,47 @@ __global__ void swiglu_kernel(const float* __restrict__ g, const float* __restri
 
 // out[t][h] = sum over the token's k slots, in ascending (expert, kpos) order,
 // of y(pair) * w[t][kpos] (codebook_experts.py:476-480: multiply, then index_add_).
-__global__ void combine_kernel(const float* __restrict__ part, int n_split, int64_t P,
-                               const int32_t* __restrict__ row_of_pair, const int64_t* __restrict__ topk,
-                               const void* __restrict__ w, int w_dtype, int T, int k, int H, void* __restrict__ out,
-                               int out_dtype) {
-  const int64_t total = (int64_t)T * H;
+// One CTA per token: the slot order is resolved once in shared memory, then
+// the threads stream the token's k rows over h.
+constexpr int CB_THREADS = 256;
+
+__global__ void __launch_bounds__(CB_THREADS) combine_kernel(const float* __restrict__ part, int n_split, int64_t P,
+                                                             const int32_t* __restrict__ row_of_pair,
+                                                             const int64_t* __restrict__ topk, const void* __restrict__ w,
+                                                             int w_dtype, int T, int k, int H, void* __restrict__ out,
+                                                             int out_dtype) {
+  __shared__ int s_row[32];
+  __shared__ float s_w[32];
   const int64_t stride = P * H;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int t = (int)(i / H), h = (int)(i % H);
-    float acc = 0.f;
-    uint32_t done = 0;
-    for (int step = 0; step < k; ++step) {
-      int best = -1;
-      int64_t be = 0;
-      for (int kp = 0; kp < k; ++kp) {
-        if (done >> kp & 1u) continue;
-        const int64_t e = topk[(int64_t)t * k + kp];
-        if (best < 0 || e < be) {
-          best = kp;
-          be = e;
+  for (int t = blockIdx.x; t < T; t += gridDim.x) {
+    if (threadIdx.x == 0) {
+      uint32_t done = 0;
+      for (int step = 0; step < k; ++step) {
+        int best = -1;
+        int64_t be = 0;
+        for (int kp = 0; kp < k; ++kp) {
+          if (done >> kp & 1u) continue;
+          const int64_t e = topk[(int64_t)t * k + kp];
+          if (best < 0 || e < be) {
+            best = kp;
+            be = e;
+          }
         }
+        done |= 1u << best;
+        s_row[step] = row_of_pair[(int64_t)best * T + t];
+        s_w[step] = ld_any(w, (int64_t)t * k + best, w_dtype);
       }
-      done |= 1u << best;
-      const int r = row_of_pair[(int64_t)best * T + t];
-      const float y = sum_parts(part, n_split, stride, (int64_t)r * H + h);
-      acc = __fadd_rn(acc, __fmul_rn(y, ld_any(w, (int64_t)t * k + best, w_dtype)));
     }
-    st_any(out, i, out_dtype, acc);
+    __syncthreads();
+    for (int h = threadIdx.x; h < H; h += CB_THREADS) {
+      float acc = 0.f;
+      for (int step = 0; step < k; ++step) {
+        const float y = sum_parts(part, n_split, stride, (int64_t)s_row[step] * H + h);
+        acc = __fadd_rn(acc, __fmul_rn(y, s_w[step]));
+      }
+      st_any(out, (int64_t)t * H + h, out_dtype, acc);
+    }
+    __syncthreads();
   }
 }
 
@@ -527,7 +569,8 @@ extern "C" int skcq_route_sort(const int64_t* topk, int T, int k, int n_experts,
 extern "C" int skcq_codebook_forward(const skcq_fwd_layer* layers, int n_layers, const void* x, int x_dtype,
                                      int64_t x_ld, const int32_t* row_token, int T, const int32_t* seg,
                                      const int32_t* seg_expert, const int32_t* active, int n_seg, int max_active,
-                                     int in_dim, int out_dim, int n_split, float* part, int64_t P, void* stream) {
+                                     int in_dim, int out_dim, int n_split, int rows_hint, float* part, int64_t P,
+                                     void* stream) {
   SKCQ_REQUIRE(layers && x && seg && part, SKCQ_ERR_INVALID, "codebook_forward: null pointer");
   SKCQ_REQUIRE(x_dtype == SKCQ_DTYPE_F32 || x_dtype == SKCQ_DTYPE_BF16, SKCQ_ERR_INVALID,
                "codebook_forward: x dtype %d", x_dtype);
@@ -537,6 +580,7 @@ extern "C" int skcq_codebook_forward(const skcq_fwd_layer* layers, int n_layers,
                "codebook_forward: %d segments, %d active", n_seg, max_active);
   SKCQ_REQUIRE(n_split >= 1 && n_split <= 256, SKCQ_ERR_INVALID, "codebook_forward: %d splits", n_split);
   SKCQ_REQUIRE(row_token == nullptr || T > 0, SKCQ_ERR_INVALID, "codebook_forward: token map without tokens");
+  const int R = rows_hint <= 1 ? 1 : rows_hint <= 2 ? 2 : rows_hint <= 4 ? 4 : FW_ROWS;
   size_t smem_max = 0;
   for (int i = 0; i < n_layers; ++i) {
     const skcq_fwd_layer& L = layers[i];
@@ -551,7 +595,7 @@ extern "C" int skcq_codebook_forward(const skcq_fwd_layer* layers, int n_layers,
     SKCQ_REQUIRE(L.rem == 0 || L.rem_dtype == SKCQ_DTYPE_F32 || L.rem_dtype == SKCQ_DTYPE_BF16, SKCQ_ERR_INVALID,
                  "codebook_forward: layer %d remainder dtype %d", i, L.rem_dtype);
     const int per = (L.n_blocks + n_split - 1) / n_split;
-    const size_t smem = (size_t)FW_ROWS * (per * L.bs + L.rem) * sizeof(float);
+    const size_t smem = (size_t)R * (per * L.bs + L.rem) * sizeof(float);
     if (smem > smem_max) smem_max = smem;
   }
   SKCQ_REQUIRE(smem_max <= 200 * 1024, SKCQ_ERR_INVALID, "codebook_forward: %zu bytes of rows per CTA", smem_max);
@@ -577,15 +621,15 @@ extern "C" int skcq_codebook_forward(const skcq_fwd_layer* layers, int n_layers,
   for (int i = 0; i < n_layers; ++i) {
     const skcq_fwd_layer& L = layers[i];
     const int per = (L.n_blocks + n_split - 1) / n_split;
-    const size_t smem = (size_t)FW_ROWS * (per * L.bs + L.rem) * sizeof(float);
+    const size_t smem = (size_t)R * (per * L.bs + L.rem) * sizeof(float);
     a.accumulate = i > 0;
     switch (L.bs) {
-      case 4: launch_layer<4>(a, L, (int)grid64, smem, s); break;
-      case 6: launch_layer<6>(a, L, (int)grid64, smem, s); break;
-      case 8: launch_layer<8>(a, L, (int)grid64, smem, s); break;
-      case 12: launch_layer<12>(a, L, (int)grid64, smem, s); break;
-      case 16: launch_layer<16>(a, L, (int)grid64, smem, s); break;
-      default: launch_layer<0>(a, L, (int)grid64, smem, s); break;
+      case 4: launch_layer<4>(a, L, R, (int)grid64, smem, s); break;
+      case 6: launch_layer<6>(a, L, R, (int)grid64, smem, s); break;
+      case 8: launch_layer<8>(a, L, R, (int)grid64, smem, s); break;
+      case 12: launch_layer<12>(a, L, R, (int)grid64, smem, s); break;
+      case 16: launch_layer<16>(a, L, R, (int)grid64, smem, s); break;
+      default: launch_layer<0>(a, L, R, (int)grid64, smem, s); break;
     }
     int rc = check_launch("codebook_forward");
     if (rc != SKCQ_OK) return rc;
@@ -622,7 +666,8 @@ extern "C" int skcq_combine(const float* part, int n_split, int64_t P, const int
   SKCQ_REQUIRE(out_dtype == SKCQ_DTYPE_F32 || out_dtype == SKCQ_DTYPE_BF16, SKCQ_ERR_INVALID,
                "combine: output dtype %d", out_dtype);
   if ((int64_t)T * H <= 0) return SKCQ_OK;
-  combine_kernel<<<gridf((int64_t)T * H), 256, 0, (cudaStream_t)stream>>>(part, n_split, P, row_of_pair, topk, weights,
-                                                                          w_dtype, T, k, H, out, out_dtype);
+  const int grid = T < 148 * 16 ? T : 148 * 16;
+  combine_kernel<<<grid, CB_THREADS, 0, (cudaStream_t)stream>>>(part, n_split, P, row_of_pair, topk, weights, w_dtype,
+                                                                T, k, H, out, out_dtype);
   return check_launch("combine");
 }

@@ -162,114 +162,148 @@ struct DqSet {
   int n;
 };
 
-// acc[0..CW) += the layer's contribution to columns [c0, c0 + CW) of row o.
-template <int BS, int CW, typename T>
-__device__ __forceinline__ void dq_layer(const skcq_fwd_layer& L, bool primary, int e, int o, int out, int c0,
-                                         float (&acc)[CW]) {
+// One CTA per 32 KB chunk of W (256 image rows x 64 columns) of one expert;
+// thread rr owns image row rr and accumulates its 64 columns in a private
+// shared-memory row (stride 65 floats: conflict-free), adding for every layer
+// the scaled, signed centroid of each block that overlaps the chunk (and raw
+// remainder columns), then writes its eight 16-byte units. blockIdx.y (the
+// chunk's column range) varies slowest, so the CTAs in flight read the same
+// blocks' centroid tables and those stay in L2.
+constexpr int DQ_THREADS = 256;
+constexpr int DQ_LD = PF_BK + 1;
+
+template <int BS, typename T>
+__device__ __forceinline__ void dq_blocks(const skcq_fwd_layer& L, bool scaled, int e, int o, int out, int c0,
+                                          float* __restrict__ acc) {
   const int nb = L.n_blocks;
-  const int cov = nb * BS;
+  const int b_lo = c0 / BS;
+  const int b_hi = min(nb, (c0 + PF_BK + BS - 1) / BS);
+  const T* table = static_cast<const T*>(L.table);
+  const uint16_t* ix = L.idx16 + (int64_t)e * nb * out + o;
+  const uint32_t* sg = L.sign_mask ? L.sign_mask + (int64_t)e * nb * out + o : nullptr;
+  constexpr int U = BS <= 4 ? 8 : 4;
+  int b = b_lo;
+  for (; b + U <= b_hi; b += U) {
+    int idx[U];
 #pragma unroll
-  for (int bb = 0; bb < CW / BS; ++bb) {
-    const int b = c0 / BS + bb;
-    if (b < nb) {
-      const int64_t eb = ((int64_t)e * nb + b) * out + o;
-      const int idx = __ldg(L.idx16 + eb);
-      float w[BS];
-      load_centroid<BS, T>(static_cast<const T*>(L.table) + ((int64_t)b * L.K + idx) * BS, w);
-      const uint32_t m = L.sign_mask ? __ldg(L.sign_mask + eb) : 0u;
-      const float sc = (primary && L.scales) ? ld_scale(L.scales, eb, L.scale_dtype, L.q_scale) : 1.f;
+    for (int u = 0; u < U; ++u) idx[u] = __ldg(ix + (int64_t)(b + u) * out);
+    float w[U][BS];
+#pragma unroll
+    for (int u = 0; u < U; ++u) load_centroid<BS, T>(table + ((int64_t)(b + u) * L.K + idx[u]) * BS, w[u]);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t eb = ((int64_t)e * nb + b + u) * out + o;
+      const uint32_t m = sg ? __ldg(sg + (int64_t)(b + u) * out) : 0u;
+      const float sc = scaled ? ld_scale(L.scales, eb, L.scale_dtype, L.q_scale) : 1.f;
+      const int col0 = (b + u) * BS - c0;
 #pragma unroll
       for (int j = 0; j < BS; ++j) {
-        const float v = (m >> j & 1u) ? -w[j] : w[j];
-        acc[bb * BS + j] = (primary && L.scales) ? __fmaf_rn(v, sc, acc[bb * BS + j]) : acc[bb * BS + j] + v;
+        const int col = col0 + j;
+        if (col >= 0 && col < PF_BK) {
+          const float v = (m >> j & 1u) ? -w[u][j] : w[u][j];
+          acc[col] = scaled ? __fmaf_rn(v, sc, acc[col]) : acc[col] + v;
+        }
       }
-    } else {
+    }
+  }
+  for (; b < b_hi; ++b) {
+    const int idx = __ldg(ix + (int64_t)b * out);
+    float w[BS];
+    load_centroid<BS, T>(table + ((int64_t)b * L.K + idx) * BS, w);
+    const int64_t eb = ((int64_t)e * nb + b) * out + o;
+    const uint32_t m = sg ? __ldg(sg + (int64_t)b * out) : 0u;
+    const float sc = scaled ? ld_scale(L.scales, eb, L.scale_dtype, L.q_scale) : 1.f;
 #pragma unroll
-      for (int j = 0; j < BS; ++j) {
-        const int col = c0 + bb * BS + j - cov;
-        if (col >= 0 && col < L.rem) acc[bb * BS + j] += ld_any(L.remainder, ((int64_t)e * out + o) * L.rem + col,
-                                                               L.rem_dtype);
+    for (int j = 0; j < BS; ++j) {
+      const int col = b * BS + j - c0;
+      if (col >= 0 && col < PF_BK) {
+        const float v = (m >> j & 1u) ? -w[j] : w[j];
+        acc[col] = scaled ? __fmaf_rn(v, sc, acc[col]) : acc[col] + v;
       }
     }
   }
 }
 
-template <int CW, typename T>
-__device__ __forceinline__ void dq_layer_any(const skcq_fwd_layer& L, bool primary, int e, int o, int out, int c0,
-                                             float (&acc)[CW]) {
-  switch (L.bs) {
-    case 4: if constexpr (CW % 4 == 0) { dq_layer<4, CW, T>(L, primary, e, o, out, c0, acc); return; } break;
-    case 6: if constexpr (CW % 6 == 0) { dq_layer<6, CW, T>(L, primary, e, o, out, c0, acc); return; } break;
-    case 8: if constexpr (CW % 8 == 0) { dq_layer<8, CW, T>(L, primary, e, o, out, c0, acc); return; } break;
-    case 12: if constexpr (CW % 12 == 0) { dq_layer<12, CW, T>(L, primary, e, o, out, c0, acc); return; } break;
-    case 16: if constexpr (CW % 16 == 0) { dq_layer<16, CW, T>(L, primary, e, o, out, c0, acc); return; } break;
-    default: break;
-  }
-  // any other block size dividing CW: element by element
-  const int nb = L.n_blocks, bs = L.bs, cov = nb * bs;
+// any block size <= 32: element loads
+template <typename T>
+__device__ __forceinline__ void dq_blocks_any(const skcq_fwd_layer& L, bool scaled, int e, int o, int out, int c0,
+                                              float* __restrict__ acc) {
+  const int nb = L.n_blocks, bs = L.bs;
   const T* table = static_cast<const T*>(L.table);
-#pragma unroll
-  for (int j = 0; j < CW; ++j) {
-    const int c = c0 + j, b = c / bs;
-    if (b < nb) {
-      const int64_t eb = ((int64_t)e * nb + b) * out + o;
-      const int idx = L.idx16[eb];
-      const int jj = c - b * bs;
+  const int b_lo = c0 / bs, b_hi = min(nb, (c0 + PF_BK + bs - 1) / bs);
+  for (int b = b_lo; b < b_hi; ++b) {
+    const int64_t eb = ((int64_t)e * nb + b) * out + o;
+    const int idx = L.idx16[eb];
+    const uint32_t m = L.sign_mask ? L.sign_mask[eb] : 0u;
+    const float sc = scaled ? ld_scale(L.scales, eb, L.scale_dtype, L.q_scale) : 1.f;
+    for (int j = 0; j < bs; ++j) {
+      const int col = b * bs + j - c0;
+      if (col < 0 || col >= PF_BK) continue;
       float v;
       if constexpr (sizeof(T) == 4)
-        v = reinterpret_cast<const float*>(table)[((int64_t)b * L.K + idx) * bs + jj];
+        v = reinterpret_cast<const float*>(table)[((int64_t)b * L.K + idx) * bs + j];
       else
-        v = __uint_as_float((uint32_t) reinterpret_cast<const uint16_t*>(table)[((int64_t)b * L.K + idx) * bs + jj]
+        v = __uint_as_float((uint32_t) reinterpret_cast<const uint16_t*>(table)[((int64_t)b * L.K + idx) * bs + j]
                             << 16);
-      if (L.sign_mask && (L.sign_mask[eb] >> jj & 1u)) v = -v;
-      acc[j] = (primary && L.scales) ? __fmaf_rn(v, ld_scale(L.scales, eb, L.scale_dtype, L.q_scale), acc[j])
-                                     : acc[j] + v;
-    } else if (c - cov < L.rem) {
-      acc[j] += ld_any(L.remainder, ((int64_t)e * out + o) * L.rem + (c - cov), L.rem_dtype);
+      if (m >> j & 1u) v = -v;
+      acc[col] = scaled ? __fmaf_rn(v, sc, acc[col]) : acc[col] + v;
     }
   }
 }
 
-// thread = (slot, column group, output o), o fastest
-template <int CW>
-__global__ void prefill_dequant_kernel(DqSet set, const int32_t* __restrict__ active, int max_slots, int out,
-                                       int in_dim, int NT, int KC, uint4* __restrict__ W) {
-  const int n_slots = active ? active[0] : max_slots;
-  const int groups = (KC * PF_BK + CW - 1) / CW;
-  const int64_t total = (int64_t)max_slots * groups * out;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int o = (int)(i % out);
-    const int64_t sg = i / out;
-    const int g = (int)(sg % groups), slot = (int)(sg / groups);
-    if (slot >= n_slots) break;  // slots are outermost
-    const int e = active ? active[1 + slot] : slot;
-    const int c0 = g * CW;
-    float acc[CW];
-#pragma unroll
-    for (int j = 0; j < CW; ++j) acc[j] = 0.f;
-    if (c0 < in_dim) {
-      for (int li = 0; li < set.n; ++li) {
-        const skcq_fwd_layer& L = set.l[li];
-        if (L.table_dtype == SKCQ_DTYPE_BF16)
-          dq_layer_any<CW, __nv_bfloat16>(L, li == 0, e, o, out, c0, acc);
-        else
-          dq_layer_any<CW, float>(L, li == 0, e, o, out, c0, acc);
-      }
-#pragma unroll
-      for (int j = 0; j < CW; ++j)
-        if (c0 + j >= in_dim) acc[j] = 0.f;
+template <typename T>
+__device__ __forceinline__ void dq_layer(const skcq_fwd_layer& L, bool scaled, int e, int o, int out, int c0,
+                                         float* acc) {
+  switch (L.bs) {
+    case 4: dq_blocks<4, T>(L, scaled, e, o, out, c0, acc); break;
+    case 6: dq_blocks<6, T>(L, scaled, e, o, out, c0, acc); break;
+    case 8: dq_blocks<8, T>(L, scaled, e, o, out, c0, acc); break;
+    case 12: dq_blocks<12, T>(L, scaled, e, o, out, c0, acc); break;
+    case 16: dq_blocks<16, T>(L, scaled, e, o, out, c0, acc); break;
+    default: dq_blocks_any<T>(L, scaled, e, o, out, c0, acc); break;
+  }
+  // raw remainder columns [cov, cov + rem) (codebook_experts.py:64-74)
+  const int cov = L.n_blocks * L.bs;
+  const int lo = max(cov, c0), hi = min(cov + L.rem, c0 + PF_BK);
+  for (int c = lo; c < hi; ++c) acc[c - c0] += ld_any(L.remainder, ((int64_t)e * out + o) * L.rem + (c - cov), L.rem_dtype);
+}
+
+// half < 0: image rows are 256 outputs; half = 0 | 1: image rows [128 half,
+// 128 half + 128) hold this module's 128 features (gate and up interleaved).
+__global__ void __launch_bounds__(DQ_THREADS, 3) prefill_dequant_kernel(DqSet set, const int32_t* __restrict__ active,
+                                                                     int out, int in_dim, int NT, int KC, int half,
+                                                                     uint4* __restrict__ W) {
+  extern __shared__ float dq_acc[];  // [DQ_THREADS][DQ_LD]
+  const int n_slots = active ? active[0] : (int)(gridDim.x / NT);
+  const int slot = blockIdx.x / NT, nt = blockIdx.x - slot * NT, kc = blockIdx.y;
+  if (slot >= n_slots) return;
+  const int e = active ? active[1 + slot] : slot;
+  // half < 0: 256 threads, one per image row; half >= 0: 128 threads for this
+  // module's rows [128 half, 128 half + 128)
+  const int rr = threadIdx.x + (half < 0 ? 0 : half * (PF_BN / 2));
+  const int o = half < 0 ? nt * PF_BN + rr : nt * (PF_BN / 2) + threadIdx.x;
+  if (o >= out) return;  // rows past out_dim stay unwritten: their accumulator columns are never stored
+  float* acc = dq_acc + threadIdx.x * DQ_LD;
+#pragma unroll 8
+  for (int c = 0; c < PF_BK; ++c) acc[c] = 0.f;
+  const int c0 = kc * PF_BK;
+  if (c0 < in_dim) {
+    for (int li = 0; li < set.n; ++li) {
+      const skcq_fwd_layer& L = set.l[li];
+      const bool scaled = li == 0 && L.scales != nullptr;
+      if (L.table_dtype == SKCQ_DTYPE_BF16)
+        dq_layer<__nv_bfloat16>(L, scaled, e, o, out, c0, acc);
+      else
+        dq_layer<float>(L, scaled, e, o, out, c0, acc);
     }
-    const int nt = o / PF_BN, rr = o % PF_BN;
-    uint4* chunk0 = W + (((int64_t)slot * NT + nt) * KC) * (PF_B_BYTES / 16);
+    for (int c = max(0, in_dim - c0); c < PF_BK; ++c) acc[c] = 0.f;  // K padding
+  }
+  uint4* chunk = W + (((int64_t)slot * NT + nt) * KC + kc) * (PF_B_BYTES / 16);
 #pragma unroll
-    for (int q = 0; q < CW / 8; ++q) {
-      const int c = c0 + q * 8;
-      if (c >= KC * PF_BK) break;  // a group may run past the padded width (CW not dividing 64)
-      const int kc = c / PF_BK, kg = (c % PF_BK) / 8;
-      chunk0[(int64_t)kc * (PF_B_BYTES / 16) + canon_unit(rr, kg)] =
-          make_uint4(pack_bf16x2(acc[q * 8], acc[q * 8 + 1]), pack_bf16x2(acc[q * 8 + 2], acc[q * 8 + 3]),
-                     pack_bf16x2(acc[q * 8 + 4], acc[q * 8 + 5]), pack_bf16x2(acc[q * 8 + 6], acc[q * 8 + 7]));
-    }
+  for (int kg = 0; kg < 8; ++kg) {
+    const float* a = acc + kg * 8;
+    chunk[canon_unit(rr, kg)] = make_uint4(pack_bf16x2(a[0], a[1]), pack_bf16x2(a[2], a[3]),
+                                           pack_bf16x2(a[4], a[5]), pack_bf16x2(a[6], a[7]));
   }
 }
 
@@ -281,11 +315,17 @@ struct GemmArgs {
   const uint8_t* W;  // [slots][NT][KC] 32 KB chunks
   const int32_t* tiles;
   int KC, NT, out;
-  float* y;
+  float* y;  // mode 0: f32 rows
   int64_t y_ld;
+  uint4* a_out;  // mode 1: SwiGLU rows in the A image ([max_tiles][KC_out] chunks)
+  int KC_out;
   int* err;
 };
 
+// MODE 0: y[row][256 nt + c] = D[r][c]. MODE 1 (gate and up interleaved):
+// columns [0, 128) are gate and [128, 256) up for features 128 nt + c; the
+// epilogue writes silu(gate) * up as bf16 into the A image of the next GEMM.
+template <int MODE>
 __global__ void __launch_bounds__(PF_THREADS, 1) prefill_gemm_kernel(GemmArgs g) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const int t = blockIdx.x, nt = blockIdx.y;
@@ -348,6 +388,33 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_gemm_kernel(GemmArgs g)
         tc_commit(empty + s);
       }
       if (ok) tc_commit(acc_full);
+    }
+  } else if (MODE == 1) {
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    if (mbar_wait(acc_full, 0, g.err, 53)) {
+      tc_fence_after();
+      const int r = q * 32 + lane;
+      const bool live = row0 + r < row1;
+      for (int j = 0; j < PF_BN / 64; ++j) {
+        float gv[32], uv[32];
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + j * 32, gv);
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + PF_BN / 2 + j * 32, uv);
+        tmem_wait_ld();
+        const int f0 = nt * (PF_BN / 2) + j * 32;
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const float a = gv[c];
+          gv[c] = (live && f0 + c < g.out) ? __fdiv_rn(a, 1.0f + expf(-a)) * uv[c] : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int k = f0 + u * 8;
+          if (k < g.KC_out * PF_BK)
+            g.a_out[((int64_t)t * g.KC_out + k / PF_BK) * (PF_A_BYTES / 16) + canon_unit(r, (k % PF_BK) / 8)] =
+                make_uint4(pack_bf16x2(gv[u * 8], gv[u * 8 + 1]), pack_bf16x2(gv[u * 8 + 2], gv[u * 8 + 3]),
+                           pack_bf16x2(gv[u * 8 + 4], gv[u * 8 + 5]), pack_bf16x2(gv[u * 8 + 6], gv[u * 8 + 7]));
+        }
+      }
     }
   } else {
     const int q = warp & 3;  // TMEM lane quarter this warp may access
@@ -416,18 +483,19 @@ extern "C" int skcq_prefill_pack(int mode, const void* x, int x_dtype, int64_t x
 }
 
 extern "C" int skcq_prefill_dequant(const skcq_fwd_layer* layers, int n_layers, const int32_t* active, int max_slots,
-                                    int out_dim, int in_dim, int col_group, void* W, void* stream) {
+                                    int out_dim, int in_dim, int half, void* W, void* stream) {
   SKCQ_REQUIRE(layers && W, SKCQ_ERR_INVALID, "prefill_dequant: null pointer");
   SKCQ_REQUIRE(n_layers >= 1 && n_layers <= SKCQ_MAX_CODECS, SKCQ_ERR_INVALID, "prefill_dequant: %d layers",
                n_layers);
   SKCQ_REQUIRE(((uintptr_t)W & 15) == 0 && out_dim > 0 && in_dim > 0 && max_slots >= 0, SKCQ_ERR_INVALID,
                "prefill_dequant: bad sizes");
+  SKCQ_REQUIRE(half >= -1 && half <= 1, SKCQ_ERR_INVALID, "prefill_dequant: half %d", half);
   DqSet set;
   set.n = n_layers;
   for (int i = 0; i < n_layers; ++i) {
     const skcq_fwd_layer& L = layers[i];
-    SKCQ_REQUIRE(L.table && L.idx16 && L.bs > 0 && L.bs <= 32 && L.K > 0 && col_group % L.bs == 0, SKCQ_ERR_INVALID,
-                 "prefill_dequant: layer %d (bs %d) does not fit column groups of %d", i, L.bs, col_group);
+    SKCQ_REQUIRE(L.table && L.idx16 && L.bs > 0 && L.bs <= 32 && L.K > 0 && L.n_blocks >= 0, SKCQ_ERR_INVALID,
+                 "prefill_dequant: layer %d incomplete or bs %d out of range", i, L.bs);
     SKCQ_REQUIRE(L.table_dtype == SKCQ_DTYPE_F32 || L.table_dtype == SKCQ_DTYPE_BF16, SKCQ_ERR_INVALID,
                  "prefill_dequant: layer %d table dtype %d", i, L.table_dtype);
     SKCQ_REQUIRE(L.n_blocks * L.bs + L.rem <= in_dim && (L.rem == 0 || L.remainder), SKCQ_ERR_INVALID,
@@ -435,25 +503,36 @@ extern "C" int skcq_prefill_dequant(const skcq_fwd_layer* layers, int n_layers, 
     set.l[i] = L;
   }
   if (max_slots == 0) return SKCQ_OK;
-  const int KC = ceil_div(in_dim, PF_BK), NT = ceil_div(out_dim, PF_BN);
-  SKCQ_REQUIRE(out_dim <= NT * PF_BN, SKCQ_ERR_INVALID, "prefill_dequant: out");
-  cudaStream_t s = (cudaStream_t)stream;
-  // rows of the last 256-output tile past out_dim stay as the caller left them;
-  // they only feed accumulator columns that the GEMM never stores
-  const int64_t total = (int64_t)max_slots * ((KC * PF_BK + col_group - 1) / col_group) * out_dim;
-  int64_t grid = (total + 127) / 128;
-  if (grid > 148 * 64) grid = 148 * 64;
-  uint4* w = static_cast<uint4*>(W);
-  switch (col_group) {
-    case 8: prefill_dequant_kernel<8><<<(int)grid, 128, 0, s>>>(set, active, max_slots, out_dim, in_dim, NT, KC, w); break;
-    case 16: prefill_dequant_kernel<16><<<(int)grid, 128, 0, s>>>(set, active, max_slots, out_dim, in_dim, NT, KC, w); break;
-    case 24: prefill_dequant_kernel<24><<<(int)grid, 128, 0, s>>>(set, active, max_slots, out_dim, in_dim, NT, KC, w); break;
-    case 32: prefill_dequant_kernel<32><<<(int)grid, 128, 0, s>>>(set, active, max_slots, out_dim, in_dim, NT, KC, w); break;
-    case 48: prefill_dequant_kernel<48><<<(int)grid, 128, 0, s>>>(set, active, max_slots, out_dim, in_dim, NT, KC, w); break;
-    case 64: prefill_dequant_kernel<64><<<(int)grid, 128, 0, s>>>(set, active, max_slots, out_dim, in_dim, NT, KC, w); break;
-    default: return set_error(SKCQ_ERR_INVALID, "prefill_dequant: column group %d not in {8, 16, 24, 32, 48, 64}", col_group);
+  const int KC = ceil_div(in_dim, PF_BK), NT = ceil_div(out_dim, half < 0 ? PF_BN : PF_BN / 2);
+  SKCQ_REQUIRE((int64_t)max_slots * NT < (1LL << 31) && KC < 65536, SKCQ_ERR_INVALID, "prefill_dequant: grid");
+  static thread_local int configured_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int threads = half < 0 ? DQ_THREADS : DQ_THREADS / 2;
+  const int smem = threads * DQ_LD * (int)sizeof(float);
+  if (configured_dev != dev) {
+    cudaError_t e = cudaFuncSetAttribute(prefill_dequant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         DQ_THREADS * DQ_LD * (int)sizeof(float));
+    if (e != cudaSuccess) return set_error(SKCQ_ERR_CUDA, "prefill_dequant: %s", cudaGetErrorString(e));
+    configured_dev = dev;
   }
+  dim3 grid((unsigned)(max_slots * NT), (unsigned)KC);
+  prefill_dequant_kernel<<<grid, threads, smem, (cudaStream_t)stream>>>(set, active, out_dim, in_dim, NT, KC, half,
+                                                                      static_cast<uint4*>(W));
   return check_launch("prefill_dequant");
+}
+
+static int gemm_configure() {
+  static thread_local int configured_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_dev == dev) return SKCQ_OK;
+  cudaError_t e = cudaFuncSetAttribute(prefill_gemm_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PF_SMEM);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(prefill_gemm_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PF_SMEM);
+  if (e != cudaSuccess) return set_error(SKCQ_ERR_CUDA, "prefill_gemm: %s", cudaGetErrorString(e));
+  configured_dev = dev;
+  return SKCQ_OK;
 }
 
 extern "C" int skcq_prefill_gemm(const void* A, const void* W, const int32_t* tiles, int max_tiles, int in_dim,
@@ -464,17 +543,29 @@ extern "C" int skcq_prefill_gemm(const void* A, const void* W, const int32_t* ti
   SKCQ_REQUIRE(max_tiles > 0 && in_dim > 0 && out_dim > 0, SKCQ_ERR_INVALID, "prefill_gemm: bad sizes");
   int* err = device_error_word();
   SKCQ_REQUIRE(err != nullptr, SKCQ_ERR_CUDA, "prefill_gemm: no device error word");
-  static thread_local int configured_dev = -1;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (configured_dev != dev) {
-    cudaError_t e = cudaFuncSetAttribute(prefill_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PF_SMEM);
-    if (e != cudaSuccess) return set_error(SKCQ_ERR_CUDA, "prefill_gemm: %s", cudaGetErrorString(e));
-    configured_dev = dev;
-  }
+  const int rc = gemm_configure();
+  if (rc != SKCQ_OK) return rc;
   GemmArgs g{static_cast<const uint8_t*>(A), static_cast<const uint8_t*>(W), tiles, ceil_div(in_dim, PF_BK),
-             ceil_div(out_dim, PF_BN), out_dim, y, y_ld, err};
+             ceil_div(out_dim, PF_BN), out_dim, y, y_ld, nullptr, 0, err};
   dim3 grid((unsigned)max_tiles, (unsigned)g.NT);
-  prefill_gemm_kernel<<<grid, PF_THREADS, PF_SMEM, (cudaStream_t)stream>>>(g);
+  prefill_gemm_kernel<0><<<grid, PF_THREADS, PF_SMEM, (cudaStream_t)stream>>>(g);
   return check_launch("prefill_gemm");
+}
+
+extern "C" int skcq_prefill_gemm_swiglu(const void* A, const void* W_gate_up, const int32_t* tiles, int max_tiles,
+                                        int in_dim, int inter_dim, void* A_out, void* stream) {
+  SKCQ_REQUIRE(A && W_gate_up && tiles && A_out, SKCQ_ERR_INVALID, "prefill_gemm_swiglu: null pointer");
+  SKCQ_REQUIRE(((uintptr_t)A & 15) == 0 && ((uintptr_t)W_gate_up & 15) == 0 && ((uintptr_t)A_out & 15) == 0,
+               SKCQ_ERR_INVALID, "prefill_gemm_swiglu: operands must be 16-byte aligned");
+  SKCQ_REQUIRE(max_tiles > 0 && in_dim > 0 && inter_dim > 0, SKCQ_ERR_INVALID, "prefill_gemm_swiglu: bad sizes");
+  int* err = device_error_word();
+  SKCQ_REQUIRE(err != nullptr, SKCQ_ERR_CUDA, "prefill_gemm_swiglu: no device error word");
+  const int rc = gemm_configure();
+  if (rc != SKCQ_OK) return rc;
+  GemmArgs g{static_cast<const uint8_t*>(A), static_cast<const uint8_t*>(W_gate_up), tiles, ceil_div(in_dim, PF_BK),
+             ceil_div(inter_dim, PF_BN / 2), inter_dim, nullptr, 0, static_cast<uint4*>(A_out),
+             ceil_div(inter_dim, PF_BK), err};
+  dim3 grid((unsigned)max_tiles, (unsigned)g.NT);
+  prefill_gemm_kernel<1><<<grid, PF_THREADS, PF_SMEM, (cudaStream_t)stream>>>(g);
+  return check_launch("prefill_gemm_swiglu");
 }

@@ -386,13 +386,13 @@ def test_prefill_tensor_core_path_matches_gather_path(case):
     _lib.LAUNCHES.enabled = True
     y_tc = ex(x, topi, topw)
     _lib.LAUNCHES.enabled = False
-    assert _lib.LAUNCHES.calls.get("skcq_prefill_gemm") == 3
+    assert _lib.LAUNCHES.calls.get("skcq_prefill_gemm_swiglu") == 1 and _lib.LAUNCHES.calls.get("skcq_prefill_gemm") == 1
     ex.prefill_min_rows = 1 << 30
     _lib.LAUNCHES.reset()
     _lib.LAUNCHES.enabled = True
     y_ref = ex(x, topi, topw)
     _lib.LAUNCHES.enabled = False
-    assert "skcq_prefill_gemm" not in _lib.LAUNCHES.calls
+    assert "skcq_prefill_gemm" not in _lib.LAUNCHES.calls and "skcq_prefill_gemm_swiglu" not in _lib.LAUNCHES.calls
     a, b = y_tc.double(), y_ref.double()
     cos = torch.nn.functional.cosine_similarity(a.flatten(), b.flatten(), dim=0).item()
     assert cos >= 0.9999, cos
@@ -431,3 +431,35 @@ def test_prefill_gemm_exact_on_bf16_operands():
         ref = xs @ W.t()
         got = y[r0:r1].double().cpu()
         assert torch.allclose(got, ref, rtol=1e-4, atol=1e-4 * ref.abs().max().item()), e
+
+
+def test_prefill_generic_activation_path():
+    """A non-SiLU act_fn takes the unfused two-GEMM prefill route."""
+    E, H, I, T, k = 4, 128, 96, 256, 2
+    ex, x, topi, topw = _prefill_case(E, H, I, T, k, [(8, 32, True)], [(8, 32, True)], seed=505)
+    ex.intermediate.act_fn = torch.nn.functional.gelu
+    y_tc = ex(x, topi, topw).double()
+    ex.prefill_min_rows = 1 << 30
+    y_ref = ex(x, topi, topw).double()
+    cos = torch.nn.functional.cosine_similarity(y_tc.flatten(), y_ref.flatten(), dim=0).item()
+    assert cos >= 0.9999 and (y_tc - y_ref).abs().max().item() <= 1e-2 * y_ref.abs().max().item()
+
+
+def test_graphed_decode_replays_eager_results():
+    """GraphedExperts (CUDA-graph replay) gives bit-identical results to the
+    eager forward for fresh inputs of the captured shape."""
+    from skcq_b200.codebook_experts import CodebookExperts, GraphedExperts
+
+    E, H, I, T, k = 16, 256, 128, 4, 4
+    gate = _random_module(E, I, H, [(8, 64, True), (4, 256, False)], seed=61, dtype=torch.bfloat16)
+    up = _random_module(E, I, H, [(8, 64, True), (4, 256, False)], seed=62, dtype=torch.bfloat16)
+    down = _random_module(E, H, I, [(8, 64, True)], seed=63, dtype=torch.bfloat16)
+    ex = CodebookExperts(gate, up, down, E, torch.nn.functional.silu)
+    g = GraphedExperts(ex, T, k)
+    gen = torch.Generator().manual_seed(64)
+    for _ in range(3):
+        x = torch.randn(T, H, generator=gen).to(torch.bfloat16).cuda()
+        topi = torch.rand(T, E, generator=gen).argsort(-1)[:, :k].cuda()
+        topw = torch.rand(T, k, generator=gen).cuda()
+        y = g(x, topi, topw).clone()
+        assert torch.equal(y, ex(x, topi, topw))
