@@ -1,6 +1,16 @@
 """Kernel micro-benchmark: time one engine kernel on synthetic shapes.
 
     python -m skcq_b200.kernel_bench assign --metric l2 --bs 4 --K 65536 --blocks 64 --rows 98304 --reps 3
+    python -m skcq_b200.kernel_bench prefill --experts 128 --tokens 16384 --reps 3
+    python -m skcq_b200.kernel_bench dequant --experts 32 --reps 3
+    python -m skcq_b200.kernel_bench decode --experts 32 --tokens 1 --reps 3
+
+The forward cases build random codebook modules with the config-2 codebook
+shapes (primary bs=8 K=4096 with bf16 scales, residuals bs=16 K=4096 and
+bs=4 K=65536; hidden 2048, intermediate 768) and uniform random indices.
+`prefill` times every launch of one CodebookExperts forward (Zipf(1.1)
+routing, top-8) with CUDA events; `dequant` decodes one gate projection's
+experts; `decode` runs one routed step of T tokens.
 
 Prints one JSON line per case with the mean CUDA-event time per launch and the
 algorithmic work rate. Useful as the target of a profiler capture (few launches,
@@ -61,9 +71,98 @@ def assign_case(metric: int, bs: int, K: int, blocks: int, rows: int, reps: int,
     }
 
 
+def _random_module(E: int, out_dim: int, in_dim: int, gen: torch.Generator):
+    from skcq_b200.codebook_experts import CodebookModule, _CodebookLayer
+
+    dev = gen.device
+    layers = []
+    for i, (bs, K) in enumerate([(8, 4096), (16, 4096), (4, 65536)]):
+        nb = in_dim // bs
+        cb = (torch.randn(nb, bs, K, generator=gen, device=dev) * 0.05).to(torch.bfloat16)
+        a = torch.randint(0, K, (E, nb, out_dim), generator=gen, device=dev)
+        sc = (torch.rand(E, nb, out_dim, generator=gen, device=dev) * 0.1).to(torch.bfloat16) if i == 0 else None
+        layers.append(_CodebookLayer(cb, a, nb, bs, out_dim, K, scales=sc))
+    return CodebookModule(torch.nn.ModuleList(layers), len(layers), out_dim)
+
+
+def _experts(E: int, gen: torch.Generator):
+    from skcq_b200.codebook_experts import CodebookExperts
+
+    H, I = 2048, 768
+    ex = CodebookExperts(_random_module(E, I, H, gen), _random_module(E, I, H, gen), _random_module(E, H, I, gen),
+                         E, torch.nn.functional.silu)
+    ex.check_errors = False
+    return ex
+
+
+def forward_case(kind: str, E: int, T: int, reps: int, warmup: int) -> dict:
+    """Median device time of one forward-path call and per-launch stage times."""
+    import skcq_b200.codebook_experts as ce
+
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(0)
+    if kind == "dequant":
+        gate = _random_module(E, 768, 2048, g)
+        KC, NT = 2048 // 64, 768 // 256
+        W = torch.empty(E * NT * KC * 16384, dtype=torch.bfloat16, device=dev)
+
+        def fn():
+            gate.dequant_into(W, None, E, 2048)
+
+        work = {"weights": E * 768 * 2048}
+    else:
+        ex = _experts(E, g)
+        if kind == "prefill":
+            ranks = torch.randperm(E, generator=g, device=dev).float() + 1
+            u = torch.rand(T, E, generator=g, device=dev).clamp_(1e-20, 1)
+            logits = -1.1 * torch.log(ranks)[None] - torch.log(-torch.log(u))
+        else:
+            logits = torch.randn(T, E, generator=g, device=dev)
+        topw, topi = torch.topk(torch.softmax(logits, -1), 8, dim=-1)
+        x = torch.randn(T, 2048, generator=g, device=dev).to(torch.bfloat16)
+
+        def fn():
+            ex(x, topi, topw)
+
+        work = {"tokens": T, "flops": 2.0 * T * 8 * 3 * 2048 * 768}
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    stages: dict[str, list] = {}
+    orig = ce.call
+
+    def timed(name, *args):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        rc = orig(name, *args)
+        b.record()
+        stages.setdefault(name, []).append((a, b))
+        return rc
+
+    total = []
+    for _ in range(reps):
+        stages.clear()
+        ce.call = timed
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        try:
+            a.record()
+            fn()
+            b.record()
+        finally:
+            ce.call = orig
+        torch.cuda.synchronize()
+        total.append(a.elapsed_time(b))
+    _lib.poll_device_error()
+    ms = sorted(total)[len(total) // 2]
+    return {"case": kind, "experts": E, "tokens": T, "ms": ms, **work,
+            "stages_ms": {k: [round(x.elapsed_time(y), 4) for x, y in v] for k, v in stages.items()}}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["assign"])
+    ap.add_argument("kernel", choices=["assign", "prefill", "dequant", "decode"])
+    ap.add_argument("--experts", type=int, default=128)
+    ap.add_argument("--tokens", type=int, default=16384)
     ap.add_argument("--metric", default="l2", choices=["cosine", "l2"])
     ap.add_argument("--bs", type=int, default=4)
     ap.add_argument("--K", type=int, default=65536)
@@ -73,6 +172,9 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=1)
     a = ap.parse_args()
     _lib.load()
+    if a.kernel != "assign":
+        print(json.dumps(forward_case(a.kernel, a.experts, a.tokens, a.reps, a.warmup)), flush=True)
+        return
     metric = _engine.COSINE if a.metric == "cosine" else _engine.L2
     print(json.dumps(assign_case(metric, a.bs, a.K, a.blocks, a.rows, a.reps, a.warmup)), flush=True)
 
