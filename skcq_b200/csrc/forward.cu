@@ -459,8 +459,9 @@ __global__ void swiglu_kernel(const float* __restrict__ g, const float* __restri
 
 // out[t][h] = sum over the token's k slots, in ascending (expert, kpos) order,
 // of y(pair) * w[t][kpos] (codebook_experts.py:476-480: multiply, then index_add_).
-// One CTA per token: the slot order is resolved once in shared memory, then
-// the threads stream the token's k rows over h.
+// A CTA owns one token and a stripe of h (grid.y stripes, so a one-token
+// decode step still spreads over the SMs): the slot order is resolved once in
+// shared memory, then the threads stream the token's k rows over h.
 constexpr int CB_THREADS = 256;
 
 __global__ void __launch_bounds__(CB_THREADS) combine_kernel(const float* __restrict__ part, int n_split, int64_t P,
@@ -491,7 +492,7 @@ __global__ void __launch_bounds__(CB_THREADS) combine_kernel(const float* __rest
       }
     }
     __syncthreads();
-    for (int h = threadIdx.x; h < H; h += CB_THREADS) {
+    for (int h = blockIdx.y * CB_THREADS + threadIdx.x; h < H; h += gridDim.y * CB_THREADS) {
       float acc = 0.f;
       for (int step = 0; step < k; ++step) {
         const float y = sum_parts(part, n_split, stride, (int64_t)s_row[step] * H + h);
@@ -666,8 +667,11 @@ extern "C" int skcq_combine(const float* part, int n_split, int64_t P, const int
   SKCQ_REQUIRE(out_dtype == SKCQ_DTYPE_F32 || out_dtype == SKCQ_DTYPE_BF16, SKCQ_ERR_INVALID,
                "combine: output dtype %d", out_dtype);
   if ((int64_t)T * H <= 0) return SKCQ_OK;
-  const int grid = T < 148 * 16 ? T : 148 * 16;
-  combine_kernel<<<grid, CB_THREADS, 0, (cudaStream_t)stream>>>(part, n_split, P, row_of_pair, topk, weights, w_dtype,
-                                                                T, k, H, out, out_dtype);
+  const int gx = T < 148 * 16 ? T : 148 * 16;
+  int gy = ceil_div(H, CB_THREADS);
+  const int want_y = ceil_div(148 * 4, gx);
+  if (gy > want_y) gy = want_y;
+  combine_kernel<<<dim3(gx, gy), CB_THREADS, 0, (cudaStream_t)stream>>>(part, n_split, P, row_of_pair, topk, weights,
+                                                                        w_dtype, T, k, H, out, out_dtype);
   return check_launch("combine");
 }
