@@ -328,7 +328,9 @@ struct GemmArgs {
 template <int MODE>
 __global__ void __launch_bounds__(PF_THREADS, 1) prefill_gemm_kernel(GemmArgs g) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  const int t = blockIdx.x, nt = blockIdx.y;
+  // output tiles vary fastest: the CTAs in flight share their row tile's A
+  // chunks (L2 hits) instead of streaming every row tile once per output tile
+  const int nt = blockIdx.x, t = blockIdx.y;
   if (t >= g.tiles[0]) return;
   const int row0 = g.tiles[1 + 3 * t], row1 = g.tiles[2 + 3 * t], slot = g.tiles[3 + 3 * t];
   uint8_t* base = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
@@ -540,14 +542,15 @@ extern "C" int skcq_prefill_gemm(const void* A, const void* W, const int32_t* ti
   SKCQ_REQUIRE(A && W && tiles && y, SKCQ_ERR_INVALID, "prefill_gemm: null pointer");
   SKCQ_REQUIRE(((uintptr_t)A & 15) == 0 && ((uintptr_t)W & 15) == 0, SKCQ_ERR_INVALID,
                "prefill_gemm: operands must be 16-byte aligned");
-  SKCQ_REQUIRE(max_tiles > 0 && in_dim > 0 && out_dim > 0, SKCQ_ERR_INVALID, "prefill_gemm: bad sizes");
+  SKCQ_REQUIRE(max_tiles > 0 && max_tiles <= 65535 && in_dim > 0 && out_dim > 0, SKCQ_ERR_INVALID,
+               "prefill_gemm: bad sizes (%d row tiles)", max_tiles);
   int* err = device_error_word();
   SKCQ_REQUIRE(err != nullptr, SKCQ_ERR_CUDA, "prefill_gemm: no device error word");
   const int rc = gemm_configure();
   if (rc != SKCQ_OK) return rc;
   GemmArgs g{static_cast<const uint8_t*>(A), static_cast<const uint8_t*>(W), tiles, ceil_div(in_dim, PF_BK),
              ceil_div(out_dim, PF_BN), out_dim, y, y_ld, nullptr, 0, err};
-  dim3 grid((unsigned)max_tiles, (unsigned)g.NT);
+  dim3 grid((unsigned)g.NT, (unsigned)max_tiles);
   prefill_gemm_kernel<0><<<grid, PF_THREADS, PF_SMEM, (cudaStream_t)stream>>>(g);
   return check_launch("prefill_gemm");
 }
@@ -557,7 +560,8 @@ extern "C" int skcq_prefill_gemm_swiglu(const void* A, const void* W_gate_up, co
   SKCQ_REQUIRE(A && W_gate_up && tiles && A_out, SKCQ_ERR_INVALID, "prefill_gemm_swiglu: null pointer");
   SKCQ_REQUIRE(((uintptr_t)A & 15) == 0 && ((uintptr_t)W_gate_up & 15) == 0 && ((uintptr_t)A_out & 15) == 0,
                SKCQ_ERR_INVALID, "prefill_gemm_swiglu: operands must be 16-byte aligned");
-  SKCQ_REQUIRE(max_tiles > 0 && in_dim > 0 && inter_dim > 0, SKCQ_ERR_INVALID, "prefill_gemm_swiglu: bad sizes");
+  SKCQ_REQUIRE(max_tiles > 0 && max_tiles <= 65535 && in_dim > 0 && inter_dim > 0, SKCQ_ERR_INVALID,
+               "prefill_gemm_swiglu: bad sizes (%d row tiles)", max_tiles);
   int* err = device_error_word();
   SKCQ_REQUIRE(err != nullptr, SKCQ_ERR_CUDA, "prefill_gemm_swiglu: no device error word");
   const int rc = gemm_configure();
@@ -565,7 +569,7 @@ extern "C" int skcq_prefill_gemm_swiglu(const void* A, const void* W_gate_up, co
   GemmArgs g{static_cast<const uint8_t*>(A), static_cast<const uint8_t*>(W_gate_up), tiles, ceil_div(in_dim, PF_BK),
              ceil_div(inter_dim, PF_BN / 2), inter_dim, nullptr, 0, static_cast<uint4*>(A_out),
              ceil_div(inter_dim, PF_BK), err};
-  dim3 grid((unsigned)max_tiles, (unsigned)g.NT);
+  dim3 grid((unsigned)g.NT, (unsigned)max_tiles);
   prefill_gemm_kernel<1><<<grid, PF_THREADS, PF_SMEM, (cudaStream_t)stream>>>(g);
   return check_launch("prefill_gemm_swiglu");
 }
