@@ -10,14 +10,18 @@
 //   3. dequant: each active expert's W[out][in] = sum over codebooks of
 //               scale * sign * C_b[idx] (+ raw remainder columns), bf16, in the
 //               same image layout, 32 KB chunks of 256 outputs x 64 k;
-//   4. gemm:    one CTA per (row tile, 256-output tile): a producer warp
-//               streams A and B chunks with 1-D bulk copies into a 4-stage
-//               ring, one thread issues tcgen05.mma kind::f16 (M=128, N=256,
-//               K=16 per instruction) into a TMEM accumulator, four warps read
-//               it back with tcgen05.ld and store fp32 rows.
+//   4. gemm:    persistent CTAs walk (row tile, 256-output tile) items: a
+//               producer warp streams A and B chunks with 1-D bulk copies into
+//               a 4-stage ring, one thread issues tcgen05.mma kind::f16
+//               (M=128, N=256, K=16 per instruction) into one of two TMEM
+//               accumulators, four warps read it back with tcgen05.ld and
+//               store fp32 rows (or SwiGLU rows for the next GEMM) while the
+//               next item accumulates in the other.
 // Because the packer and the decoder write the exact shared-memory image, no
 // tensor map is needed: each stage is two contiguous bulk copies.
 #include <cuda_bf16.h>
+
+#include <algorithm>
 
 #include "common.cuh"
 #include "fwd_common.cuh"
@@ -327,119 +331,168 @@ struct GemmArgs {
 // epilogue writes silu(gate) * up as bf16 into the A image of the next GEMM.
 template <int MODE>
 __global__ void __launch_bounds__(PF_THREADS, 1) prefill_gemm_kernel(GemmArgs g) {
+  // Persistent: one CTA per SM walks the (row tile, output tile) items with
+  // the output tile varying fastest (consecutive items share their row tile's
+  // A chunks in L2). Two 256-column TMEM accumulators let the epilogue of one
+  // item run under the main loop of the next; the stage ring runs on across
+  // items.
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  // output tiles vary fastest: the CTAs in flight share their row tile's A
-  // chunks (L2 hits) instead of streaming every row tile once per output tile
-  const int nt = blockIdx.x, t = blockIdx.y;
-  if (t >= g.tiles[0]) return;
-  const int row0 = g.tiles[1 + 3 * t], row1 = g.tiles[2 + 3 * t], slot = g.tiles[3 + 3 * t];
   uint8_t* base = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t* sa = base;
   uint8_t* sb = base + PF_STAGES * PF_A_BYTES;
   uint64_t* full = reinterpret_cast<uint64_t*>(sb + PF_STAGES * PF_B_BYTES);
   uint64_t* empty = full + PF_STAGES;
-  uint64_t* acc_full = empty + PF_STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  uint64_t* acc_full = empty + PF_STAGES;  // [2]
+  uint64_t* acc_empty = acc_full + 2;      // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int i = 0; i < PF_STAGES; ++i) {
       mbar_init(full + i, 1);
       mbar_init(empty + i, 1);
     }
-    mbar_init(acc_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(acc_full + i, 1);
+      mbar_init(acc_empty + i, 4);  // one arrival per epilogue warp
+    }
     fence_barrier_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, PF_BN);
+    tmem_alloc(tmem_slot, 2 * PF_BN);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int KC = g.KC;
+  const int KC = g.KC, NT = g.NT;
+  const int n_items = g.tiles[0] * NT;
 
   if (warp == 0) {
     if (lane == 0) {
-      const uint8_t* a_src = g.A + (size_t)t * KC * PF_A_BYTES;
-      const uint8_t* b_src = g.W + ((size_t)slot * g.NT + nt) * KC * PF_B_BYTES;
-      for (int kc = 0; kc < KC; ++kc) {
-        const int s = kc % PF_STAGES;
-        if (kc >= PF_STAGES && !mbar_wait(empty + s, ((kc / PF_STAGES) - 1) & 1, g.err, 51)) break;
-        mbar_arrive_expect_tx(full + s, PF_A_BYTES + PF_B_BYTES);
-        bulk_g2s(sa + s * PF_A_BYTES, a_src + (size_t)kc * PF_A_BYTES, PF_A_BYTES, full + s);
-        bulk_g2s(sb + s * PF_B_BYTES, b_src + (size_t)kc * PF_B_BYTES, PF_B_BYTES, full + s);
+      uint32_t s = 0, ph = 0;
+      for (int w = blockIdx.x; w < n_items; w += gridDim.x) {
+        const int t = w / NT, nt = w - t * NT;
+        const int slot = g.tiles[3 + 3 * t];
+        const uint8_t* a_src = g.A + (size_t)t * KC * PF_A_BYTES;
+        const uint8_t* b_src = g.W + ((size_t)slot * NT + nt) * KC * PF_B_BYTES;
+        bool ok = true;
+        for (int kc = 0; kc < KC; ++kc) {
+          if (!mbar_wait(empty + s, ph ^ 1, g.err, 51)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(full + s, PF_A_BYTES + PF_B_BYTES);
+          bulk_g2s(sa + s * PF_A_BYTES, a_src + (size_t)kc * PF_A_BYTES, PF_A_BYTES, full + s);
+          bulk_g2s(sb + s * PF_B_BYTES, b_src + (size_t)kc * PF_B_BYTES, PF_B_BYTES, full + s);
+          if (++s == PF_STAGES) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+        if (!ok) break;
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_bf16(PF_BM, PF_BN);
+      uint32_t s = 0, ph = 0, ab = 0, aph = 0;
       bool ok = true;
-      for (int kc = 0; kc < KC; ++kc) {
-        const int s = kc % PF_STAGES;
-        if (!mbar_wait(full + s, (kc / PF_STAGES) & 1, g.err, 52)) {
-          ok = false;
-          break;
-        }
+      for (int w = blockIdx.x; ok && w < n_items; w += gridDim.x) {
+        if (!mbar_wait(acc_empty + ab, aph ^ 1, g.err, 54)) break;
         tc_fence_after();
-        const uint32_t a0 = smem_u32(sa + s * PF_A_BYTES), b0 = smem_u32(sb + s * PF_B_BYTES);
+        const uint32_t d = tmem + ab * PF_BN;
+        for (int kc = 0; kc < KC; ++kc) {
+          if (!mbar_wait(full + s, ph, g.err, 52)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sa + s * PF_A_BYTES), b0 = smem_u32(sb + s * PF_B_BYTES);
 #pragma unroll
-        for (int kk = 0; kk < PF_BK / 16; ++kk)
-          mma_bf16(tmem, smem_desc(a0 + kk * 256, 128, 1024), smem_desc(b0 + kk * 256, 128, 1024), idesc,
-                   (kc | kk) != 0 ? 1u : 0u);
-        tc_commit(empty + s);
-      }
-      if (ok) tc_commit(acc_full);
-    }
-  } else if (MODE == 1) {
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
-    if (mbar_wait(acc_full, 0, g.err, 53)) {
-      tc_fence_after();
-      const int r = q * 32 + lane;
-      const bool live = row0 + r < row1;
-      for (int j = 0; j < PF_BN / 64; ++j) {
-        float gv[32], uv[32];
-        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + j * 32, gv);
-        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + PF_BN / 2 + j * 32, uv);
-        tmem_wait_ld();
-        const int f0 = nt * (PF_BN / 2) + j * 32;
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const float a = gv[c];
-          gv[c] = (live && f0 + c < g.out) ? __fdiv_rn(a, 1.0f + expf(-a)) * uv[c] : 0.f;
+          for (int kk = 0; kk < PF_BK / 16; ++kk)
+            mma_bf16(d, smem_desc(a0 + kk * 256, 128, 1024), smem_desc(b0 + kk * 256, 128, 1024), idesc,
+                     (kc | kk) != 0 ? 1u : 0u);
+          tc_commit(empty + s);
+          if (++s == PF_STAGES) {
+            s = 0;
+            ph ^= 1;
+          }
         }
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int k = f0 + u * 8;
-          if (k < g.KC_out * PF_BK)
-            g.a_out[((int64_t)t * g.KC_out + k / PF_BK) * (PF_A_BYTES / 16) + canon_unit(r, (k % PF_BK) / 8)] =
-                make_uint4(pack_bf16x2(gv[u * 8], gv[u * 8 + 1]), pack_bf16x2(gv[u * 8 + 2], gv[u * 8 + 3]),
-                           pack_bf16x2(gv[u * 8 + 4], gv[u * 8 + 5]), pack_bf16x2(gv[u * 8 + 6], gv[u * 8 + 7]));
+        if (!ok) break;
+        tc_commit(acc_full + ab);
+        if (++ab == 2) {
+          ab = 0;
+          aph ^= 1;
         }
       }
     }
   } else {
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    if (mbar_wait(acc_full, 0, g.err, 53)) {
+    const int r = q * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    uint32_t ab = 0, aph = 0;
+    for (int w = blockIdx.x; w < n_items; w += gridDim.x) {
+      const int t = w / NT, nt = w - t * NT;
+      const int row0 = g.tiles[1 + 3 * t], row1 = g.tiles[2 + 3 * t];
+      if (!__all_sync(0xffffffffu, mbar_wait(acc_full + ab, aph, g.err, 53))) break;
       tc_fence_after();
-      const int r = q * 32 + lane;
-      const int row = row0 + r;
-      float* yr = g.y + (int64_t)row * g.y_ld + (int64_t)nt * PF_BN;
-      const int ncol = min(PF_BN, g.out - nt * PF_BN);
-      for (int j = 0; j < PF_BN / 32; ++j) {
-        float v[32];
-        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + j * 32, v);
-        tmem_wait_ld();
-        if (row < row1) {
-          if (j * 32 + 32 <= ncol && (g.y_ld & 3) == 0) {
+      const uint32_t d = tmem + lane_off + ab * PF_BN;
+      if (MODE == 1) {
+        const bool live = row0 + r < row1;
+        for (int j = 0; j < PF_BN / 64; ++j) {
+          float gv[32], uv[32];
+          tmem_ld32(d + j * 32, gv);
+          tmem_ld32(d + PF_BN / 2 + j * 32, uv);
+          tmem_wait_ld();
+          if (j == PF_BN / 64 - 1) {  // every column of this accumulator is in registers
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty + ab);
+          }
+          const int f0 = nt * (PF_BN / 2) + j * 32;
 #pragma unroll
-            for (int c = 0; c < 32; c += 4)
-              *reinterpret_cast<float4*>(yr + j * 32 + c) = make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]);
-          } else {
-            for (int c = 0; c < 32; ++c)
-              if (j * 32 + c < ncol) yr[j * 32 + c] = v[c];
+          for (int c = 0; c < 32; ++c) {
+            const float a = gv[c];
+            gv[c] = (live && f0 + c < g.out) ? __fdiv_rn(a, 1.0f + expf(-a)) * uv[c] : 0.f;
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int k = f0 + u * 8;
+            if (k < g.KC_out * PF_BK)
+              g.a_out[((int64_t)t * g.KC_out + k / PF_BK) * (PF_A_BYTES / 16) + canon_unit(r, (k % PF_BK) / 8)] =
+                  make_uint4(pack_bf16x2(gv[u * 8], gv[u * 8 + 1]), pack_bf16x2(gv[u * 8 + 2], gv[u * 8 + 3]),
+                             pack_bf16x2(gv[u * 8 + 4], gv[u * 8 + 5]), pack_bf16x2(gv[u * 8 + 6], gv[u * 8 + 7]));
           }
         }
+      } else {
+        const int row = row0 + r;
+        float* yr = g.y + (int64_t)row * g.y_ld + (int64_t)nt * PF_BN;
+        const int ncol = min(PF_BN, g.out - nt * PF_BN);
+        for (int j = 0; j < PF_BN / 32; ++j) {
+          float v[32];
+          tmem_ld32(d + j * 32, v);
+          tmem_wait_ld();
+          if (j == PF_BN / 32 - 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty + ab);
+          }
+          if (row < row1) {
+            if (j * 32 + 32 <= ncol && (g.y_ld & 3) == 0) {
+#pragma unroll
+              for (int c = 0; c < 32; c += 4)
+                *reinterpret_cast<float4*>(yr + j * 32 + c) = make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]);
+            } else {
+              for (int c = 0; c < 32; ++c)
+                if (j * 32 + c < ncol) yr[j * 32 + c] = v[c];
+            }
+          }
+        }
+      }
+      if (++ab == 2) {
+        ab = 0;
+        aph ^= 1;
       }
     }
   }
@@ -447,8 +500,19 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_gemm_kernel(GemmArgs g)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, PF_BN);
+    tmem_dealloc(tmem, 2 * PF_BN);
   }
+}
+
+static int num_sms_cached() {
+  static thread_local int dev_cached = -1, sms = 148;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev != dev_cached) {
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
+    dev_cached = dev;
+  }
+  return sms;
 }
 
 }  // namespace skcq
@@ -550,7 +614,8 @@ extern "C" int skcq_prefill_gemm(const void* A, const void* W, const int32_t* ti
   if (rc != SKCQ_OK) return rc;
   GemmArgs g{static_cast<const uint8_t*>(A), static_cast<const uint8_t*>(W), tiles, ceil_div(in_dim, PF_BK),
              ceil_div(out_dim, PF_BN), out_dim, y, y_ld, nullptr, 0, err};
-  dim3 grid((unsigned)g.NT, (unsigned)max_tiles);
+  const int64_t items = (int64_t)max_tiles * g.NT;
+  const int grid = (int)std::min<int64_t>(items, num_sms_cached());
   prefill_gemm_kernel<0><<<grid, PF_THREADS, PF_SMEM, (cudaStream_t)stream>>>(g);
   return check_launch("prefill_gemm");
 }
@@ -569,7 +634,8 @@ extern "C" int skcq_prefill_gemm_swiglu(const void* A, const void* W_gate_up, co
   GemmArgs g{static_cast<const uint8_t*>(A), static_cast<const uint8_t*>(W_gate_up), tiles, ceil_div(in_dim, PF_BK),
              ceil_div(inter_dim, PF_BN / 2), inter_dim, nullptr, 0, static_cast<uint4*>(A_out),
              ceil_div(inter_dim, PF_BK), err};
-  dim3 grid((unsigned)g.NT, (unsigned)max_tiles);
+  const int64_t items = (int64_t)max_tiles * g.NT;
+  const int grid = (int)std::min<int64_t>(items, num_sms_cached());
   prefill_gemm_kernel<1><<<grid, PF_THREADS, PF_SMEM, (cudaStream_t)stream>>>(g);
   return check_launch("prefill_gemm_swiglu");
 }
