@@ -311,6 +311,130 @@ __global__ void __launch_bounds__(DQ_THREADS, 3) prefill_dequant_kernel(DqSet se
   }
 }
 
+// Fast path for bf16 tables and up to three layers whose block sizes divide
+// the 64-column chunk (4, 8 or 16; 0 = no such layer): the chunk's columns are
+// accumulated in registers at compile-time positions, and each layer's index
+// loads are all issued before its centroid gathers, so a thread keeps a whole
+// layer's loads in flight and touches no shared memory.
+template <int BS>
+__device__ __forceinline__ void dqf_layer(const skcq_fwd_layer& L, bool scaled, int e, int o, int out, int c0,
+                                          float (&acc)[PF_BK]) {
+  if constexpr (BS > 0) {
+    constexpr int NBC = PF_BK / BS;
+    const int nb = L.n_blocks;
+    const int b0 = c0 / BS;
+    const __nv_bfloat16* table = static_cast<const __nv_bfloat16*>(L.table);
+    const uint16_t* ix = L.idx16 + (int64_t)e * nb * out + o;
+    const int cov = nb * BS;
+    // blocks per batch of loads: all of them, except 8 at a time for bs = 4
+    // (16 gathers of 4 values would not fit the register budget next to acc)
+    constexpr int G = NBC > 8 ? 8 : NBC;
+#pragma unroll
+    for (int g0 = 0; g0 < NBC; g0 += G) {
+    int idx[G];
+#pragma unroll
+    for (int u = 0; u < G; ++u) idx[u] = (b0 + g0 + u < nb) ? (int)__ldg(ix + (int64_t)(b0 + g0 + u) * out) : 0;
+#pragma unroll
+    for (int uu = 0; uu < G; ++uu) {
+      const int u = g0 + uu;
+      const int b = b0 + u;
+      if (b < nb) {
+        float w[BS];
+        load_centroid<BS, __nv_bfloat16>(table + ((int64_t)b * L.K + idx[uu]) * BS, w);
+        const int64_t eb = ((int64_t)e * nb + b) * out + o;
+        const uint32_t m = L.sign_mask ? __ldg(L.sign_mask + eb) : 0u;
+        const float sc = scaled ? ld_scale(L.scales, eb, L.scale_dtype, L.q_scale) : 1.f;
+#pragma unroll
+        for (int j = 0; j < BS; ++j) {
+          const float v = (m >> j & 1u) ? -w[j] : w[j];
+          acc[u * BS + j] = scaled ? __fmaf_rn(v, sc, acc[u * BS + j]) : acc[u * BS + j] + v;
+        }
+      } else if (L.rem > 0) {
+        // raw remainder columns [cov, cov + rem) (codebook_experts.py:64-74)
+#pragma unroll
+        for (int j = 0; j < BS; ++j) {
+          const int col = b * BS + j - cov;
+          if (col >= 0 && col < L.rem)
+            acc[u * BS + j] += ld_any(L.remainder, ((int64_t)e * out + o) * L.rem + col, L.rem_dtype);
+        }
+      }
+    }
+    }
+  }
+}
+
+template <int BS0, int BS1, int BS2>
+__global__ void __launch_bounds__(DQ_THREADS, 2) prefill_dequant_fast_kernel(DqSet set,
+                                                                            const int32_t* __restrict__ active,
+                                                                            int out, int in_dim, int NT, int KC,
+                                                                            int half, uint4* __restrict__ W) {
+  const int n_slots = active ? active[0] : (int)(gridDim.x / NT);
+  const int slot = blockIdx.x / NT, nt = blockIdx.x - slot * NT, kc = blockIdx.y;
+  if (slot >= n_slots) return;
+  const int e = active ? active[1 + slot] : slot;
+  const int rr = threadIdx.x + (half < 0 ? 0 : half * (PF_BN / 2));
+  const int o = half < 0 ? nt * PF_BN + rr : nt * (PF_BN / 2) + threadIdx.x;
+  if (o >= out) return;  // rows past out_dim stay unwritten: their accumulator columns are never stored
+  float acc[PF_BK];
+#pragma unroll
+  for (int c = 0; c < PF_BK; ++c) acc[c] = 0.f;
+  const int c0 = kc * PF_BK;
+  if (c0 < in_dim) {
+    dqf_layer<BS0>(set.l[0], set.l[0].scales != nullptr, e, o, out, c0, acc);
+    if (set.n > 1) dqf_layer<BS1>(set.l[1], false, e, o, out, c0, acc);
+    if (set.n > 2) dqf_layer<BS2>(set.l[2], false, e, o, out, c0, acc);
+#pragma unroll
+    for (int c = 0; c < PF_BK; ++c)
+      if (c0 + c >= in_dim) acc[c] = 0.f;  // K padding
+  }
+  uint4* chunk = W + (((int64_t)slot * NT + nt) * KC + kc) * (PF_B_BYTES / 16);
+#pragma unroll
+  for (int kg = 0; kg < 8; ++kg)
+    chunk[canon_unit(rr, kg)] =
+        make_uint4(pack_bf16x2(acc[kg * 8], acc[kg * 8 + 1]), pack_bf16x2(acc[kg * 8 + 2], acc[kg * 8 + 3]),
+                   pack_bf16x2(acc[kg * 8 + 4], acc[kg * 8 + 5]), pack_bf16x2(acc[kg * 8 + 6], acc[kg * 8 + 7]));
+}
+
+using DqFastFn = void (*)(DqSet, const int32_t*, int, int, int, int, int, uint4*);
+
+template <int BS0, int BS1>
+DqFastFn dq_fast_pick3(int bs2) {
+  switch (bs2) {
+    case 0: return prefill_dequant_fast_kernel<BS0, BS1, 0>;
+    case 4: return prefill_dequant_fast_kernel<BS0, BS1, 4>;
+    case 8: return prefill_dequant_fast_kernel<BS0, BS1, 8>;
+    case 16: return prefill_dequant_fast_kernel<BS0, BS1, 16>;
+    default: return nullptr;
+  }
+}
+
+template <int BS0>
+DqFastFn dq_fast_pick2(int bs1, int bs2) {
+  switch (bs1) {
+    case 0: return bs2 == 0 ? prefill_dequant_fast_kernel<BS0, 0, 0> : nullptr;
+    case 4: return dq_fast_pick3<BS0, 4>(bs2);
+    case 8: return dq_fast_pick3<BS0, 8>(bs2);
+    case 16: return dq_fast_pick3<BS0, 16>(bs2);
+    default: return nullptr;
+  }
+}
+
+// The fast-path instantiation for these layers, or nullptr.
+inline DqFastFn dq_fast_pick(const DqSet& set) {
+  if (set.n > 3) return nullptr;
+  int bs[3] = {0, 0, 0};
+  for (int i = 0; i < set.n; ++i) {
+    if (set.l[i].table_dtype != SKCQ_DTYPE_BF16) return nullptr;
+    bs[i] = set.l[i].bs;
+  }
+  switch (bs[0]) {
+    case 4: return dq_fast_pick2<4>(bs[1], bs[2]);
+    case 8: return dq_fast_pick2<8>(bs[1], bs[2]);
+    case 16: return dq_fast_pick2<16>(bs[1], bs[2]);
+    default: return nullptr;
+  }
+}
+
 // ---------------------------------------------------------------------------
 // 4. grouped GEMM on tcgen05
 // ---------------------------------------------------------------------------
@@ -583,6 +707,11 @@ extern "C" int skcq_prefill_dequant(const skcq_fwd_layer* layers, int n_layers, 
     configured_dev = dev;
   }
   dim3 grid((unsigned)(max_slots * NT), (unsigned)KC);
+  if (DqFastFn fast = dq_fast_pick(set)) {
+    fast<<<grid, threads, 0, (cudaStream_t)stream>>>(set, active, out_dim, in_dim, NT, KC, half,
+                                                     static_cast<uint4*>(W));
+    return check_launch("prefill_dequant");
+  }
   prefill_dequant_kernel<<<grid, threads, smem, (cudaStream_t)stream>>>(set, active, out_dim, in_dim, NT, KC, half,
                                                                       static_cast<uint4*>(W));
   return check_launch("prefill_dequant");
