@@ -299,7 +299,12 @@ int skcq_pack_sign_masks(const int8_t* signs, int E, int out, int64_t sign_ld, i
  * active[1..] their ids ascending (n_experts + 1 entries). An expert id outside
  * [0, n_experts) sets the device error (the reference's one_hot raises). */
 int skcq_route_sort(const int64_t* topk, int T, int k, int n_experts, int32_t* perm, int32_t* seg,
-                    int32_t* row_of_pair, int32_t* active, void* stream);
+                    int32_t* row_of_pair, int32_t* active, void* scratch, size_t scratch_bytes, void* stream);
+
+/* Scratch bytes with which skcq_route_sort spreads a large batch over many
+ * CTAs (0: the one-CTA sort is used; it also runs when scratch is NULL or
+ * smaller than this). The result is the same either way. */
+size_t skcq_route_sort_scratch_bytes(int T, int k, int n_experts);
 
 /* CodebookModule.forward over expert segments (codebook_experts.py:325-339):
  * for the rows r of segment s (expert seg_expert[s], or s when NULL; only the

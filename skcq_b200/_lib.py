@@ -67,7 +67,8 @@ _SIGS: dict[str, list] = {
     "skcq_pack_indices16": [P, L, I, P, P],
     "skcq_transpose_codebook": [P, I, I, I, I, P, P],
     "skcq_pack_sign_masks": [P, I, I, L, I, I, P, P],
-    "skcq_route_sort": [P, I, I, I, P, P, P, P, P],
+    "skcq_route_sort": [P, I, I, I, P, P, P, P, P, C.c_size_t, P],
+    "skcq_route_sort_scratch_bytes": [I, I, I],
     "skcq_codebook_forward": [P, I, P, I, L, P, I, P, P, P, I, I, I, I, I, I, P, L, P],
     "skcq_sum_splits": [P, I, L, I, P, I, L, P],
     "skcq_swiglu": [P, P, I, L, P, P],
@@ -78,7 +79,7 @@ _SIGS: dict[str, list] = {
     "skcq_prefill_gemm": [P, P, P, I, I, I, P, L, P],
     "skcq_prefill_gemm_swiglu": [P, P, P, I, I, I, P, P],
 }
-_RESTYPES = {"skcq_reseed_scratch_bytes": C.c_size_t}
+_RESTYPES = {"skcq_reseed_scratch_bytes": C.c_size_t, "skcq_route_sort_scratch_bytes": C.c_size_t}
 
 _lib: C.CDLL | None = None
 
@@ -149,7 +150,12 @@ def call(name: str, *args) -> int:
         raise RuntimeError(f"{name} failed ({rc}): {last_error()}")
     if LAUNCHES.enabled:
         # the grouped forward launches one kernel per codebook layer (argument 1)
-        LAUNCHES.kernels += args[1] if name == "skcq_codebook_forward" else _KERNELS_PER_CALL.get(name, 0)
+        if name == "skcq_codebook_forward":
+            LAUNCHES.kernels += args[1]  # one kernel per codebook layer
+        elif name == "skcq_route_sort":
+            LAUNCHES.kernels += 3 if args[8] else 1  # multi-CTA form when given scratch
+        else:
+            LAUNCHES.kernels += _KERNELS_PER_CALL.get(name, 0)
         LAUNCHES.calls[name] = LAUNCHES.calls.get(name, 0) + 1
     return rc
 

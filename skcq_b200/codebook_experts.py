@@ -469,7 +469,10 @@ class CodebookExperts(nn.Module):
         inv = route[max(P, 1):2 * max(P, 1)]
         seg = route[2 * max(P, 1):2 * max(P, 1) + E + 1]
         active = route[2 * max(P, 1) + E + 1:]
-        call("skcq_route_sort", ptr(topk), T, k, E, ptr(perm), ptr(seg), ptr(inv), ptr(active), stream())
+        scratch_bytes = int(_lib.load().skcq_route_sort_scratch_bytes(T, k, E))
+        scratch = torch.empty(scratch_bytes, dtype=torch.uint8, device=dev) if scratch_bytes else None
+        call("skcq_route_sort", ptr(topk), T, k, E, ptr(perm), ptr(seg), ptr(inv), ptr(active), ptr(scratch),
+             scratch_bytes, stream())
         max_active = min(E, P)
         I = self.gate.out_dim
         if self._use_prefill(h, P, max_active):

@@ -183,6 +183,102 @@ __global__ void __launch_bounds__(RT_THREADS) route_sort_kernel(const int64_t* _
   }
 }
 
+// Multi-CTA form for large batches (up to RT_SMALL_E experts): count per
+// chunk of RS_CHUNK pairs, one CTA turns the counts into each chunk's first
+// row per expert (and seg / active), then every chunk places its pairs with
+// the same stable warp ranking as the one-CTA kernel. hist is
+// [chunks][n_experts + 1] ints of caller scratch.
+constexpr int RS_CHUNK = 4096;
+
+__global__ void __launch_bounds__(RT_THREADS) route_count_kernel(const int64_t* __restrict__ topk, int T, int k, int E,
+                                                                 int32_t* __restrict__ hist, int* err) {
+  extern __shared__ int sm[];
+  const int NB = E + 1, P = T * k;
+  for (int b = threadIdx.x; b < NB; b += RT_THREADS) sm[b] = 0;
+  __syncthreads();
+  const int p0 = blockIdx.x * RS_CHUNK, p1 = min(P, p0 + RS_CHUNK);
+  for (int p = p0 + threadIdx.x; p < p1; p += RT_THREADS) atomicAdd(&sm[pair_bucket(topk, T, k, E, p, err)], 1);
+  __syncthreads();
+  for (int b = threadIdx.x; b < NB; b += RT_THREADS) hist[(int64_t)blockIdx.x * NB + b] = sm[b];
+}
+
+__global__ void __launch_bounds__(RT_THREADS) route_scan_kernel(int E, int n_chunks, int32_t* __restrict__ hist,
+                                                                int32_t* __restrict__ seg, int32_t* __restrict__ active) {
+  extern __shared__ int sm[];  // [NB] bucket totals
+  const int NB = E + 1;
+  for (int b = threadIdx.x; b < NB; b += RT_THREADS) {
+    int t = 0;
+    for (int c = 0; c < n_chunks; ++c) t += hist[(int64_t)c * NB + b];
+    sm[b] = t;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int run = 0, na = 0;
+    for (int b = 0; b < NB; ++b) {
+      const int c = sm[b];
+      sm[b] = run;
+      if (b < E) {
+        seg[b] = run;
+        if (c > 0) active[1 + na++] = b;
+      }
+      run += c;
+    }
+    seg[E] = sm[E];
+    active[0] = na;
+  }
+  __syncthreads();
+  for (int b = threadIdx.x; b < NB; b += RT_THREADS) {
+    int run = sm[b];
+    for (int c = 0; c < n_chunks; ++c) {
+      const int h = hist[(int64_t)c * NB + b];
+      hist[(int64_t)c * NB + b] = run;
+      run += h;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(RT_THREADS) route_scatter_kernel(const int64_t* __restrict__ topk, int T, int k,
+                                                                   int E, const int32_t* __restrict__ hist,
+                                                                   int32_t* __restrict__ perm,
+                                                                   int32_t* __restrict__ inv, int* err) {
+  extern __shared__ int sm[];
+  const int NB = E + 1, P = T * k;
+  int* base = sm;            // [NB]
+  int* tot = base + NB;      // [NB]
+  int* wcnt = tot + NB;      // [32][NB]
+  const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
+  for (int b = tid; b < NB; b += RT_THREADS) base[b] = hist[(int64_t)blockIdx.x * NB + b];
+  const int p0 = blockIdx.x * RS_CHUNK, p1 = min(P, p0 + RS_CHUNK);
+  for (int c0 = p0; c0 < p1; c0 += RT_THREADS) {
+    for (int i = tid; i < 32 * NB; i += RT_THREADS) wcnt[i] = 0;
+    __syncthreads();
+    const int p = c0 + tid;
+    const int bk = p < p1 ? pair_bucket(topk, T, k, E, p, err) : -1;
+    const unsigned peers = __match_any_sync(0xffffffffu, bk);
+    const int rank = __popc(peers & ((1u << lane) - 1u));
+    if (bk >= 0 && lane == __ffs(peers) - 1) wcnt[w * NB + bk] = __popc(peers);
+    __syncthreads();
+    for (int b = tid; b < NB; b += RT_THREADS) {
+      int run = 0;
+      for (int ww = 0; ww < 32; ++ww) {
+        const int c = wcnt[ww * NB + b];
+        wcnt[ww * NB + b] = run;
+        run += c;
+      }
+      tot[b] = run;
+    }
+    __syncthreads();
+    if (bk >= 0) {
+      const int pos = base[bk] + wcnt[w * NB + bk] + rank;
+      perm[pos] = p;
+      inv[p] = pos;
+    }
+    __syncthreads();
+    for (int b = tid; b < NB; b += RT_THREADS) base[b] += tot[b];
+    __syncthreads();
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Grouped codebook forward
 // ---------------------------------------------------------------------------
@@ -551,8 +647,15 @@ extern "C" int skcq_pack_sign_masks(const int8_t* signs, int E, int out, int64_t
   return check_launch("pack_sign_masks");
 }
 
+extern "C" size_t skcq_route_sort_scratch_bytes(int T, int k, int n_experts) {
+  const int64_t P = (int64_t)T * k;
+  if (T <= 0 || k <= 0 || n_experts <= 0 || n_experts > RT_SMALL_E || P <= RS_CHUNK) return 0;
+  return (size_t)((P + RS_CHUNK - 1) / RS_CHUNK) * (size_t)(n_experts + 1) * sizeof(int32_t);
+}
+
 extern "C" int skcq_route_sort(const int64_t* topk, int T, int k, int n_experts, int32_t* perm, int32_t* seg,
-                               int32_t* row_of_pair, int32_t* active, void* stream) {
+                               int32_t* row_of_pair, int32_t* active, void* scratch, size_t scratch_bytes,
+                               void* stream) {
   SKCQ_REQUIRE(topk && perm && seg && row_of_pair && active, SKCQ_ERR_INVALID, "route_sort: null pointer");
   SKCQ_REQUIRE(T >= 0 && k > 0 && k <= 31 && n_experts > 0 && n_experts <= 8192, SKCQ_ERR_INVALID,
                "route_sort: bad sizes (T %d, k %d, experts %d)", T, k, n_experts);
@@ -560,6 +663,18 @@ extern "C" int skcq_route_sort(const int64_t* topk, int T, int k, int n_experts,
   int* err = device_error_word();
   SKCQ_REQUIRE(err != nullptr, SKCQ_ERR_CUDA, "route_sort: no device error word");
   const int NB = n_experts + 1;
+  const size_t need = skcq_route_sort_scratch_bytes(T, k, n_experts);
+  if (need > 0 && scratch != nullptr && scratch_bytes >= need) {
+    cudaStream_t s = (cudaStream_t)stream;
+    const int P = T * k;
+    const int chunks = (P + RS_CHUNK - 1) / RS_CHUNK;
+    int32_t* hist = static_cast<int32_t*>(scratch);
+    route_count_kernel<<<chunks, RT_THREADS, (size_t)NB * sizeof(int), s>>>(topk, T, k, n_experts, hist, err);
+    route_scan_kernel<<<1, RT_THREADS, (size_t)NB * sizeof(int), s>>>(n_experts, chunks, hist, seg, active);
+    route_scatter_kernel<<<chunks, RT_THREADS, (size_t)34 * NB * sizeof(int), s>>>(topk, T, k, n_experts, hist, perm,
+                                                                                   row_of_pair, err);
+    return check_launch("route_sort");
+  }
   size_t smem = (size_t)3 * NB * sizeof(int);
   if (n_experts <= RT_SMALL_E) smem += (size_t)32 * NB * sizeof(int);
   route_sort_kernel<<<1, RT_THREADS, smem, (cudaStream_t)stream>>>(topk, T, k, n_experts, perm, seg, row_of_pair,
