@@ -312,23 +312,23 @@ __global__ void __launch_bounds__(DQ_THREADS, 3) prefill_dequant_kernel(DqSet se
 }
 
 // Fast path for bf16 tables and up to three layers whose block sizes divide
-// the 64-column chunk (4, 8 or 16; 0 = no such layer): the chunk's columns are
+// a 32-column strip (4, 8 or 16; 0 = no such layer): the strip's columns are
 // accumulated in registers at compile-time positions, and each layer's index
-// loads are all issued before its centroid gathers, so a thread keeps a whole
-// layer's loads in flight and touches no shared memory.
-template <int BS>
+// loads are issued before its centroid gathers (8 at a time), so a thread
+// keeps a layer's loads in flight and touches no shared memory.
+template <int BS, int CW>
 __device__ __forceinline__ void dqf_layer(const skcq_fwd_layer& L, bool scaled, int e, int o, int out, int c0,
-                                          float (&acc)[PF_BK]) {
+                                          float (&acc)[CW]) {
   if constexpr (BS > 0) {
-    constexpr int NBC = PF_BK / BS;
+    constexpr int NBC = CW / BS;
     const int nb = L.n_blocks;
     const int b0 = c0 / BS;
     const __nv_bfloat16* table = static_cast<const __nv_bfloat16*>(L.table);
     const uint16_t* ix = L.idx16 + (int64_t)e * nb * out + o;
     const int cov = nb * BS;
-    // blocks per batch of loads: all of them, except 8 at a time for bs = 4
-    // (16 gathers of 4 values would not fit the register budget next to acc)
-    constexpr int G = NBC > 8 ? 8 : NBC;
+    // blocks per batch of loads: at most 16 gathered values in flight per
+    // thread, which keeps the strip's accumulators in registers
+    constexpr int G = (16 / BS) < NBC ? (16 / BS > 0 ? 16 / BS : 1) : NBC;
 #pragma unroll
     for (int g0 = 0; g0 < NBC; g0 += G) {
     int idx[G];
@@ -363,36 +363,42 @@ __device__ __forceinline__ void dqf_layer(const skcq_fwd_layer& L, bool scaled, 
   }
 }
 
+// Two threads per image row, each owning 32 of the chunk's 64 columns (half
+// the accumulator registers of one thread per row, so twice the warps fit).
+constexpr int DQF_CW = PF_BK / 2;
+
 template <int BS0, int BS1, int BS2>
-__global__ void __launch_bounds__(DQ_THREADS, 2) prefill_dequant_fast_kernel(DqSet set,
-                                                                            const int32_t* __restrict__ active,
-                                                                            int out, int in_dim, int NT, int KC,
-                                                                            int half, uint4* __restrict__ W) {
+__global__ void __launch_bounds__(2 * DQ_THREADS, 2) prefill_dequant_fast_kernel(DqSet set,
+                                                                                const int32_t* __restrict__ active,
+                                                                                int out, int in_dim, int NT, int KC,
+                                                                                int half, uint4* __restrict__ W) {
   const int n_slots = active ? active[0] : (int)(gridDim.x / NT);
   const int slot = blockIdx.x / NT, nt = blockIdx.x - slot * NT, kc = blockIdx.y;
   if (slot >= n_slots) return;
   const int e = active ? active[1 + slot] : slot;
-  const int rr = threadIdx.x + (half < 0 ? 0 : half * (PF_BN / 2));
-  const int o = half < 0 ? nt * PF_BN + rr : nt * (PF_BN / 2) + threadIdx.x;
+  const int rows = blockDim.x >> 1;  // image rows of this launch (256, or 128 per interleaved module)
+  const int strip = threadIdx.x / rows, tr = threadIdx.x - strip * rows;
+  const int rr = tr + (half < 0 ? 0 : half * (PF_BN / 2));
+  const int o = half < 0 ? nt * PF_BN + rr : nt * (PF_BN / 2) + tr;
   if (o >= out) return;  // rows past out_dim stay unwritten: their accumulator columns are never stored
-  float acc[PF_BK];
+  float acc[DQF_CW];
 #pragma unroll
-  for (int c = 0; c < PF_BK; ++c) acc[c] = 0.f;
-  const int c0 = kc * PF_BK;
+  for (int c = 0; c < DQF_CW; ++c) acc[c] = 0.f;
+  const int c0 = kc * PF_BK + strip * DQF_CW;
   if (c0 < in_dim) {
-    dqf_layer<BS0>(set.l[0], set.l[0].scales != nullptr, e, o, out, c0, acc);
-    if (set.n > 1) dqf_layer<BS1>(set.l[1], false, e, o, out, c0, acc);
-    if (set.n > 2) dqf_layer<BS2>(set.l[2], false, e, o, out, c0, acc);
+    dqf_layer<BS0, DQF_CW>(set.l[0], set.l[0].scales != nullptr, e, o, out, c0, acc);
+    if (set.n > 1) dqf_layer<BS1, DQF_CW>(set.l[1], false, e, o, out, c0, acc);
+    if (set.n > 2) dqf_layer<BS2, DQF_CW>(set.l[2], false, e, o, out, c0, acc);
 #pragma unroll
-    for (int c = 0; c < PF_BK; ++c)
+    for (int c = 0; c < DQF_CW; ++c)
       if (c0 + c >= in_dim) acc[c] = 0.f;  // K padding
   }
   uint4* chunk = W + (((int64_t)slot * NT + nt) * KC + kc) * (PF_B_BYTES / 16);
 #pragma unroll
-  for (int kg = 0; kg < 8; ++kg)
-    chunk[canon_unit(rr, kg)] =
-        make_uint4(pack_bf16x2(acc[kg * 8], acc[kg * 8 + 1]), pack_bf16x2(acc[kg * 8 + 2], acc[kg * 8 + 3]),
-                   pack_bf16x2(acc[kg * 8 + 4], acc[kg * 8 + 5]), pack_bf16x2(acc[kg * 8 + 6], acc[kg * 8 + 7]));
+  for (int q = 0; q < DQF_CW / 8; ++q)
+    chunk[canon_unit(rr, strip * (DQF_CW / 8) + q)] =
+        make_uint4(pack_bf16x2(acc[q * 8], acc[q * 8 + 1]), pack_bf16x2(acc[q * 8 + 2], acc[q * 8 + 3]),
+                   pack_bf16x2(acc[q * 8 + 4], acc[q * 8 + 5]), pack_bf16x2(acc[q * 8 + 6], acc[q * 8 + 7]));
 }
 
 using DqFastFn = void (*)(DqSet, const int32_t*, int, int, int, int, int, uint4*);
@@ -708,8 +714,8 @@ extern "C" int skcq_prefill_dequant(const skcq_fwd_layer* layers, int n_layers, 
   }
   dim3 grid((unsigned)(max_slots * NT), (unsigned)KC);
   if (DqFastFn fast = dq_fast_pick(set)) {
-    fast<<<grid, threads, 0, (cudaStream_t)stream>>>(set, active, out_dim, in_dim, NT, KC, half,
-                                                     static_cast<uint4*>(W));
+    fast<<<grid, 2 * threads, 0, (cudaStream_t)stream>>>(set, active, out_dim, in_dim, NT, KC, half,
+                                                         static_cast<uint4*>(W));
     return check_launch("prefill_dequant");
   }
   prefill_dequant_kernel<<<grid, threads, smem, (cudaStream_t)stream>>>(set, active, out_dim, in_dim, NT, KC, half,
