@@ -332,9 +332,10 @@ int skcq_swiglu(const float* gate, const float* up, int n_split, int64_t n, floa
 
 /* out[t] = sum over the token's k slots, in ascending (expert, kpos) order, of
  * (sum_s part[s][row_of_pair[kpos * T + t]]) * weights[t][kpos]
- * (codebook_experts.py:476-480). weights and out f32 | bf16. */
-int skcq_combine(const float* part, int n_split, int64_t P, const int32_t* row_of_pair, const int64_t* topk,
-                 const void* weights, int w_dtype, int T, int k, int H, void* out, int out_dtype, void* stream);
+ * (codebook_experts.py:476-480). part, weights and out f32 | bf16. */
+int skcq_combine(const void* part, int part_dtype, int n_split, int64_t P, const int32_t* row_of_pair,
+                 const int64_t* topk, const void* weights, int w_dtype, int T, int k, int H, void* out, int out_dtype,
+                 void* stream);
 
 /* ---- prefill forward on the tensor cores ------------------------------------
  * For large batches (many rows per expert) the active experts' weights are
@@ -370,9 +371,10 @@ int skcq_prefill_dequant(const skcq_fwd_layer* layers, int n_layers, const int32
                          int out_dim, int in_dim, int half, void* W, void* stream);
 
 /* y[r][o] = sum_k A[r][k] * W_slot(r)[o][k] for the rows of every planned
- * tile (f32 out, row stride y_ld; rows outside tiles untouched). */
+ * tile (fp32 accumulation; y f32 | bf16, row stride y_ld; rows outside tiles
+ * untouched). */
 int skcq_prefill_gemm(const void* A, const void* W, const int32_t* tiles, int max_tiles, int in_dim, int out_dim,
-                      float* y, int64_t y_ld, void* stream);
+                      void* y, int y_dtype, int64_t y_ld, void* stream);
 
 /* Gate and up in one GEMM (W_gate_up from skcq_prefill_dequant with half 0 and
  * 1): for every planned tile, silu(x W_gate^T) * (x W_up^T) as bf16 rows in

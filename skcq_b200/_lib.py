@@ -72,11 +72,11 @@ _SIGS: dict[str, list] = {
     "skcq_codebook_forward": [P, I, P, I, L, P, I, P, P, P, I, I, I, I, I, I, P, L, P],
     "skcq_sum_splits": [P, I, L, I, P, I, L, P],
     "skcq_swiglu": [P, P, I, L, P, P],
-    "skcq_combine": [P, I, L, P, P, P, I, I, I, I, P, I, P],
+    "skcq_combine": [P, I, I, L, P, P, P, I, I, I, I, P, I, P],
     "skcq_prefill_plan": [P, I, I, P, P],
     "skcq_prefill_pack": [I, P, I, L, P, I, P, L, I, P, I, P, P],
     "skcq_prefill_dequant": [P, I, P, I, I, I, I, P, P],
-    "skcq_prefill_gemm": [P, P, P, I, I, I, P, L, P],
+    "skcq_prefill_gemm": [P, P, P, I, I, I, P, I, L, P],
     "skcq_prefill_gemm_swiglu": [P, P, P, I, I, I, P, P],
 }
 _RESTYPES = {"skcq_reseed_scratch_bytes": C.c_size_t, "skcq_route_sort_scratch_bytes": C.c_size_t}

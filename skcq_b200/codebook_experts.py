@@ -353,17 +353,18 @@ class CodebookModule(nn.Module):
              self.out_dim, in_dim, half, ptr(W), stream())
 
     def prefill(self, A: torch.Tensor, tiles: torch.Tensor, max_tiles: int, active: torch.Tensor | None,
-                max_slots: int, n_rows: int, in_dim: int) -> torch.Tensor:
+                max_slots: int, n_rows: int, in_dim: int, out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
         """Tensor-core forward of packed rows ``A`` (skcq_prefill_pack layout):
-        decode the active experts' weights once, then one grouped GEMM.
-        Returns (n_rows, out_dim) f32."""
+        decode the active experts' weights once, then one grouped GEMM
+        (fp32 accumulation). Returns (n_rows, out_dim) in ``out_dtype``
+        (f32 or bf16)."""
         dev = A.device
         KC, NT = -(-in_dim // 64), -(-self.out_dim // 256)
         W = torch.empty(max_slots * NT * KC * 16384, dtype=torch.bfloat16, device=dev)
         self.dequant_into(W, active, max_slots, in_dim)
-        y = torch.empty(n_rows, self.out_dim, dtype=torch.float32, device=dev)
-        call("skcq_prefill_gemm", ptr(A), ptr(W), ptr(tiles), max_tiles, in_dim, self.out_dim, ptr(y), y.stride(0),
-             stream())
+        y = torch.empty(n_rows, self.out_dim, dtype=out_dtype, device=dev)
+        call("skcq_prefill_gemm", ptr(A), ptr(W), ptr(tiles), max_tiles, in_dim, self.out_dim, ptr(y),
+             _DTYPE[out_dtype], y.stride(0), stream())
         return y
 
     def forward(self, hidden_states: torch.Tensor, expert_idx: int) -> torch.Tensor:
@@ -493,8 +494,8 @@ class CodebookExperts(nn.Module):
             inter.copy_(self.intermediate(gs, us))
         d, Sd = self.down.run_segments(inter, seg, None, E, **seg_kw)
         out = torch.empty(T, H, dtype=h.dtype, device=dev)
-        call("skcq_combine", ptr(d), Sd, P, ptr(inv), ptr(topk), ptr(w), _DTYPE[w.dtype], T, k, H, ptr(out),
-             _DTYPE[out.dtype], stream())
+        call("skcq_combine", ptr(d), _DTYPE[d.dtype], Sd, P, ptr(inv), ptr(topk), ptr(w), _DTYPE[w.dtype], T, k, H,
+             ptr(out), _DTYPE[out.dtype], stream())
         if self.check_errors:
             _lib.poll_device_error()
         return out.to(device=hidden_states.device, dtype=hidden_states.dtype)
@@ -535,10 +536,11 @@ class CodebookExperts(nn.Module):
             call("skcq_prefill_pack", 0, ptr(inter), _DTYPE[torch.float32], inter.stride(0), None, 0, None, 0, I,
                  ptr(tiles), max_tiles, ptr(A2), stream())
         del A
-        d = self.down.prefill(A2, tiles, max_tiles, active, max_active, P, I)
+        # bf16 down outputs, as the reference's bf16 module produces them
+        d = self.down.prefill(A2, tiles, max_tiles, active, max_active, P, I, out_dtype=torch.bfloat16)
         out = torch.empty(T, H, dtype=h.dtype, device=dev)
-        call("skcq_combine", ptr(d), 1, P, ptr(inv), ptr(topk), ptr(w), _DTYPE[w.dtype], T, k, H, ptr(out),
-             _DTYPE[out.dtype], stream())
+        call("skcq_combine", ptr(d), _DTYPE[d.dtype], 1, P, ptr(inv), ptr(topk), ptr(w), _DTYPE[w.dtype], T, k, H,
+             ptr(out), _DTYPE[out.dtype], stream())
         return out
 
 

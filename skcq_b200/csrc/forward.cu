@@ -560,7 +560,8 @@ __global__ void swiglu_kernel(const float* __restrict__ g, const float* __restri
 // shared memory, then the threads stream the token's k rows over h.
 constexpr int CB_THREADS = 256;
 
-__global__ void __launch_bounds__(CB_THREADS) combine_kernel(const float* __restrict__ part, int n_split, int64_t P,
+__global__ void __launch_bounds__(CB_THREADS) combine_kernel(const void* __restrict__ part, int part_dtype,
+                                                             int n_split, int64_t P,
                                                              const int32_t* __restrict__ row_of_pair,
                                                              const int64_t* __restrict__ topk, const void* __restrict__ w,
                                                              int w_dtype, int T, int k, int H, void* __restrict__ out,
@@ -591,7 +592,9 @@ __global__ void __launch_bounds__(CB_THREADS) combine_kernel(const float* __rest
     for (int h = blockIdx.y * CB_THREADS + threadIdx.x; h < H; h += gridDim.y * CB_THREADS) {
       float acc = 0.f;
       for (int step = 0; step < k; ++step) {
-        const float y = sum_parts(part, n_split, stride, (int64_t)s_row[step] * H + h);
+        const int64_t i = (int64_t)s_row[step] * H + h;
+        float y = ld_any(part, i, part_dtype);
+        for (int sp = 1; sp < n_split; ++sp) y += ld_any(part, sp * stride + i, part_dtype);
         acc = __fadd_rn(acc, __fmul_rn(y, s_w[step]));
       }
       st_any(out, (int64_t)t * H + h, out_dtype, acc);
@@ -772,10 +775,12 @@ extern "C" int skcq_swiglu(const float* gate, const float* up, int n_split, int6
   return check_launch("swiglu");
 }
 
-extern "C" int skcq_combine(const float* part, int n_split, int64_t P, const int32_t* row_of_pair, const int64_t* topk,
-                            const void* weights, int w_dtype, int T, int k, int H, void* out, int out_dtype,
-                            void* stream) {
+extern "C" int skcq_combine(const void* part, int part_dtype, int n_split, int64_t P, const int32_t* row_of_pair,
+                            const int64_t* topk, const void* weights, int w_dtype, int T, int k, int H, void* out,
+                            int out_dtype, void* stream) {
   SKCQ_REQUIRE(part && row_of_pair && topk && weights && out, SKCQ_ERR_INVALID, "combine: null pointer");
+  SKCQ_REQUIRE(part_dtype == SKCQ_DTYPE_F32 || part_dtype == SKCQ_DTYPE_BF16, SKCQ_ERR_INVALID,
+               "combine: partial-sum dtype %d", part_dtype);
   SKCQ_REQUIRE(k > 0 && k <= 31 && n_split >= 1, SKCQ_ERR_INVALID, "combine: top-k %d, %d splits", k, n_split);
   SKCQ_REQUIRE(w_dtype == SKCQ_DTYPE_F32 || w_dtype == SKCQ_DTYPE_BF16, SKCQ_ERR_INVALID, "combine: weight dtype %d",
                w_dtype);
@@ -786,7 +791,8 @@ extern "C" int skcq_combine(const float* part, int n_split, int64_t P, const int
   int gy = ceil_div(H, CB_THREADS);
   const int want_y = ceil_div(148 * 4, gx);
   if (gy > want_y) gy = want_y;
-  combine_kernel<<<dim3(gx, gy), CB_THREADS, 0, (cudaStream_t)stream>>>(part, n_split, P, row_of_pair, topk, weights,
-                                                                        w_dtype, T, k, H, out, out_dtype);
+  combine_kernel<<<dim3(gx, gy), CB_THREADS, 0, (cudaStream_t)stream>>>(part, part_dtype, n_split, P, row_of_pair,
+                                                                        topk, weights, w_dtype, T, k, H, out,
+                                                                        out_dtype);
   return check_launch("combine");
 }

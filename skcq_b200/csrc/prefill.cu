@@ -449,7 +449,8 @@ struct GemmArgs {
   const uint8_t* W;  // [slots][NT][KC] 32 KB chunks
   const int32_t* tiles;
   int KC, NT, out;
-  float* y;  // mode 0: f32 rows
+  void* y;  // mode 0: rows, f32 or bf16 (y_dtype)
+  int y_dtype;
   int64_t y_ld;
   uint4* a_out;  // mode 1: SwiGLU rows in the A image ([max_tiles][KC_out] chunks)
   int KC_out;
@@ -597,7 +598,10 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_gemm_kernel(GemmArgs g)
         }
       } else {
         const int row = row0 + r;
-        float* yr = g.y + (int64_t)row * g.y_ld + (int64_t)nt * PF_BN;
+        const int64_t y0 = (int64_t)row * g.y_ld + (int64_t)nt * PF_BN;
+        float* yr = static_cast<float*>(g.y) + y0;
+        uint16_t* yh = static_cast<uint16_t*>(g.y) + y0;
+        const bool bf = g.y_dtype == SKCQ_DTYPE_BF16;
         const int ncol = min(PF_BN, g.out - nt * PF_BN);
         for (int j = 0; j < PF_BN / 32; ++j) {
           float v[32];
@@ -609,7 +613,21 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_gemm_kernel(GemmArgs g)
             if (lane == 0) mbar_arrive(acc_empty + ab);
           }
           if (row < row1) {
-            if (j * 32 + 32 <= ncol && (g.y_ld & 3) == 0) {
+            if (bf) {
+              if (j * 32 + 32 <= ncol && (g.y_ld & 7) == 0) {
+#pragma unroll
+                for (int c = 0; c < 32; c += 8)
+                  *reinterpret_cast<uint4*>(yh + j * 32 + c) =
+                      make_uint4(pack_bf16x2(v[c], v[c + 1]), pack_bf16x2(v[c + 2], v[c + 3]),
+                                 pack_bf16x2(v[c + 4], v[c + 5]), pack_bf16x2(v[c + 6], v[c + 7]));
+              } else {
+                for (int c = 0; c < 32; ++c)
+                  if (j * 32 + c < ncol) {
+                    const __nv_bfloat16 hv = __float2bfloat16_rn(v[c]);
+                    yh[j * 32 + c] = *reinterpret_cast<const uint16_t*>(&hv);
+                  }
+              }
+            } else if (j * 32 + 32 <= ncol && (g.y_ld & 3) == 0) {
 #pragma unroll
               for (int c = 0; c < 32; c += 4)
                 *reinterpret_cast<float4*>(yr + j * 32 + c) = make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]);
@@ -737,8 +755,10 @@ static int gemm_configure() {
 }
 
 extern "C" int skcq_prefill_gemm(const void* A, const void* W, const int32_t* tiles, int max_tiles, int in_dim,
-                                 int out_dim, float* y, int64_t y_ld, void* stream) {
+                                 int out_dim, void* y, int y_dtype, int64_t y_ld, void* stream) {
   SKCQ_REQUIRE(A && W && tiles && y, SKCQ_ERR_INVALID, "prefill_gemm: null pointer");
+  SKCQ_REQUIRE(y_dtype == SKCQ_DTYPE_F32 || y_dtype == SKCQ_DTYPE_BF16, SKCQ_ERR_INVALID,
+               "prefill_gemm: output dtype %d", y_dtype);
   SKCQ_REQUIRE(((uintptr_t)A & 15) == 0 && ((uintptr_t)W & 15) == 0, SKCQ_ERR_INVALID,
                "prefill_gemm: operands must be 16-byte aligned");
   SKCQ_REQUIRE(max_tiles > 0 && max_tiles <= 65535 && in_dim > 0 && out_dim > 0, SKCQ_ERR_INVALID,
@@ -748,7 +768,7 @@ extern "C" int skcq_prefill_gemm(const void* A, const void* W, const int32_t* ti
   const int rc = gemm_configure();
   if (rc != SKCQ_OK) return rc;
   GemmArgs g{static_cast<const uint8_t*>(A), static_cast<const uint8_t*>(W), tiles, ceil_div(in_dim, PF_BK),
-             ceil_div(out_dim, PF_BN), out_dim, y, y_ld, nullptr, 0, err};
+             ceil_div(out_dim, PF_BN), out_dim, y, y_dtype, y_ld, nullptr, 0, err};
   const int64_t items = (int64_t)max_tiles * g.NT;
   const int grid = (int)std::min<int64_t>(items, num_sms_cached());
   prefill_gemm_kernel<0><<<grid, PF_THREADS, PF_SMEM, (cudaStream_t)stream>>>(g);
@@ -767,7 +787,7 @@ extern "C" int skcq_prefill_gemm_swiglu(const void* A, const void* W_gate_up, co
   const int rc = gemm_configure();
   if (rc != SKCQ_OK) return rc;
   GemmArgs g{static_cast<const uint8_t*>(A), static_cast<const uint8_t*>(W_gate_up), tiles, ceil_div(in_dim, PF_BK),
-             ceil_div(inter_dim, PF_BN / 2), inter_dim, nullptr, 0, static_cast<uint4*>(A_out),
+             ceil_div(inter_dim, PF_BN / 2), inter_dim, nullptr, SKCQ_DTYPE_F32, 0, static_cast<uint4*>(A_out),
              ceil_div(inter_dim, PF_BK), err};
   const int64_t items = (int64_t)max_tiles * g.NT;
   const int grid = (int)std::min<int64_t>(items, num_sms_cached());
