@@ -296,6 +296,22 @@ class CodebookModule(nn.Module):
         module.load_state_dict(data["state_dict"])
         return module
 
+    def slice_experts(self, e0: int, e1: int) -> CodebookModule:
+        """A module for experts [e0, e1) only: per-expert buffers (assignments,
+        scales, remainder, signs) sliced, per-block codebooks shared. Used for
+        expert-parallel placement."""
+        layers = []
+        for lay in self.layers:
+            q = getattr(lay, "scale_q_scale", None)
+            layers.append(_CodebookLayer(
+                lay.codebook.detach(), lay.assignments[e0:e1], lay.n_blocks, lay.block_size, lay.out_dim, lay.k,
+                remainder=lay.remainder[e0:e1],
+                signs=lay.signs[e0:e1] if lay.signs is not None else None,
+                scales=lay.scales.detach()[e0:e1] if lay.has_scale and lay.scales is not None else None,
+                scale_q_scale=q,
+            ))
+        return CodebookModule(nn.ModuleList(layers), self.n_codebooks, self.out_dim)
+
     def _all_layers(self) -> list[_CodebookLayer]:
         return list(self.layers)
 

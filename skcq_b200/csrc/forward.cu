@@ -570,22 +570,18 @@ __global__ void __launch_bounds__(CB_THREADS) combine_kernel(const void* __restr
   __shared__ float s_w[32];
   const int64_t stride = P * H;
   for (int t = blockIdx.x; t < T; t += gridDim.x) {
-    if (threadIdx.x == 0) {
-      uint32_t done = 0;
-      for (int step = 0; step < k; ++step) {
-        int best = -1;
-        int64_t be = 0;
-        for (int kp = 0; kp < k; ++kp) {
-          if (done >> kp & 1u) continue;
-          const int64_t e = topk[(int64_t)t * k + kp];
-          if (best < 0 || e < be) {
-            best = kp;
-            be = e;
-          }
-        }
-        done |= 1u << best;
-        s_row[step] = row_of_pair[(int64_t)best * T + t];
-        s_w[step] = ld_any(w, (int64_t)t * k + best, w_dtype);
+    if (threadIdx.x < 32) {
+      // lane kp ranks its slot by (expert, kpos) among the token's k slots
+      const int lane = threadIdx.x;
+      const int64_t e = lane < k ? topk[(int64_t)t * k + lane] : INT64_MAX;
+      int rank = 0;
+      for (int j = 0; j < k; ++j) {
+        const int64_t ej = __shfl_sync(0xffffffffu, e, j);
+        rank += (ej < e || (ej == e && j < lane)) ? 1 : 0;
+      }
+      if (lane < k) {
+        s_row[rank] = row_of_pair[(int64_t)lane * T + t];
+        s_w[rank] = ld_any(w, (int64_t)t * k + lane, w_dtype);
       }
     }
     __syncthreads();

@@ -1,0 +1,81 @@
+"""Expert-parallel CodebookExperts (skcq_b200/expert_parallel.py) against the
+single-process forward on the same tokens: two gloo ranks sharing one GPU (no
+kernel waits on another rank), fp32 small batch (gather kernels) and bf16
+large batch (tensor-core prefill on each rank)."""
+
+from __future__ import annotations
+
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _module(E, out_dim, in_dim, seed, dtype):
+    from skcq_b200.codebook_experts import CodebookModule, _CodebookLayer
+
+    g = torch.Generator().manual_seed(seed)
+    layers = []
+    for i, (bs, K) in enumerate([(8, 64), (4, 256)]):
+        nb = in_dim // bs
+        layers.append(_CodebookLayer(
+            (torch.randn(nb, bs, K, generator=g) * 0.05).to(dtype), torch.randint(0, K, (E, nb, out_dim), generator=g),
+            nb, bs, out_dim, K, scales=(torch.rand(E, nb, out_dim, generator=g) * 0.1).to(dtype) if i == 0 else None))
+    return CodebookModule(torch.nn.ModuleList(layers), len(layers), out_dim).cuda()
+
+
+def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
+    import torch.distributed as dist
+
+    from skcq_b200.codebook_experts import CodebookExperts
+    from skcq_b200.expert_parallel import ExpertParallelExperts
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(0)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        res = {}
+        for name, dtype, T, k in (("f32_small", torch.float32, 5, 2), ("bf16_large", torch.bfloat16, 2048, 2)):
+            E, H, I = 8, 64, 32
+            mods = [_module(E, I, H, 1, dtype), _module(E, I, H, 2, dtype), _module(E, H, I, 3, dtype)]
+            full = CodebookExperts(*mods, E, torch.nn.functional.silu)
+            ep = ExpertParallelExperts(*mods, E, torch.nn.functional.silu)
+            g = torch.Generator().manual_seed(100 + rank)  # each rank has its own tokens
+            x = torch.randn(T, H, generator=g).to(dtype).cuda()
+            topi = torch.rand(T, E, generator=g).argsort(-1)[:, :k].cuda()
+            topw = torch.rand(T, k, generator=g).cuda()
+            y_ep = ep(x, topi, topw).double()
+            y_ref = full(x, topi, topw).double()
+            cos = torch.nn.functional.cosine_similarity(y_ep.flatten(), y_ref.flatten(), dim=0).item()
+            res[name] = ((y_ep - y_ref).abs().max().item() / y_ref.abs().max().item(), cos)
+        # a rank with no tokens still takes part in the collectives
+        x0 = torch.empty(0 if rank == 1 else 3, 64).cuda()
+        t0 = torch.zeros(x0.shape[0], 2, dtype=torch.int64).cuda()
+        t0[:, 1] = 5
+        y0 = ep(x0, t0, torch.ones(x0.shape[0], 2).cuda())
+        res["empty_ok"] = y0.shape == x0.shape and bool(torch.isfinite(y0).all())
+        torch.save(res, os.path.join(out_dir, f"ep{rank}.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_expert_parallel_matches_single_process(tmp_path):
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    import torch.multiprocessing as mp
+
+    mp.spawn(_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    for r in range(2):
+        res = torch.load(tmp_path / f"ep{r}.pt")
+        assert res["f32_small"][0] < 1e-5 and res["f32_small"][1] > 0.999999, res
+        assert res["bf16_large"][0] < 1e-2 and res["bf16_large"][1] > 0.9999, res
+        assert res["empty_ok"]
