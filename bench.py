@@ -318,6 +318,46 @@ def measured_peaks() -> tuple[dict, str]:
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
+def ep_forward_bench(wl: dict, world: int, rank: int, dev: str, iters: int = 3) -> dict:
+    """Config-5 prefill expert-parallel over the ranks: 16384 tokens in all
+    (16384 / world per rank), top-8 with Zipf(1.1) expert load, experts split
+    across ranks, NCCL all-to-all dispatch and return. The modules carry the
+    layer's codebook shapes with random centroids and uniform indices (built
+    identically on every rank); max over ranks of the device time."""
+    from skcq_b200.expert_parallel import ExpertParallelExperts
+    from skcq_b200.kernel_bench import _random_module
+
+    E, H, I = wl["experts"], wl["hidden"], wl["inter"]
+    g = torch.Generator(device=dev).manual_seed(777)
+    mods = [_random_module(E, I, H, g), _random_module(E, I, H, g), _random_module(E, H, I, g)]
+    ep = ExpertParallelExperts(*mods, E, torch.nn.functional.silu)
+    T_all = 16384
+    T = T_all // world
+    gt = torch.Generator(device=dev).manual_seed(1000 + rank)
+    ranks = torch.randperm(E, generator=torch.Generator(device=dev).manual_seed(4321), device=dev).float() + 1
+    u = torch.rand(T, E, generator=gt, device=dev).clamp_(1e-20, 1)
+    topw, topi = torch.topk(torch.softmax(-1.1 * torch.log(ranks)[None] - torch.log(-torch.log(u)), -1), 8, dim=-1)
+    x = torch.randn(T, H, generator=gt, device=dev).to(torch.bfloat16)
+    for _ in range(2):
+        ep(x, topi, topw)
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(iters):
+        barrier(world)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        ep(x, topi, topw)
+        b.record()
+        torch.cuda.synchronize()
+        ts.append(max_over_ranks(a.elapsed_time(b), world))
+    ms = statistics.median(ts)
+    del ep, mods
+    torch.cuda.empty_cache()
+    return {"tokens": T_all, "tokens_per_rank": T, "experts_per_rank": E // world, "ms": ms,
+            "tokens_per_s": T_all / (ms / 1e3), "dispatch": "NCCL all_to_all_single (rows bf16, ids, counts)",
+            "codebooks": "random centroids, uniform indices, config-2 shapes"}
+
+
 # ---------------------------------------------------------------------------
 # CPU leg: the oracle port on a bounded sample of the same workload
 # ---------------------------------------------------------------------------
@@ -557,6 +597,11 @@ def main() -> None:
     if not args.no_forward and not args.no_e2e and fits and not rows_mode:
         fwd = forward_bench(wl, fits, dev, peaks)
         fits.clear()
+    fwd_ep = None
+    if not args.no_forward and world > 1:
+        fits.clear()
+        torch.cuda.empty_cache()
+        fwd_ep = ep_forward_bench(wl, world, rank, dev)
     a = ksum.get("assign", {"ms": 0.0, "work": 0.0, "launches": 0, "padded": 0.0})
     achieved = a["work"] / (a["ms"] / 1e3) / 1e12 if a["ms"] > 0 else 0.0
     issued = a["padded"] / (a["ms"] / 1e3) / 1e12 if a["ms"] > 0 else 0.0
@@ -585,6 +630,7 @@ def main() -> None:
             "block_iters_per_step": total_block_iters / args.steps,
             "roofline": roofline, "clocks": clocks.summary(), "gpu_launches": launches, "e2e": e2e,
             "forward": fwd,
+            "forward_expert_parallel": fwd_ep,
         }
         if not args.no_cpu and world == 1:
             line["cpu_baseline"] = {k: v for k, v in cpu_rate(wl).items() if k != "est_layer_s"}
