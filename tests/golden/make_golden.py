@@ -265,6 +265,48 @@ def case_config1(out: Path, cb, bpw_mod) -> None:
     print(f"config1: rel_fro_err={rel:.5f} bpw={bpw:.3f}")
 
 
+VQ_SPECS = [
+    # name, projection, block_size, K, n_codebooks, metric, residual_k, residual_sign_split, shared, sign_split,
+    # max_iters, scale_dtype, residual_block_sizes, codebook_bits
+    ("cos_int8", "gate", 4, 16, 2, "cosine", 8, None, False, True, 8, "int8", None, 8),
+    ("euc_shared", "down", 4, 16, 2, "euclidean", 8, True, True, False, 8, "bf16", 6, 16),
+]
+
+
+def case_vq(out: Path, vq_experiment, vq_runner) -> None:
+    """The sweep runner (skcq/vq/experiment.py VQRunExperiment.fit) on two small
+    configurations, and the integer / fp8 baselines (skcq/vq/runner.py)."""
+    res = {}
+    torch.manual_seed(41)
+    w = torch.randn(64, 40) * 0.05
+    res["int_w"] = w.numpy()
+    for name, fn in vq_runner.integer_schemes(8):
+        recon, bpw = fn(w.clone())
+        res[f"int__{name}__recon"] = recon.float().numpy()
+        res[f"int__{name}__bpw"] = np.array([bpw])
+    for (name, proj, bs, K, ncb, metric, rk, rss, shared, ss, iters, sdt, rbs, cbits) in VQ_SPECS:
+        torch.manual_seed(43)
+        E, H, I = 4, 16, 8
+        rows, in_dim = (E * I, H) if proj != "down" else (E * H, I + 6)
+        w = torch.randn(rows, in_dim) * 0.1
+        cfg = vq_experiment.VQRunConfig(
+            projection=proj, in_dim=in_dim, num_experts=E, hidden_size=H, intermediate_size=I, block_size=bs, K=K,
+            n_codebooks=ncb, metric=metric, residual_k=rk, residual_sign_split=rss, shared_codebook=shared,
+            sign_split=ss, max_iters=iters, scale_dtype=sdt, residual_block_sizes=rbs, codebook_bits=cbits,
+            layer_idx=3, device=torch.device("cpu"), chunk_budget_mb=64)
+        with RandpermRecorder() as rec:
+            row = vq_experiment.VQRunExperiment(cfg).fit(w)
+        res[f"vq__{name}__w"] = w.numpy()
+        res[f"vq__{name}__err"] = np.array([row["rel_fro_err"]])
+        res[f"vq__{name}__bpw"] = np.array([row["bits_per_weight"]])
+        res[f"vq__{name}__scheme"] = np.array([row["scheme"]])
+        res[f"vq__{name}__rbs"] = np.array(row["residual_block_sizes"], dtype=np.int64)
+        for kk, v in pack_perms(rec.perms).items():
+            res[f"vq__{name}__{kk}"] = v
+        print(f"vq {name}: {row['scheme']} err={row['rel_fro_err']:.5f} bpw={row['bits_per_weight']:.3f}")
+    np.savez_compressed(out / "vq.npz", **res)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
@@ -277,8 +319,10 @@ def main() -> None:
     import skcq.codebook.kmeans as km
     import skcq.codebook_experts as experts_mod
     import skcq.vq.bpw as bpw_mod
+    import skcq.vq.experiment as vq_experiment
+    import skcq.vq.runner as vq_runner
 
-    todo = args.only.split(",") if args.only else ["assign", "kmeans", "codecs", "experts", "config1"]
+    todo = args.only.split(",") if args.only else ["assign", "kmeans", "codecs", "experts", "config1", "vq"]
     if "assign" in todo:
         case_assign(HERE, km)
     if "kmeans" in todo:
@@ -289,6 +333,8 @@ def main() -> None:
         case_experts(HERE, cb, experts_mod)
     if "config1" in todo:
         case_config1(HERE, cb, bpw_mod)
+    if "vq" in todo:
+        case_vq(HERE, vq_experiment, vq_runner)
 
 
 if __name__ == "__main__":
