@@ -34,7 +34,11 @@ from skcq_b200.distributed import expert_row_range
 
 
 class ExpertParallelExperts(torch.nn.Module):
-    """``CodebookExperts.forward`` semantics with experts placed across ranks."""
+    """``CodebookExperts.forward`` semantics with experts placed across ranks.
+    ``check_errors`` (default on) reads the device error word once at the end
+    of each call, so an expert id outside [0, num_experts) raises."""
+
+    check_errors: bool = True
 
     def __init__(self, gate: CodebookModule, up: CodebookModule, down: CodebookModule, num_experts: int,
                  act_fn: Callable[[torch.Tensor], torch.Tensor], group: dist.ProcessGroup | None = None) -> None:
@@ -78,11 +82,14 @@ class ExpertParallelExperts(torch.nn.Module):
         if w.dtype not in (torch.float32, torch.bfloat16):
             w = w.float()
         w = w.contiguous()
-        if P and (int(topk.min()) < 0 or int(topk.max()) >= self.num_experts):
-            raise RuntimeError(f"expert index outside [0, {self.num_experts})")
         # 1. pairs in pair order p = kpos * T + token, grouped by destination rank
+        # (an id outside [0, E) is routed by its clamped value and then flagged
+        # by the owning rank's route sort, raising at the end of the call)
         expert = topk.t().reshape(-1)
-        dest = self.owner.to(dev)[expert]
+        if P:  # the sender flags its own out-of-range ids too (no host sync)
+            chk = torch.empty(P, dtype=torch.int16, device=dev)
+            call("skcq_pack_indices16", ptr(topk), P, self.num_experts, ptr(chk), stream())
+        dest = self.owner.to(dev)[expert.clamp(0, self.num_experts - 1)]
         order = torch.sort(dest, stable=True).indices
         send_counts = torch.bincount(dest, minlength=self.world)
         # 2. counts, then rows and expert ids
@@ -101,7 +108,6 @@ class ExpertParallelExperts(torch.nn.Module):
         if n_recv:
             ones = torch.ones(n_recv, 1, dtype=torch.float32, device=dev)
             y = self.local(recv_rows, (recv_ids - self.e0)[:, None], ones)
-            _lib.poll_device_error()
         else:
             y = torch.empty(0, H, dtype=h.dtype, device=dev)
         # 4. outputs back, then the weighted combine in (expert, kpos) order
@@ -116,4 +122,6 @@ class ExpertParallelExperts(torch.nn.Module):
                  _DTYPE[w.dtype], T, k, H, ptr(out), _DTYPE[out.dtype], stream())
         else:
             out.zero_()
+        if self.check_errors:
+            _lib.poll_device_error()
         return out.to(device=hidden_states.device, dtype=hidden_states.dtype)

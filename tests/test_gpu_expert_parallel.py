@@ -63,6 +63,15 @@ def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
         t0[:, 1] = 5
         y0 = ep(x0, t0, torch.ones(x0.shape[0], 2).cuda())
         res["empty_ok"] = y0.shape == x0.shape and bool(torch.isfinite(y0).all())
+        # an expert id outside [0, E) raises (after the collectives, on the owning rank's flag)
+        bad = torch.zeros(2, 2, dtype=torch.int64).cuda()
+        bad[:, 1] = 1
+        bad[0, 0] = 9 if rank == 0 else 0
+        try:
+            ep(torch.randn(2, 64).cuda(), bad, torch.ones(2, 2).cuda())
+            res["raised"] = False
+        except RuntimeError:
+            res["raised"] = True
         torch.save(res, os.path.join(out_dir, f"ep{rank}.pt"))
     finally:
         dist.destroy_process_group()
@@ -79,3 +88,6 @@ def test_expert_parallel_matches_single_process(tmp_path):
         assert res["f32_small"][0] < 1e-5 and res["f32_small"][1] > 0.999999, res
         assert res["bf16_large"][0] < 1e-2 and res["bf16_large"][1] > 0.9999, res
         assert res["empty_ok"]
+    # the id 9 of rank 0 is flagged by rank 0 itself and, clamped to expert 7,
+    # by its owner rank 1
+    assert torch.load(tmp_path / "ep0.pt")["raised"] and torch.load(tmp_path / "ep1.pt")["raised"]
