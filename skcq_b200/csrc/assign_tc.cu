@@ -1,16 +1,31 @@
 // Nearest-centroid assignment on the 5th-generation tensor cores
 // (skcq/codebook/kmeans.py:25-66, assign_cosine / assign_l2).
 //
-// Kernel 1 -- one persistent CTA per SM, warp-specialised:
-//   warp 0      producer: 1-D bulk copies (TMA engine) of the point tile
-//               (256 points, double buffered across work units) and a ring
-//               of centroid tiles (128 centroids each, up to 16 deep);
-//   warp 1      issues tcgen05.mma kind::tf32 (M=128, N=128, K=8) into one of
-//               two tensor-memory accumulator sets (double buffered);
-//   warps 2-17  epilogue: tcgen05.ld 64 columns of the fp32 scores of one
-//               (row tile, lane quarter), release the accumulator, then keep
-//               a running (best value, best group of 32 centroids) per point
+// Kernel 1 (packed widths of at most two MMA k-steps, kp <= 16: l2 with
+// bs <= 4, cosine with bs <= 5; wider ones run the shared-memory-operand form
+// in assign_ss.cu) -- one persistent CTA per SM, warp-specialised:
+//   warp 0      producer: 1-D bulk copies (TMA engine) of the work unit's
+//               256 points and a ring of centroid tiles (N = 224 centroids);
+//   warp 1      issues the tensor-core work: at the start of each unit
+//               tcgen05.cp moves the two 128-point row tiles from shared into
+//               tensor memory, then for every centroid tile one chain of
+//               tcgen05.mma kind::tf32 (M=128, N, K=8, A from tensor memory,
+//               B from shared memory) per row tile;
+//   warps 2-17  epilogue: 8 warps per row tile tcgen05.ld the fp32 scores of
+//               their (lane quarter, column half) two groups of 32 at a time,
+//               release the accumulator after the last read, and keep a
+//               running (best value, best group of 32 centroids) per point
 //               with 3-input max; the distance matrix never leaves the SM.
+// Tensor memory holds one accumulator per row tile and the two A tiles. The
+// row tiles alternate: while the epilogue drains one accumulator the tensor
+// core fills the other, so an accumulator's turnaround (MMA completion,
+// epilogue read, release) overlaps the other row tile's chain. Wide N keeps
+// each MMA long enough to run near the tensor pipe's rate (N=128
+// instructions at K=8 run at about a third of it), and A in tensor memory
+// halves the shared-memory operand traffic. tcgen05.mma issue blocks the
+// issuing thread until the tensor core accepts the instruction, so the MMA
+// thread checks the next tile's operands between the two row-tile chains,
+// while the tensor core is busy, not after both.
 // Operands are split-tf32 (hi/lo) so A.B reproduces the fp32 dot product to
 // ~2^-21 relative.
 // Kernel 2 -- refine: one thread per point re-scores the 32 centroids of its
@@ -18,6 +33,7 @@
 // reading the problem's centroid table from shared-memory slices.
 #include <algorithm>
 
+#include "assign_ss.cuh"
 #include "common.cuh"
 
 namespace skcq {
@@ -25,18 +41,26 @@ namespace skcq {
 constexpr int TC_BM = 128;                       // points per MMA (TMEM lanes)
 constexpr int TC_RT = 2;                         // row tiles per work unit
 constexpr int TC_ROWS = TC_BM * TC_RT;           // points per work unit
-constexpr int TC_BN = 128;                       // centroids per tile
 constexpr int TC_STAGES = 16;                    // max centroid tile ring depth (as many as shared memory holds)
-constexpr int TC_ABUF = 2;                       // point tiles in flight (next unit loads during this one)
 constexpr int TC_EPI_WARPS = 8 * TC_RT;          // one warp per (row tile, lane quarter, column half)
 constexpr int TC_THREADS = (2 + TC_EPI_WARPS) * 32;
-constexpr int TC_TMEM_COLS = 2 * TC_RT * TC_BN;  // 512: two accumulator sets
+constexpr int TC_TMEM_COLS = 512;                // accumulators (2 x N) + A tiles (2 x kp)
 constexpr size_t TC_MIN_SMEM = 116 * 1024;       // keeps one CTA (and one TMEM owner) per SM
-constexpr int TC_MAX_KSTEPS = 8;                 // kp <= 64: bs <= 20 (l2) / 21 (cosine)
+constexpr int TC_MAX_KSTEPS = 8;                 // kp <= 64 (both forms): bs <= 20 (l2) / 21 (cosine)
 constexpr int GROUP = 32;                        // centroids per re-scored group
 
+// This form serves packed widths of at most TC_TS_MAX_KSTEPS MMA k-steps
+// (kp <= 16); wider ones go to the shared-memory-operand form in
+// assign_ss.cu, which measured faster once a tile's MMA chain is long.
+constexpr int TC_TS_MAX_KSTEPS = 2;
+// Centroids per tile: the widest N (a multiple of 32) with 2 N + 2 kp <= 512
+// tensor-memory columns.
+constexpr int TC_BN = 224;
+__host__ __device__ constexpr int tc_tile_n(int) { return TC_BN; }
+
 static_assert(TC_ROWS == SKCQ_ROWS_PER_UNIT, "work unit size is part of the ABI");
-static_assert(TC_BN == SKCQ_CENT_TILE, "centroid tile size is part of the ABI");
+static_assert(2 * TC_BN + 2 * 8 * TC_TS_MAX_KSTEPS <= TC_TMEM_COLS, "accumulators and A tiles must fit tensor memory");
+static_assert(TC_BN % GROUP == 0, "tiles hold whole groups");
 
 struct TcParams {
   const float* A;  // [nblk][n_pad/8][kp/4][8][4]
@@ -56,10 +80,10 @@ struct TcSmem {
   uint64_t* a_empty;
   uint64_t* b_full;
   uint64_t* b_empty;
-  uint64_t* acc_full;
-  uint64_t* acc_empty;
+  uint64_t* acc_full;   // [TC_RT]
+  uint64_t* acc_empty;  // [TC_RT]
   uint32_t* tmem_slot;
-  uint32_t a_bytes, b_bytes;
+  uint32_t a_bytes, b_stage_bytes;
 };
 
 __device__ __forceinline__ bool unit_live(const TcParams& p, int64_t u, int upb, int* b, int* r0) {
@@ -82,25 +106,48 @@ struct Ring {
   }
 };
 
+// D(tmem) (+)= A(tmem) * B(smem desc), kind::tf32, fp32 accumulate.
+__device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// 128 rows x 256 bits (eight fp32 columns) of a no-swizzle K-major shared
+// image into tensor memory, row i to lane i. Ordered before later
+// tcgen05.mma issued by the same thread.
+__device__ __forceinline__ void tmem_cp_128x256b(uint32_t taddr, uint64_t s_desc) {
+  asm volatile("tcgen05.cp.cta_group::1.128x256b [%0], %1;" ::"r"(taddr), "l"(s_desc) : "memory");
+}
+
+template <int KSTEPS>
 __device__ void tc_producer(const TcParams& p, const TcSmem& s) {
+  constexpr int N = tc_tile_n(KSTEPS);
   const int upb = p.n_pad / TC_ROWS;
   const int64_t n_units = (int64_t)p.nblk * upb;
-  const uint32_t b_floats = (uint32_t)TC_BN * p.kp;
+  const int64_t tile_floats = (int64_t)N * p.kp;
   Ring ar, br;
   for (int64_t u = blockIdx.x; u < n_units; u += gridDim.x) {
     int b, r0;
     if (!unit_live(p, u, upb, &b, &r0)) continue;
-    const int nbt = ceil_div(p.k[b], TC_BN);
-    if (!mbar_wait(s.a_empty + ar.idx, ar.phase ^ 1, p.err, 11)) return;
-    mbar_arrive_expect_tx(s.a_full + ar.idx, s.a_bytes);
-    bulk_g2s(s.a + ar.idx * (TC_ROWS * p.kp), p.A + ((int64_t)b * p.n_pad + r0) * p.kp, s.a_bytes,
-             s.a_full + ar.idx);
-    ar.next(TC_ABUF);
+    const int nbt = ceil_div(p.k[b], N);
+    if (!mbar_wait(s.a_empty, ar.phase ^ 1, p.err, 11)) return;
+    mbar_arrive_expect_tx(s.a_full, s.a_bytes);
+    bulk_g2s(s.a, p.A + ((int64_t)b * p.n_pad + r0) * p.kp, s.a_bytes, s.a_full);
+    ar.next(1);
     const float* bsrc = p.B + (int64_t)b * p.k_pad * p.kp;
-    for (int j = 0; j < nbt; ++j, bsrc += b_floats) {
+    for (int j = 0; j < nbt; ++j, bsrc += tile_floats) {
+      // the last tile may run past k_pad (a multiple of 128): copy only the
+      // rows that exist; the epilogue masks every column >= k
+      const int rows = min(N, p.k_pad - j * N);
+      const uint32_t bytes = (uint32_t)rows * p.kp * 4;
       if (!mbar_wait(s.b_empty + br.idx, br.phase ^ 1, p.err, 12)) return;
-      mbar_arrive_expect_tx(s.b_full + br.idx, s.b_bytes);
-      bulk_g2s(s.b + br.idx * b_floats, bsrc, s.b_bytes, s.b_full + br.idx);
+      mbar_arrive_expect_tx(s.b_full + br.idx, bytes);
+      bulk_g2s(s.b + (size_t)br.idx * tile_floats, bsrc, bytes, s.b_full + br.idx);
       br.next(p.stages);
     }
   }
@@ -108,44 +155,58 @@ __device__ void tc_producer(const TcParams& p, const TcSmem& s) {
 
 template <int KSTEPS>
 __device__ void tc_mma(const TcParams& p, const TcSmem& s, uint32_t tmem_base) {
+  constexpr int N = tc_tile_n(KSTEPS);
+  constexpr int KP = KSTEPS * 8;
+  constexpr uint32_t idesc = idesc_tf32(TC_BM, N);
   const int upb = p.n_pad / TC_ROWS;
   const int64_t n_units = (int64_t)p.nblk * upb;
-  constexpr uint32_t idesc = idesc_tf32(TC_BM, TC_BN);
-  const uint32_t sbo = (uint32_t)p.kp * 32;  // bytes between 8-row core-matrix groups
+  const uint32_t sbo = (uint32_t)KP * 32;  // bytes between 8-row core-matrix groups
   // Descriptors advance by (bytes >> 4) in their start-address field.
   const uint64_t a0 = smem_desc(smem_u32(s.a), 128, sbo);
   const uint64_t b0 = smem_desc(smem_u32(s.b), 128, sbo);
-  const uint64_t a_rt = (uint64_t)(TC_BM * p.kp * 4) >> 4;
-  const uint64_t a_buf = (uint64_t)s.a_bytes >> 4;
-  const uint64_t b_st = (uint64_t)s.b_bytes >> 4;
-  Ring ar, br, cr;
+  const uint64_t a_rt = (uint64_t)(TC_BM * KP * 4) >> 4;
+  const uint64_t b_st = (uint64_t)s.b_stage_bytes >> 4;
+  Ring ar, br;
+  uint32_t acc_phase = 0;
   for (int64_t u = blockIdx.x; u < n_units; u += gridDim.x) {
     int b, r0;
     if (!unit_live(p, u, upb, &b, &r0)) continue;
-    const int nbt = ceil_div(p.k[b], TC_BN);
-    if (!mbar_wait(s.a_full + ar.idx, ar.phase, p.err, 13)) return;
+    const int nbt = ceil_div(p.k[b], N);
+    if (!mbar_wait(s.a_full, ar.phase, p.err, 13)) return;
     tc_fence_after();
-    const uint64_t a_unit = a0 + ar.idx * a_buf;
     uint64_t bd = b0 + br.idx * b_st;
-    for (int j = 0; j < nbt; ++j) {
-      if (!mbar_wait(s.b_full + br.idx, br.phase, p.err, 14)) return;
-      if (!mbar_wait(s.acc_empty + cr.idx, cr.phase ^ 1, p.err, 15)) return;
-      tc_fence_after();
-      const uint32_t d0 = tmem_base + cr.idx * (TC_RT * TC_BN);
+    if (nbt > 0 && !mbar_wait(s.b_full + br.idx, br.phase, p.err, 14)) return;
+    for (int i = 0; i < nbt; ++i) {
 #pragma unroll
       for (int rt = 0; rt < TC_RT; ++rt) {
-        const uint64_t ad = a_unit + rt * a_rt;
+        // the accumulator is free once the epilogue has read it; that also
+        // means the MMAs that read this row tile's A have completed
+        if (!mbar_wait(s.acc_empty + rt, acc_phase ^ 1, p.err, 15)) return;
+        tc_fence_after();
+        const uint32_t a_tm = tmem_base + 2 * N + rt * KP;
+        if (i == 0) {
 #pragma unroll
-        for (int ks = 0; ks < KSTEPS; ++ks) mma_tf32(d0 + rt * TC_BN, ad + 16 * ks, bd + 16 * ks, idesc, ks > 0 ? 1u : 0u);
+          for (int ks = 0; ks < KSTEPS; ++ks) tmem_cp_128x256b(a_tm + ks * 8, a0 + rt * a_rt + 16 * ks);
+        }
+#pragma unroll
+        for (int ks = 0; ks < KSTEPS; ++ks)
+          mma_tf32_ts(tmem_base + rt * N, a_tm + ks * 8, bd + 16 * ks, idesc, ks > 0 ? 1u : 0u);
+        tc_commit(s.acc_full + rt);
+        if (rt == 0 && i + 1 < nbt) {
+          // next tile's centroids: waited for here, while row tile 0's chain runs
+          Ring nx = br;
+          nx.next(p.stages);
+          if (!mbar_wait(s.b_full + nx.idx, nx.phase, p.err, 14)) return;
+        }
       }
+      if (i == 0) tc_commit(s.a_empty);  // the points are in tensor memory: shared copy reusable
       tc_commit(s.b_empty + br.idx);
-      tc_commit(s.acc_full + cr.idx);
-      cr.next(2);
+      acc_phase ^= 1;
       br.next(p.stages);
       bd = br.idx == 0 ? b0 : bd + b_st;
     }
-    tc_commit(s.a_empty + ar.idx);
-    ar.next(TC_ABUF);
+    if (nbt == 0) tc_commit(s.a_empty);  // nothing issued: release the points at once
+    ar.next(1);
   }
 }
 
@@ -167,21 +228,39 @@ __device__ __forceinline__ float group_max32(const float (&v)[32]) {
   return max3f(max3f(m0, m1, m2), m3, m3);
 }
 
+// Mask the columns of one 32-centroid group at or past the problem's k.
+__device__ __forceinline__ void mask_group(float (&v)[32], int cbase, int kb) {
+  if (cbase + GROUP > kb) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (cbase + i >= kb) v[i] = -INFINITY;
+  }
+}
+
 // Epilogue warp e = warp - 2 owns TMEM lane quarter warp % 4 (hardware rule),
-// row tile (e >> 2) & 1 and column half e >> 3 of every 128-column tile. The
-// two halves of a row keep separate (best, group) pairs, merged through shared
-// memory at the end of each work unit (larger value, then lower group, wins).
+// row tile (e >> 2) & 1 and column half e >> 3 of every N-column tile (the
+// first half takes the extra group when N / 32 is odd). It reads its groups
+// two at a time, releases the accumulator after the last read, and folds
+// each group into a running (best, group); tiles arrive in index order, so
+// a strictly larger maximum is needed to move to a later group. The two
+// halves of a row keep separate pairs, merged through shared memory at the
+// end of each work unit (larger value, then lower group, wins).
+template <int KSTEPS>
 __device__ void tc_epilogue(const TcParams& p, const TcSmem& s, uint32_t tmem_base, int warp, int lane,
                             float* m_best, int* m_group) {
+  constexpr int N = tc_tile_n(KSTEPS);
+  constexpr int NG = N / GROUP;
   const int upb = p.n_pad / TC_ROWS;
   const int64_t n_units = (int64_t)p.nblk * upb;
   const int e = warp - 2;
   const int q = warp & 3;
   const int rt = (e >> 2) & 1;
   const int half = e >> 3;
+  const int g0 = half ? (NG + 1) / 2 : 0;
+  const int g1 = half ? NG : (NG + 1) / 2;
   const int lrow = rt * TC_BM + q * 32 + lane;  // row within the unit
-  const uint32_t lane_off = (uint32_t)(q * 32) << 16;
-  Ring cr;
+  const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + rt * N;
+  uint32_t acc_phase = 0;
   // After a failed wait a warp stops touching tensor memory but keeps joining
   // the named barriers below, so its partner warps are never left waiting.
   bool failed = false;
@@ -189,41 +268,40 @@ __device__ void tc_epilogue(const TcParams& p, const TcSmem& s, uint32_t tmem_ba
     int b, r0;
     if (!unit_live(p, u, upb, &b, &r0)) continue;
     const int kb = p.k[b], nb = p.n[b];
-    const int nbt = ceil_div(kb, TC_BN);
+    const int nbt = ceil_div(kb, N);
     float best = -INFINITY;
     int bestg = 0x7fffffff;
     for (int j = 0; j < nbt; ++j) {
       if (failed) continue;
-      const uint32_t acc = cr.idx;
-      const bool ok = mbar_wait(s.acc_full + acc, cr.phase, p.err, 16);
-      cr.next(2);
+      const bool ok = mbar_wait(s.acc_full + rt, acc_phase, p.err, 16);
+      acc_phase ^= 1;
       if (!__all_sync(0xffffffffu, ok)) {
         failed = true;
         continue;
       }
       tc_fence_after();
-      const uint32_t taddr = tmem_base + lane_off + (acc * TC_RT + rt) * TC_BN + half * 64;
-      float v0[32], v1[32];
-      tmem_ld32(taddr + 0, v0);
-      tmem_ld32(taddr + 32, v1);
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(s.acc_empty + acc);  // one arrival per warp
-      const int cbase = j * TC_BN + half * 64;
-      if (cbase + 64 > kb) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          if (cbase + i >= kb) v0[i] = -INFINITY;
-          if (cbase + 32 + i >= kb) v1[i] = -INFINITY;
+      for (int g = g0; g < g1; g += 2) {
+        float v0[32], v1[32];
+        const bool pair = g + 1 < g1;
+        tmem_ld32(taddr + g * GROUP, v0);
+        if (pair) tmem_ld32(taddr + (g + 1) * GROUP, v1);
+        tmem_wait_ld();
+        if (g + 2 >= g1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(s.acc_empty + rt);  // one arrival per warp
+        }
+        const int gg = j * NG + g;  // global group index
+        mask_group(v0, gg * GROUP, kb);
+        float m = group_max32(v0);
+        if (m > best) { best = m; bestg = gg; }
+        if (pair) {
+          mask_group(v1, (gg + 1) * GROUP, kb);
+          m = group_max32(v1);
+          if (m > best) { best = m; bestg = gg + 1; }
         }
       }
-      const int g0 = cbase / GROUP;
-      float m;
-      m = group_max32(v0);
-      if (m > best) { best = m; bestg = g0; }
-      m = group_max32(v1);
-      if (m > best) { best = m; bestg = g0 + 1; }
     }
     // merge the two column halves of each row (epilogue warps only: named barrier 1)
     if (half == 1) {
@@ -247,37 +325,35 @@ __device__ void tc_epilogue(const TcParams& p, const TcSmem& s, uint32_t tmem_ba
 
 template <int KSTEPS>
 __global__ void __launch_bounds__(TC_THREADS, 1) assign_tc_kernel(TcParams p) {
+  constexpr int N = tc_tile_n(KSTEPS);
   extern __shared__ __align__(128) uint8_t smem_raw[];
   TcSmem s;
   s.a_bytes = (uint32_t)TC_ROWS * p.kp * 4;
-  s.b_bytes = (uint32_t)TC_BN * p.kp * 4;
+  s.b_stage_bytes = (uint32_t)N * p.kp * 4;
   s.a = reinterpret_cast<float*>(smem_raw);
-  s.b = reinterpret_cast<float*>(smem_raw + (size_t)TC_ABUF * s.a_bytes);
-  uint64_t* bars =
-      reinterpret_cast<uint64_t*>(smem_raw + (size_t)TC_ABUF * s.a_bytes + (size_t)p.stages * s.b_bytes);
+  s.b = reinterpret_cast<float*>(smem_raw + (size_t)s.a_bytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw + (size_t)s.a_bytes + (size_t)p.stages * s.b_stage_bytes);
   s.a_full = bars;
-  s.a_empty = bars + TC_ABUF;
-  s.b_full = bars + 2 * TC_ABUF;
+  s.a_empty = bars + 1;
+  s.b_full = bars + 2;
   s.b_empty = s.b_full + TC_STAGES;
   s.acc_full = s.b_empty + TC_STAGES;
-  s.acc_empty = s.acc_full + 2;
-  s.tmem_slot = reinterpret_cast<uint32_t*>(s.acc_empty + 2);
+  s.acc_empty = s.acc_full + TC_RT;
+  s.tmem_slot = reinterpret_cast<uint32_t*>(s.acc_empty + TC_RT);
   float* m_best = reinterpret_cast<float*>(s.tmem_slot + 4);  // [TC_ROWS] half-row merge
   int* m_group = reinterpret_cast<int*>(m_best + TC_ROWS);      // [TC_ROWS]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < TC_ABUF; ++i) {
-      mbar_init(s.a_full + i, 1);
-      mbar_init(s.a_empty + i, 1);
-    }
+    mbar_init(s.a_full, 1);
+    mbar_init(s.a_empty, 1);
     for (int i = 0; i < p.stages; ++i) {
       mbar_init(s.b_full + i, 1);
       mbar_init(s.b_empty + i, 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < TC_RT; ++i) {
       mbar_init(s.acc_full + i, 1);
-      mbar_init(s.acc_empty + i, TC_EPI_WARPS);
+      mbar_init(s.acc_empty + i, TC_EPI_WARPS / TC_RT);
     }
     fence_barrier_init();
   }
@@ -291,11 +367,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) assign_tc_kernel(TcParams p) {
   const uint32_t tmem_base = *s.tmem_slot;
 
   if (warp == 0) {
-    if (lane == 0) tc_producer(p, s);
+    if (lane == 0) tc_producer<KSTEPS>(p, s);
   } else if (warp == 1) {
     if (lane == 0) tc_mma<KSTEPS>(p, s, tmem_base);
   } else {
-    tc_epilogue(p, s, tmem_base, warp, lane, m_best, m_group);
+    tc_epilogue<KSTEPS>(p, s, tmem_base, warp, lane, m_best, m_group);
   }
   tc_fence_before();
   __syncthreads();
@@ -309,29 +385,57 @@ __global__ void __launch_bounds__(TC_THREADS, 1) assign_tc_kernel(TcParams p) {
 // the winning group g of 32 centroids; on exit labels[b][i] = the argmax over
 // c in [32 g, 32 g + 32) of the exact fp32 reference score (first maximum
 // wins). One CTA owns a range of points of one problem and walks the
-// problem's centroid table in shared-memory slices (each group padded by one
-// float so that threads of a warp working on different groups hit different
-// banks); L2 traffic is one table read per CTA instead of 32 centroids per point.
+// problem's centroid table in shared-memory slices stored transposed
+// ([group][coordinate][32 centroids]), so that one warp re-scores one point
+// with lane l holding centroid 32 g + l: every table read is 32 consecutive
+// words (no bank conflicts) and the point's coordinates are broadcast. Each
+// lane accumulates its dot product in coordinate order with fused
+// multiply-adds, exactly as a sequential loop would; the winner is the
+// largest score (NaN never wins), lowest lane among equals, found with a
+// warp max over order-preserving keys and a ballot.
+// A warp takes its points 32 at a time: lane l loads the label and the
+// coordinates of point base + l (one coalesced batch), a ballot picks the
+// points whose group lies in the current slice, and each of those is scored
+// with its coordinates broadcast from its lane by warp shuffles, so no
+// global-memory latency sits between one point and the next. Two CTAs fit
+// an SM, so one CTA's table fill overlaps the other's scoring.
 constexpr int RF_THREADS = 512;
-constexpr int RF_SMEM = 200 * 1024;
+constexpr int RF_WARPS = RF_THREADS / 32;
+constexpr int RF_SMEM = 100 * 1024;
 
 template <int BS>
-__global__ void __launch_bounds__(RF_THREADS)
+__device__ __forceinline__ void rf_load_point(const float* xr, int bs, float (&x)[BS > 0 ? BS : 64]) {
+  constexpr int XN = BS > 0 ? BS : 64;
+  if constexpr (BS > 0 && BS % 4 == 0) {
+#pragma unroll
+    for (int j = 0; j < BS; j += 4) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(xr + j));
+      x[j] = v.x; x[j + 1] = v.y; x[j + 2] = v.z; x[j + 3] = v.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < XN; ++j)
+      if (BS > 0 || j < bs) x[j] = __ldg(xr + j);
+  }
+}
+
+template <int BS>
+__global__ void __launch_bounds__(RF_THREADS, 2)
 refine_kernel(int metric, const float* __restrict__ X, const float* __restrict__ C,
               const float* __restrict__ cnorm, int n_pad, int k_pad, int bs_rt, int groups_per_slice,
               int chunk_rows, const int32_t* __restrict__ n, const int32_t* __restrict__ kvec,
               const int32_t* __restrict__ active, int32_t* __restrict__ labels) {
   extern __shared__ float tab[];
-  const int bs = BS > 0 ? BS : bs_rt;
   constexpr int XN = BS > 0 ? BS : 64;
+  const int bs = BS > 0 ? BS : bs_rt;
   const int b = blockIdx.y;
   if (active && !active[b]) return;
   const int nb = n[b], kb = kvec[b];
   const int r0 = blockIdx.x * chunk_rows;
   if (r0 >= nb) return;
   const int r1 = min(nb, r0 + chunk_rows);
-  const int gstride = GROUP * bs + 1;
-  float* cn = tab + (size_t)groups_per_slice * gstride;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* cn = tab + (size_t)groups_per_slice * bs * GROUP;
   const int n_groups = ceil_div(kb, GROUP);
   const float* Cb = C + (int64_t)b * k_pad * bs;
   const float* Nb = cnorm + (int64_t)b * k_pad;
@@ -340,45 +444,50 @@ refine_kernel(int metric, const float* __restrict__ X, const float* __restrict__
   for (int g0 = 0; g0 < n_groups; g0 += groups_per_slice) {
     const int g1 = min(n_groups, g0 + groups_per_slice);
     __syncthreads();
-    const int words = (g1 - g0) * GROUP * bs;
-    for (int t = threadIdx.x; t < words; t += RF_THREADS) {
-      const int gl = t / (GROUP * bs), rem = t - gl * GROUP * bs;
-      const int c = (g0 + gl) * GROUP + rem / bs;
-      tab[gl * gstride + rem] = c < kb ? Cb[(int64_t)g0 * GROUP * bs + t] : 0.f;
-    }
-    for (int t = threadIdx.x; t < (g1 - g0) * GROUP; t += RF_THREADS) {
+    // one thread per centroid of the slice: its row in, one column of the
+    // transposed table out (consecutive threads write consecutive words).
+    // Every centroid index here is below k_pad; rows at or past k read as 0.
+    const int cents = (g1 - g0) * GROUP;
+#pragma unroll 2
+    for (int t = threadIdx.x; t < cents; t += RF_THREADS) {
       const int c = g0 * GROUP + t;
-      cn[t] = c < kb ? Nb[c] : 0.f;
-    }
-    __syncthreads();
-    for (int i = r0 + threadIdx.x; i < r1; i += RF_THREADS) {
-      const int v = Lb[i];
-      if (v >= 0) continue;
-      const int g = -v - 1;
-      if (g < g0 || g >= g1) continue;
-      float x[XN];
-      const float* xr = Xb + (int64_t)i * bs;
+      const bool ok = c < kb;
+      float row[XN];
+      rf_load_point<BS>(Cb + (int64_t)c * bs, bs, row);
+      float* dst = tab + (size_t)(t >> 5) * bs * GROUP + (t & 31);
 #pragma unroll
       for (int j = 0; j < XN; ++j)
-        if (BS > 0 || j < bs) x[j] = xr[j];
-      const float* T = tab + (g - g0) * gstride;
-      const float* TN = cn + (g - g0) * GROUP;
-      const int cnt = min(GROUP, kb - g * GROUP);
-      float sbest = -INFINITY;
-      int ibest = 0;
-      for (int ii = 0; ii < cnt; ++ii) {
-        const float* cc = T + ii * bs;
+        if (BS > 0 || j < bs) dst[j * GROUP] = ok ? row[j] : 0.f;
+      cn[t] = ok ? __ldg(Nb + c) : 0.f;
+    }
+    __syncthreads();
+    for (int base = r0 + warp * 32; base < r1; base += RF_WARPS * 32) {
+      const int i_own = base + lane;
+      const int v = i_own < r1 ? Lb[i_own] : 0;
+      const int g_own = -v - 1;
+      const bool mine = v < 0 && g_own >= g0 && g_own < g1;
+      uint32_t todo = __ballot_sync(0xffffffffu, mine);
+      if (!todo) continue;
+      // each lane loads its own point (consecutive points: coalesced); the
+      // point being scored is broadcast from its lane one coordinate at a time
+      float xo[XN];
+      if (mine) rf_load_point<BS>(Xb + (int64_t)i_own * bs, bs, xo);
+      while (todo) {
+        const int k = __ffs(todo) - 1;
+        todo &= todo - 1;
+        const int g = __shfl_sync(0xffffffffu, g_own, k);
+        const float* T = tab + (size_t)(g - g0) * bs * GROUP + lane;
         float dot = 0.f;
 #pragma unroll
         for (int j = 0; j < XN; ++j)
-          if (BS > 0 || j < bs) dot = __fmaf_rn(x[j], cc[j], dot);
-        const float sc = metric == SKCQ_METRIC_COSINE ? dot : -__fadd_rn(__fmul_rn(dot, -2.0f), TN[ii]);
-        if (sc > sbest) {
-          sbest = sc;
-          ibest = ii;
-        }
+          if (BS > 0 || j < bs) dot = __fmaf_rn(__shfl_sync(0xffffffffu, xo[j], k), T[j * GROUP], dot);
+        float sc = metric == SKCQ_METRIC_COSINE ? dot : -__fadd_rn(__fmul_rn(dot, -2.0f), cn[(g - g0) * GROUP + lane]);
+        if (g * GROUP + lane >= kb || sc != sc) sc = -INFINITY;
+        const uint32_t key = float_key(sc + 0.0f);  // -0 and +0 compare equal
+        const uint32_t top = __reduce_max_sync(0xffffffffu, key);
+        const uint32_t win = __ballot_sync(0xffffffffu, key == top);
+        if (lane == 0) Lb[base + k] = g * GROUP + (__ffs(win) - 1);
       }
-      Lb[i] = g * GROUP + ibest;
     }
   }
 }
@@ -423,13 +532,14 @@ static cudaError_t launch_refine(int metric, const float* X, const float* C, con
     if (e != cudaSuccess) return e;
     configured_dev = dev;
   }
-  const size_t group_bytes = (size_t)(GROUP * bs + 1 + GROUP) * sizeof(float);
+  const size_t group_bytes = (size_t)(GROUP * bs + GROUP) * sizeof(float);
   const int n_groups = k_pad / GROUP;
   int gps = (int)std::min<size_t>(RF_SMEM / group_bytes, (size_t)n_groups);
   if (gps < 1) gps = 1;
   const size_t smem = (size_t)gps * group_bytes;
-  // enough CTAs for two waves, each owning >= 4096 points so the table load amortises
-  const int64_t target = (int64_t)num_sms() * 2;
+  // about four CTAs per SM (two resident at a time), each owning >= 4096
+  // points so that the table load amortises
+  const int64_t target = (int64_t)num_sms() * 4;
   int64_t chunks = (target + nblk - 1) / nblk;
   int64_t chunk_rows = (n_pad + chunks - 1) / chunks;
   if (chunk_rows < 4096) chunk_rows = std::min<int64_t>(4096, n_pad);
@@ -452,37 +562,29 @@ extern "C" int skcq_assign(int metric, const float* A, const float* B, const flo
   SKCQ_REQUIRE(bs > 0 && bs <= 64, SKCQ_ERR_INVALID, "assign: block size %d outside [1, 64]", bs);
   SKCQ_REQUIRE(n_pad > 0 && n_pad % TC_ROWS == 0, SKCQ_ERR_INVALID, "assign: n_pad %d not a multiple of %d", n_pad,
                TC_ROWS);
-  SKCQ_REQUIRE(k_pad > 0 && k_pad % TC_BN == 0, SKCQ_ERR_INVALID, "assign: k_pad %d not a multiple of %d", k_pad,
-               TC_BN);
+  SKCQ_REQUIRE(k_pad > 0 && k_pad % SKCQ_CENT_TILE == 0, SKCQ_ERR_INVALID, "assign: k_pad %d not a multiple of %d",
+               k_pad, SKCQ_CENT_TILE);
   SKCQ_REQUIRE((((uintptr_t)A | (uintptr_t)B) & 15) == 0, SKCQ_ERR_INVALID, "assign: operands not 16-byte aligned");
   const int kp = skcq_packed_width(metric, bs);
   SKCQ_REQUIRE(kp / 8 <= TC_MAX_KSTEPS, SKCQ_ERR_INVALID,
                "assign: block size %d too wide for the tensor-core path (use skcq_assign_exact)", bs);
-  const size_t bar_bytes = (2 * TC_ABUF + 2 * TC_STAGES + 4) * sizeof(uint64_t) + 16 + 2 * TC_ROWS * 4;
-  int stages = TC_STAGES;
-  auto smem_for = [&](int st) {
-    return (size_t)TC_ABUF * TC_ROWS * kp * 4 + (size_t)st * TC_BN * kp * 4 + bar_bytes;
-  };
-  while (stages > 2 && smem_for(stages) > 227 * 1024) --stages;
-  size_t smem = smem_for(stages);
-  SKCQ_REQUIRE(smem <= 227 * 1024, SKCQ_ERR_INVALID, "assign: block size %d needs too much shared memory", bs);
-  if (smem < TC_MIN_SMEM) smem = TC_MIN_SMEM;
   int* err = device_error_word();
   SKCQ_REQUIRE(err != nullptr, SKCQ_ERR_CUDA, "assign: no device error word");
-  TcParams p{A, B, nblk, n_pad, k_pad, kp, stages, n, k, active, labels, err};
   const int64_t n_units = (int64_t)nblk * (n_pad / TC_ROWS);
   const int grid = (int)(n_units < num_sms() ? n_units : num_sms());
   cudaStream_t s = (cudaStream_t)stream;
   cudaError_t e;
-  switch (kp / 8) {
-    case 1: e = launch_tc<1>(p, grid, smem, s); break;
-    case 2: e = launch_tc<2>(p, grid, smem, s); break;
-    case 3: e = launch_tc<3>(p, grid, smem, s); break;
-    case 4: e = launch_tc<4>(p, grid, smem, s); break;
-    case 5: e = launch_tc<5>(p, grid, smem, s); break;
-    case 6: e = launch_tc<6>(p, grid, smem, s); break;
-    case 7: e = launch_tc<7>(p, grid, smem, s); break;
-    default: e = launch_tc<8>(p, grid, smem, s); break;
+  if (kp / 8 > TC_TS_MAX_KSTEPS) {
+    e = assign_ss_launch(A, B, nblk, n_pad, k_pad, kp, n, k, active, labels, err, grid, s);
+  } else {
+    const size_t bar_bytes = (2 + 2 * TC_STAGES + 2 * TC_RT) * sizeof(uint64_t) + 16 + 2 * TC_ROWS * 4;
+    int stages = TC_STAGES;
+    auto smem_for = [&](int st) { return (size_t)TC_ROWS * kp * 4 + (size_t)st * TC_BN * kp * 4 + bar_bytes; };
+    while (stages > 2 && smem_for(stages) > 227 * 1024) --stages;
+    size_t smem = smem_for(stages);
+    if (smem < TC_MIN_SMEM) smem = TC_MIN_SMEM;
+    TcParams p{A, B, nblk, n_pad, k_pad, kp, stages, n, k, active, labels, err};
+    e = kp / 8 == 1 ? launch_tc<1>(p, grid, smem, s) : launch_tc<2>(p, grid, smem, s);
   }
   if (e != cudaSuccess) return set_error(SKCQ_ERR_CUDA, "assign: %s", cudaGetErrorString(e));
   SKCQ_REQUIRE(nblk <= 65535, SKCQ_ERR_INVALID, "assign: %d problems exceed 65535", nblk);
