@@ -606,7 +606,7 @@ def main() -> None:
     achieved = a["work"] / (a["ms"] / 1e3) / 1e12 if a["ms"] > 0 else 0.0
     issued = a["padded"] / (a["ms"] / 1e3) / 1e12 if a["ms"] > 0 else 0.0
     roofline = {
-        "bound": "tensor", "kernel": "assign_tc_kernel", "achieved": achieved,
+        "bound": "tensor", "kernel": "skcq_assign (tensor-core pass + exact re-score)", "achieved": achieved,
         "peak": peaks["bf16_tflops"], "peak_kind": f"{peak_kind} bf16 dense (burst)", "unit": "TFLOP/s",
         "frac": achieved / peaks["bf16_tflops"], "traffic": None,
         "issued_tf32_tflops": issued,
