@@ -60,11 +60,8 @@ def _labels(pts, C, exact: bool):
     return lab[:, : pts.n_host[0]].cpu().numpy()
 
 
-@pytest.mark.parametrize("metric", [0, 1])
-@pytest.mark.parametrize("bs,K,n,nblk", [(4, 300, 1000, 3), (8, 256, 768, 5), (16, 4096, 2048, 2),
-                                          (6, 1000, 777, 2), (12, 129, 513, 2), (8, 4096, 4096, 2)])
-def test_assign_matches_oracle(metric, bs, K, n, nblk):
-    w, pts, C = _problem(metric, nblk, n, bs, K, seed=bs * 1000 + K + metric)
+def _check_assign(metric, bs, K, n, nblk, seed):
+    w, pts, C = _problem(metric, nblk, n, bs, K, seed=seed)
     lab_tc = _labels(pts, C, exact=False)
     lab_ex = _labels(pts, C, exact=True)
     for b in range(nblk):
@@ -83,6 +80,28 @@ def test_assign_matches_oracle(metric, bs, K, n, nblk):
         assert (lab_tc[b][m] == ref[m]).all(), f"block {b}: {(lab_tc[b][m] != ref[m]).sum()} tensor-core mismatches"
         assert (lab_ex[b][m] == ref[m]).all()
         assert (lab_tc[b] == ref).mean() > 0.999
+
+
+@pytest.mark.parametrize("metric", [0, 1])
+@pytest.mark.parametrize("bs,K,n,nblk", [(4, 300, 1000, 3), (8, 256, 768, 5), (16, 4096, 2048, 2),
+                                          (6, 1000, 777, 2), (12, 129, 513, 2), (8, 4096, 4096, 2)])
+def test_assign_matches_oracle(metric, bs, K, n, nblk):
+    _check_assign(metric, bs, K, n, nblk, seed=bs * 1000 + K + metric)
+
+
+@pytest.mark.parametrize("metric,bs,K", [(1, 4, 1000), (0, 4, 700), (0, 8, 500), (1, 16, 300)])
+def test_assign_many_units_per_cta(metric, bs, K):
+    """More 256-point work units than two per SM, two problems: every persistent
+    CTA runs several units and crosses from one problem to the next, so the
+    per-unit point reload (into tensor memory for packed widths <= 16, into
+    shared memory otherwise) and the centroid-ring hand-over between units are
+    exercised; K is not a multiple of either tile width."""
+    from skcq_b200 import _engine
+
+    n, nblk = 40000, 2
+    units = nblk * _engine.round_up(n, _engine.ROWS_PER_UNIT) // _engine.ROWS_PER_UNIT
+    assert units > 2 * torch.cuda.get_device_properties(0).multi_processor_count
+    _check_assign(metric, bs, K, n, nblk, seed=7 * K + bs + metric)
 
 
 def _kmeans_case(name):
