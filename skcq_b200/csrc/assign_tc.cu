@@ -394,11 +394,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) assign_tc_kernel(TcParams p) {
 // largest score (NaN never wins), lowest lane among equals, found with a
 // warp max over order-preserving keys and a ballot.
 // A warp takes its points 32 at a time: lane l loads the label and the
-// coordinates of point base + l (one coalesced batch), a ballot picks the
-// points whose group lies in the current slice, and each of those is scored
-// with its coordinates broadcast from its lane by warp shuffles, so no
-// global-memory latency sits between one point and the next. Two CTAs fit
-// an SM, so one CTA's table fill overlaps the other's scoring.
+// coordinates of point base + l (one coalesced batch) and stages the
+// coordinates in the warp's shared-memory slot; a ballot picks the points
+// whose group lies in the current slice, and each of those is scored with its
+// coordinates read as broadcast vector loads, so no global-memory latency
+// sits between one point and the next. Two CTAs fit an SM, so one CTA's table
+// fill overlaps the other's scoring.
 constexpr int RF_THREADS = 512;
 constexpr int RF_WARPS = RF_THREADS / 32;
 constexpr int RF_SMEM = 100 * 1024;
@@ -436,6 +437,7 @@ refine_kernel(int metric, const float* __restrict__ X, const float* __restrict__
   const int r1 = min(nb, r0 + chunk_rows);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float* cn = tab + (size_t)groups_per_slice * bs * GROUP;
+  float* xs = cn + (size_t)groups_per_slice * GROUP + (size_t)warp * GROUP * bs;  // this warp's 32 points
   const int n_groups = ceil_div(kb, GROUP);
   const float* Cb = C + (int64_t)b * k_pad * bs;
   const float* Nb = cnorm + (int64_t)b * k_pad;
@@ -468,19 +470,40 @@ refine_kernel(int metric, const float* __restrict__ X, const float* __restrict__
       const bool mine = v < 0 && g_own >= g0 && g_own < g1;
       uint32_t todo = __ballot_sync(0xffffffffu, mine);
       if (!todo) continue;
-      // each lane loads its own point (consecutive points: coalesced); the
-      // point being scored is broadcast from its lane one coordinate at a time
-      float xo[XN];
-      if (mine) rf_load_point<BS>(Xb + (int64_t)i_own * bs, bs, xo);
+      // each lane stages its own point (consecutive points: coalesced loads) in
+      // this warp's shared-memory slot; the point being scored is then read by
+      // all lanes at one address (broadcast), four coordinates per load when
+      // bs % 4 == 0
+      __syncwarp();
+      if (mine) {
+        float xo[XN];
+        rf_load_point<BS>(Xb + (int64_t)i_own * bs, bs, xo);
+#pragma unroll
+        for (int j = 0; j < XN; ++j)
+          if (BS > 0 || j < bs) xs[lane * bs + j] = xo[j];
+      }
+      __syncwarp();
       while (todo) {
         const int k = __ffs(todo) - 1;
         todo &= todo - 1;
         const int g = __shfl_sync(0xffffffffu, g_own, k);
         const float* T = tab + (size_t)(g - g0) * bs * GROUP + lane;
+        float x[XN];
+        if constexpr (BS > 0 && BS % 4 == 0) {
+#pragma unroll
+          for (int j = 0; j < BS; j += 4) {
+            const float4 q = *reinterpret_cast<const float4*>(xs + k * BS + j);
+            x[j] = q.x; x[j + 1] = q.y; x[j + 2] = q.z; x[j + 3] = q.w;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < XN; ++j)
+            if (BS > 0 || j < bs) x[j] = xs[k * bs + j];
+        }
         float dot = 0.f;
 #pragma unroll
         for (int j = 0; j < XN; ++j)
-          if (BS > 0 || j < bs) dot = __fmaf_rn(__shfl_sync(0xffffffffu, xo[j], k), T[j * GROUP], dot);
+          if (BS > 0 || j < bs) dot = __fmaf_rn(x[j], T[j * GROUP], dot);
         float sc = metric == SKCQ_METRIC_COSINE ? dot : -__fadd_rn(__fmul_rn(dot, -2.0f), cn[(g - g0) * GROUP + lane]);
         if (g * GROUP + lane >= kb || sc != sc) sc = -INFINITY;
         const uint32_t key = float_key(sc + 0.0f);  // -0 and +0 compare equal
@@ -533,10 +556,12 @@ static cudaError_t launch_refine(int metric, const float* X, const float* C, con
     configured_dev = dev;
   }
   const size_t group_bytes = (size_t)(GROUP * bs + GROUP) * sizeof(float);
+  const size_t stage_bytes = (size_t)RF_WARPS * GROUP * bs * sizeof(float);  // per-warp point slots
+  if (stage_bytes + group_bytes > (size_t)RF_SMEM) return cudaErrorInvalidValue;  // bs > 21 never gets here
   const int n_groups = k_pad / GROUP;
-  int gps = (int)std::min<size_t>(RF_SMEM / group_bytes, (size_t)n_groups);
+  int gps = (int)std::min<size_t>((RF_SMEM - stage_bytes) / group_bytes, (size_t)n_groups);
   if (gps < 1) gps = 1;
-  const size_t smem = (size_t)gps * group_bytes;
+  const size_t smem = (size_t)gps * group_bytes + stage_bytes;
   // about four CTAs per SM (two resident at a time), each owning >= 4096
   // points so that the table load amortises
   const int64_t target = (int64_t)num_sms() * 4;
