@@ -307,6 +307,62 @@ def case_vq(out: Path, vq_experiment, vq_runner) -> None:
     np.savez_compressed(out / "vq.npz", **res)
 
 
+# (layer, tokens) per MoE call; layer 0 is called twice, layer 3 only in the base capture
+METRIC_CALLS = [(0, 40), (1, 40), (0, 24), (2, 64), (3, 16)]
+
+
+def case_metrics(out: Path, metrics, eval_model) -> None:
+    """Routing agreement, KLD, token log-likelihoods and sliding-window perplexity
+    (skcq/metrics.py, skcq/eval_model.py) on seeded synthetic captures and a tiny
+    deterministic language model (tests/_helpers.py: TinyLM, CharTokenizer)."""
+    sys.path.insert(0, str(HERE.parent))
+    from _helpers import CharTokenizer, TinyLM, perturb_routing, routing_calls
+
+    def capture(calls):
+        cap = metrics.RoutingCapture()
+        for layer, ids, w in calls:
+            cap.layer_index.append(layer)
+            cap.top_k_index.append(ids)
+            cap.top_k_weights.append(w)
+        return cap
+
+    res = {}
+    # pair a: with weights, layer 3 missing from the quantized capture
+    base = routing_calls(51, METRIC_CALLS)
+    quant = perturb_routing(base[:-1], 52)
+    # pair b: no weights, layer 1 with a different token count (skipped)
+    base_b = routing_calls(53, METRIC_CALLS[:4], weights=False)
+    quant_b = perturb_routing(base_b, 54)
+    quant_b[1] = (1, quant_b[1][1][:30], quant_b[1][2])
+    for tag, (bc, qc) in {"a": (base, quant), "b": (base_b, quant_b)}.items():
+        summ = metrics.routing_agreement(capture(bc), capture(qc))
+        for side, calls in (("base", bc), ("quant", qc)):
+            res[f"rt_{tag}__{side}__layers"] = np.array([c[0] for c in calls], dtype=np.int64)
+            for i, (_, ids, w) in enumerate(calls):
+                res[f"rt_{tag}__{side}__idx{i}"] = ids.numpy()
+                res[f"rt_{tag}__{side}__w{i}"] = w.numpy()
+        for key in ("common_layers", "total_tokens", "set_agreement", "weight_cosine", "routing_jsd"):
+            res[f"rt_{tag}__{key}"] = np.array([summ[key]], dtype=np.float64)
+        res[f"rt_{tag}__per_layer"] = np.array([[d["layer"], d["tokens"], d["set_agreement"]]
+                                                for d in summ["per_layer"]], dtype=np.float64)
+        print(f"routing {tag}: {summ['set_agreement']:.4f} cos {summ['weight_cosine']:.6f} jsd {summ['routing_jsd']:.6f}")
+
+    rs = np.random.RandomState(7)
+    text = "".join(rs.choice(list("abcdefghij klmnop"), size=300))
+    tok = CharTokenizer()
+    model, model_q = TinyLM(seed=5), TinyLM(seed=5, noise=0.05)
+    ids = tok(text).input_ids
+    ref_logits = metrics.capture_reference_logits(model, ids, max_length=64)
+    res["lm_text"] = np.array([text])
+    res["lm_ref_logits"] = ref_logits.numpy()
+    res["lm_kld"] = np.array([metrics.kld_against_reference(model_q, ids, ref_logits)])
+    res["lm_tll"] = metrics.token_log_likelihoods(model_q, ids[:, :80]).numpy()
+    res["lm_ppl"] = np.array([eval_model.compute_perplexity(model_q, tok, text, max_length=48, stride=16)])
+    res["lm_ppl_base"] = np.array([eval_model.compute_perplexity(model, tok, text, max_length=48, stride=16)])
+    print(f"lm: kld {res['lm_kld'][0]:.6f} ppl {res['lm_ppl'][0]:.4f} base {res['lm_ppl_base'][0]:.4f}")
+    np.savez_compressed(out / "metrics.npz", **res)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
@@ -318,11 +374,14 @@ def main() -> None:
     import skcq.codebook.events as events
     import skcq.codebook.kmeans as km
     import skcq.codebook_experts as experts_mod
+    import skcq.eval_model as eval_model
+    import skcq.metrics as metrics
     import skcq.vq.bpw as bpw_mod
     import skcq.vq.experiment as vq_experiment
     import skcq.vq.runner as vq_runner
 
-    todo = args.only.split(",") if args.only else ["assign", "kmeans", "codecs", "experts", "config1", "vq"]
+    todo = (args.only.split(",") if args.only
+            else ["assign", "kmeans", "codecs", "experts", "config1", "vq", "metrics"])
     if "assign" in todo:
         case_assign(HERE, km)
     if "kmeans" in todo:
@@ -335,6 +394,8 @@ def main() -> None:
         case_config1(HERE, cb, bpw_mod)
     if "vq" in todo:
         case_vq(HERE, vq_experiment, vq_runner)
+    if "metrics" in todo:
+        case_metrics(HERE, metrics, eval_model)
 
 
 if __name__ == "__main__":
