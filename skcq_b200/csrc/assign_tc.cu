@@ -56,7 +56,6 @@ constexpr int TC_TS_MAX_KSTEPS = 2;
 // Centroids per tile: the widest N (a multiple of 32) with 2 N + 2 kp <= 512
 // tensor-memory columns.
 constexpr int TC_BN = 224;
-__host__ __device__ constexpr int tc_tile_n(int) { return TC_BN; }
 
 static_assert(TC_ROWS == SKCQ_ROWS_PER_UNIT, "work unit size is part of the ABI");
 static_assert(2 * TC_BN + 2 * 8 * TC_TS_MAX_KSTEPS <= TC_TMEM_COLS, "accumulators and A tiles must fit tensor memory");
@@ -126,7 +125,7 @@ __device__ __forceinline__ void tmem_cp_128x256b(uint32_t taddr, uint64_t s_desc
 
 template <int KSTEPS>
 __device__ void tc_producer(const TcParams& p, const TcSmem& s) {
-  constexpr int N = tc_tile_n(KSTEPS);
+  constexpr int N = TC_BN;
   const int upb = p.n_pad / TC_ROWS;
   const int64_t n_units = (int64_t)p.nblk * upb;
   const int64_t tile_floats = (int64_t)N * p.kp;
@@ -155,7 +154,7 @@ __device__ void tc_producer(const TcParams& p, const TcSmem& s) {
 
 template <int KSTEPS>
 __device__ void tc_mma(const TcParams& p, const TcSmem& s, uint32_t tmem_base) {
-  constexpr int N = tc_tile_n(KSTEPS);
+  constexpr int N = TC_BN;
   constexpr int KP = KSTEPS * 8;
   constexpr uint32_t idesc = idesc_tf32(TC_BM, N);
   const int upb = p.n_pad / TC_ROWS;
@@ -248,7 +247,7 @@ __device__ __forceinline__ void mask_group(float (&v)[32], int cbase, int kb) {
 template <int KSTEPS>
 __device__ void tc_epilogue(const TcParams& p, const TcSmem& s, uint32_t tmem_base, int warp, int lane,
                             float* m_best, int* m_group) {
-  constexpr int N = tc_tile_n(KSTEPS);
+  constexpr int N = TC_BN;
   constexpr int NG = N / GROUP;
   const int upb = p.n_pad / TC_ROWS;
   const int64_t n_units = (int64_t)p.nblk * upb;
@@ -325,7 +324,7 @@ __device__ void tc_epilogue(const TcParams& p, const TcSmem& s, uint32_t tmem_ba
 
 template <int KSTEPS>
 __global__ void __launch_bounds__(TC_THREADS, 1) assign_tc_kernel(TcParams p) {
-  constexpr int N = tc_tile_n(KSTEPS);
+  constexpr int N = TC_BN;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   TcSmem s;
   s.a_bytes = (uint32_t)TC_ROWS * p.kp * 4;
