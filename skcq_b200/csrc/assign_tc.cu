@@ -316,7 +316,7 @@ __device__ void tc_epilogue(const TcParams& p, const TcSmem& s, uint32_t tmem_ba
         bestg = og;
       }
       const int row = r0 + lrow;
-      if (row < nb && !failed) p.group[(int64_t)b * p.n_pad + row] = -(bestg + 1);  // negative: not yet refined
+      if (row < nb && !failed && nbt > 0) p.group[(int64_t)b * p.n_pad + row] = -(bestg + 1);  // negative: not yet refined
     }
     asm volatile("bar.sync 1, %0;" ::"n"(TC_EPI_WARPS * 32) : "memory");
   }
