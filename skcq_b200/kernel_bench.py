@@ -4,6 +4,8 @@
     python -m skcq_b200.kernel_bench prefill --experts 128 --tokens 16384 --reps 3
     python -m skcq_b200.kernel_bench dequant --experts 32 --reps 3
     python -m skcq_b200.kernel_bench decode --experts 32 --tokens 1 --reps 3
+    python -m skcq_b200.kernel_bench update --metric cosine --bs 8 --K 4096 --blocks 128 --rows 98304 --reps 3
+    python -m skcq_b200.kernel_bench reconstruct --rows 98304 --reps 3
 
 The forward cases build random codebook modules with the config-2 codebook
 shapes (primary bs=8 K=4096 with bf16 scales, residuals bs=16 K=4096 and
@@ -12,8 +14,16 @@ bs=4 K=65536; hidden 2048, intermediate 768) and uniform random indices.
 routing, top-8) with CUDA events; `dequant` decodes one gate projection's
 experts; `decode` runs one routed step of T tokens.
 
+`update` times the Lloyd centroid update (segmented sum of the points into
+their clusters' sums and counts) on random labels; `reconstruct` times one
+streaming reconstruction pass of a gate projection (98304 x 2048 by default)
+from random config-2 codebooks (primary bs=8 K=4096 with bf16 scales, residuals
+bs=16 K=4096 and bs=4 K=65536, int64 indices as in the CWR), as the AQLM
+residual ``raw - sum``.
+
 Prints one JSON line per case with the mean CUDA-event time per launch and the
-algorithmic work rate. Useful as the target of a profiler capture (few launches,
+algorithmic work rate (bytes for the HBM-bound cases, against the measured
+copy bandwidth in MEASURED_PEAKS.json). Useful as the target of a profiler capture (few launches,
 bounded device memory).
 """
 
@@ -69,6 +79,91 @@ def assign_case(metric: int, bs: int, K: int, blocks: int, rows: int, reps: int,
         "issued_tf32_tflops": 2 * pts.kp * elems / (ms / 1e3) / 1e12,
         "a_bytes": A.numel() * 4, "b_bytes": B.numel() * 4,
     }
+
+
+def _hbm_peak() -> float:
+    import json
+    from pathlib import Path
+
+    p = Path(__file__).resolve().parent.parent / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(p.read_text())["hbm_gbs"])
+    except (OSError, KeyError, ValueError):
+        return 6650.0  # fallback measurement on this GPU type
+
+
+def _time(launch, prepare, reps: int, warmup: int) -> float:
+    for _ in range(warmup):
+        prepare()
+        launch()
+    torch.cuda.synchronize()
+    total = 0.0
+    for _ in range(reps):
+        prepare()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        launch()
+        b.record()
+        torch.cuda.synchronize()
+        total += a.elapsed_time(b)
+    _lib.poll_device_error()
+    return total / reps
+
+
+def update_case(metric: int, bs: int, K: int, blocks: int, rows: int, reps: int, warmup: int) -> dict:
+    """skcq_update on random labels. Algorithmic bytes: each point's coordinates
+    and label read once, every cluster's sum and count written once."""
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(0)
+    w = torch.randn(rows, blocks * bs, generator=g, device=dev) * 0.02
+    pts = _engine.gather_block_points(w, bs, blocks, False, 0.0, False, metric)
+    del w
+    k_pad = _engine.round_up(K, _engine.CENT_TILE)
+    k_dev = torch.full((blocks,), K, dtype=torch.int32, device=dev)
+    labels = torch.randint(0, K, (blocks, pts.n_pad), generator=g, device=dev, dtype=torch.int32)
+    sums = torch.empty(blocks, k_pad, bs, device=dev)
+    counts = torch.empty(blocks, k_pad, dtype=torch.int32, device=dev)
+    s = stream()
+
+    def prepare():
+        sums.zero_()
+        counts.zero_()
+
+    ms = _time(lambda: call("skcq_update", ptr(pts.R), ptr(labels), blocks, pts.n_pad, k_pad, bs, ptr(pts.n),
+                            ptr(k_dev), None, ptr(sums), ptr(counts), s), prepare, reps, warmup)
+    n_pts = float(sum(pts.n_host))
+    algo = n_pts * (bs * 4 + 4) + blocks * K * (bs + 1) * 4.0
+    gbs = algo / (ms / 1e3) / 1e9
+    return {"case": "update", "metric": "cosine" if metric == 0 else "l2", "bs": bs, "K": K, "blocks": blocks,
+            "rows": rows, "ms_per_launch": ms, "algorithmic_bytes": algo, "achieved_gbs": gbs,
+            "frac_hbm": gbs / _hbm_peak()}
+
+
+def reconstruct_case(rows: int, reps: int, warmup: int, in_dim: int = 2048) -> dict:
+    """One skcq_reconstruct pass, raw - (primary + 2 residuals). Algorithmic
+    bytes: indices, scales, raw and output streamed once, each centroid table
+    read once."""
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(0)
+    views = []
+    table_bytes = idx_bytes = 0
+    for kind, bs, K, scaled in ((0, 8, 4096, True), (1, 16, 4096, False), (1, 4, 65536, False)):
+        nb = in_dim // bs
+        cent = (torch.randn(nb, bs, K, generator=g, device=dev) * 0.05).to(torch.bfloat16)
+        idxs = torch.randint(0, K, (nb, rows), generator=g, device=dev, dtype=torch.int64)
+        scales = (torch.rand(rows, nb, generator=g, device=dev) * 0.1).to(torch.bfloat16) if scaled else None
+        views.append(_engine.CodecView(kind=kind, bs=bs, n_blocks=nb, K=K, shared=False, cent=cent, idxs=idxs,
+                                       scales=scales))
+        table_bytes += cent.numel() * 2
+        idx_bytes += idxs.numel() * 8 + (scales.numel() * 2 if scales is not None else 0)
+    raw = torch.randn(rows, in_dim, generator=g, device=dev) * 0.02
+    out = torch.empty(rows, in_dim, device=dev)
+    ms = _time(lambda: _engine.reconstruct(views, rows, in_dim, raw=raw, out=out), lambda: None, reps, warmup)
+    algo = float(idx_bytes + table_bytes + raw.numel() * 4 + out.numel() * 4)
+    gbs = algo / (ms / 1e3) / 1e9
+    return {"case": "reconstruct", "rows": rows, "in_dim": in_dim, "ms_per_launch": ms, "algorithmic_bytes": algo,
+            "index_and_scale_bytes": float(idx_bytes), "table_bytes": float(table_bytes), "achieved_gbs": gbs,
+            "frac_hbm": gbs / _hbm_peak()}
 
 
 def _random_module(E: int, out_dim: int, in_dim: int, gen: torch.Generator):
@@ -160,7 +255,7 @@ def forward_case(kind: str, E: int, T: int, reps: int, warmup: int) -> dict:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["assign", "prefill", "dequant", "decode"])
+    ap.add_argument("kernel", choices=["assign", "prefill", "dequant", "decode", "update", "reconstruct"])
     ap.add_argument("--experts", type=int, default=128)
     ap.add_argument("--tokens", type=int, default=16384)
     ap.add_argument("--metric", default="l2", choices=["cosine", "l2"])
@@ -172,11 +267,16 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=1)
     a = ap.parse_args()
     _lib.load()
-    if a.kernel != "assign":
-        print(json.dumps(forward_case(a.kernel, a.experts, a.tokens, a.reps, a.warmup)), flush=True)
-        return
     metric = _engine.COSINE if a.metric == "cosine" else _engine.L2
-    print(json.dumps(assign_case(metric, a.bs, a.K, a.blocks, a.rows, a.reps, a.warmup)), flush=True)
+    if a.kernel == "assign":
+        res = assign_case(metric, a.bs, a.K, a.blocks, a.rows, a.reps, a.warmup)
+    elif a.kernel == "update":
+        res = update_case(metric, a.bs, a.K, a.blocks, a.rows, a.reps, a.warmup)
+    elif a.kernel == "reconstruct":
+        res = reconstruct_case(a.rows, a.reps, a.warmup)
+    else:
+        res = forward_case(a.kernel, a.experts, a.tokens, a.reps, a.warmup)
+    print(json.dumps(res), flush=True)
 
 
 if __name__ == "__main__":
