@@ -13,36 +13,93 @@ namespace skcq {
 // Shared-memory accumulation: one CTA owns a slice of rows of one problem and
 // the whole (k x (bs+1)) accumulator; flushed with one global atomic per
 // touched entry.
-__global__ void update_smem_kernel(const float* __restrict__ R, const int32_t* __restrict__ labels, int n_pad,
-                                   int k_pad, int bs, const int32_t* __restrict__ n,
-                                   const int32_t* __restrict__ active, const int32_t* __restrict__ kvec,
-                                   int rows_per_cta, float* __restrict__ sums, int32_t* __restrict__ counts) {
-  extern __shared__ float acc[];  // [kb][bs] sums then [kb] counts (as int)
+// Per-CTA partial sums in shared memory, flushed to global with atomics.
+// Cluster c's row is acc[c * sp .. c * sp + bs) with its count (as int) in
+// column bs; the row stride sp = (bs + 1) | 1 is odd, so the 32 random clusters
+// a warp touches spread over the banks instead of landing on the few banks a
+// stride of bs (a multiple of 4 or 8) maps them to. Each thread loads the
+// labels and coordinates of UP points before issuing their atomics, to keep
+// several global loads in flight.
+constexpr int UP = 4;
+
+__host__ __device__ constexpr int update_row_stride(int bs) { return (bs + 1) | 1; }
+
+__global__ void __launch_bounds__(512) update_smem_kernel(const float* __restrict__ R,
+                                                           const int32_t* __restrict__ labels, int n_pad,
+                                                           int k_pad, int bs, const int32_t* __restrict__ n,
+                                                           const int32_t* __restrict__ active,
+                                                           const int32_t* __restrict__ kvec, int rows_per_cta,
+                                                           float* __restrict__ sums, int32_t* __restrict__ counts) {
+  extern __shared__ float acc[];  // [kb][sp]: bs sums, then the count (as int)
   const int b = blockIdx.y;
   if (active && !active[b]) return;
   const int nb = n[b], kb = kvec[b];
   const int i0 = blockIdx.x * rows_per_cta;
   if (i0 >= nb) return;
   const int i1 = min(nb, i0 + rows_per_cta);
-  int* cnt = reinterpret_cast<int*>(acc + (size_t)kb * bs);
-  for (int t = threadIdx.x; t < kb * (bs + 1); t += blockDim.x) acc[t] = 0.f;
+  const int sp = update_row_stride(bs);
+  for (int t = threadIdx.x; t < kb * sp; t += blockDim.x) acc[t] = 0.f;
   __syncthreads();
   const float* Rb = R + (int64_t)b * n_pad * bs;
   const int32_t* Lb = labels + (int64_t)b * n_pad;
-  for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
-    const int l = Lb[i];
-    const float* x = Rb + (int64_t)i * bs;
-    for (int j = 0; j < bs; ++j) atomicAdd(&acc[l * bs + j], x[j]);
-    atomicAdd(&cnt[l], 1);
+  const bool vec4 = (bs & 3) == 0;  // rows are 16-byte aligned: R is [nblk][n_pad][bs] from an aligned base
+  for (int base = i0 + threadIdx.x; base < i1; base += UP * blockDim.x) {
+    int l[UP];
+    float x[UP][16];
+#pragma unroll
+    for (int u = 0; u < UP; ++u) {
+      const int i = base + u * blockDim.x;
+      const int v = i < i1 ? Lb[i] : -1;
+      l[u] = v < kb ? v : -1;  // a label outside [0, k) never indexes the accumulator
+    }
+    if (bs <= 16) {
+#pragma unroll
+      for (int u = 0; u < UP; ++u) {
+        if (l[u] < 0) continue;
+        const float* xr = Rb + (int64_t)(base + u * blockDim.x) * bs;
+        if (vec4) {
+#pragma unroll
+          for (int j = 0; j < 16; j += 4) {
+            if (j < bs) {
+              const float4 q = __ldg(reinterpret_cast<const float4*>(xr + j));
+              x[u][j] = q.x; x[u][j + 1] = q.y; x[u][j + 2] = q.z; x[u][j + 3] = q.w;
+            }
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (j < bs) x[u][j] = __ldg(xr + j);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < UP; ++u) {
+        if (l[u] < 0) continue;
+        float* row = acc + (size_t)l[u] * sp;
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          if (j < bs) atomicAdd(row + j, x[u][j]);
+        atomicAdd(reinterpret_cast<int*>(row + bs), 1);
+      }
+    } else {
+#pragma unroll
+      for (int u = 0; u < UP; ++u) {
+        if (l[u] < 0) continue;
+        const float* xr = Rb + (int64_t)(base + u * blockDim.x) * bs;
+        float* row = acc + (size_t)l[u] * sp;
+        for (int j = 0; j < bs; ++j) atomicAdd(row + j, xr[j]);
+        atomicAdd(reinterpret_cast<int*>(row + bs), 1);
+      }
+    }
   }
   __syncthreads();
   float* Sb = sums + (int64_t)b * k_pad * bs;
   int32_t* Cb = counts + (int64_t)b * k_pad;
   for (int c = threadIdx.x; c < kb; c += blockDim.x) {
-    const int m = cnt[c];
+    const float* row = acc + (size_t)c * sp;
+    const int m = __float_as_int(row[bs]);
     if (m == 0) continue;
     atomicAdd(&Cb[c], m);
-    for (int j = 0; j < bs; ++j) atomicAdd(&Sb[c * bs + j], acc[c * bs + j]);
+    for (int j = 0; j < bs; ++j) atomicAdd(&Sb[c * bs + j], row[j]);
   }
 }
 
@@ -294,7 +351,7 @@ extern "C" int skcq_update(const float* R, const int32_t* labels, int nblk, int 
   SKCQ_REQUIRE(R && labels && n && k && sums && counts, SKCQ_ERR_INVALID, "update: null pointer");
   SKCQ_REQUIRE(bs > 0 && bs <= 64, SKCQ_ERR_INVALID, "update: bad block size %d", bs);
   cudaStream_t s = (cudaStream_t)stream;
-  const size_t smem = (size_t)k_pad * (bs + 1) * sizeof(float);
+  const size_t smem = (size_t)k_pad * update_row_stride(bs) * sizeof(float);
   if (smem <= 160 * 1024 && nblk <= 65535) {
     static thread_local int configured_dev = -1;
     int dev = 0;
