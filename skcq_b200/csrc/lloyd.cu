@@ -14,45 +14,52 @@ namespace skcq {
 // the whole (k x (bs+1)) accumulator; flushed with one global atomic per
 // touched entry.
 // Per-CTA partial sums in shared memory, flushed to global with atomics.
-// Cluster c's row is acc[c * sp .. c * sp + bs) with its count (as int) in
-// column bs; the row stride sp = (bs + 1) | 1 is odd, so the 32 random clusters
+// blockIdx.z selects a pass over columns [j0, j0 + jn) of the points (several
+// passes when a cluster row of all bs sums does not fit); pass 0 also counts.
+// Cluster c's row is acc[c * sp .. c * sp + jn) with its count (as int) in
+// column jn; the row stride sp = (jn + 1) | 1 is odd, so the 32 random clusters
 // a warp touches spread over the banks instead of landing on the few banks a
-// stride of bs (a multiple of 4 or 8) maps them to. Each thread loads the
+// stride that is a multiple of 4 or 8 maps them to. Each thread loads the
 // labels and coordinates of UP points before issuing their atomics, to keep
 // several global loads in flight.
 constexpr int UP = 4;
+constexpr int UPDATE_SMEM = 160 * 1024;
 
-__host__ __device__ constexpr int update_row_stride(int bs) { return (bs + 1) | 1; }
+__host__ __device__ constexpr int update_row_stride(int jn) { return (jn + 1) | 1; }
 
 __global__ void __launch_bounds__(512) update_smem_kernel(const float* __restrict__ R,
-                                                           const int32_t* __restrict__ labels, int n_pad,
-                                                           int k_pad, int bs, const int32_t* __restrict__ n,
-                                                           const int32_t* __restrict__ active,
-                                                           const int32_t* __restrict__ kvec, int rows_per_cta,
-                                                           float* __restrict__ sums, int32_t* __restrict__ counts) {
-  extern __shared__ float acc[];  // [kb][sp]: bs sums, then the count (as int)
+                                                          const int32_t* __restrict__ labels, int n_pad, int k_pad,
+                                                          int bs, int cols_per_pass, const int32_t* __restrict__ n,
+                                                          const int32_t* __restrict__ active,
+                                                          const int32_t* __restrict__ kvec, int rows_per_cta,
+                                                          float* __restrict__ sums, int32_t* __restrict__ counts) {
+  extern __shared__ float acc[];  // [kb][sp]: jn sums, then the count (as int)
   const int b = blockIdx.y;
   if (active && !active[b]) return;
   const int nb = n[b], kb = kvec[b];
   const int i0 = blockIdx.x * rows_per_cta;
   if (i0 >= nb) return;
   const int i1 = min(nb, i0 + rows_per_cta);
-  const int sp = update_row_stride(bs);
+  const int j0 = blockIdx.z * cols_per_pass;
+  const int jn = min(cols_per_pass, bs - j0);
+  const bool counting = blockIdx.z == 0;
+  const int sp = update_row_stride(jn);
   for (int t = threadIdx.x; t < kb * sp; t += blockDim.x) acc[t] = 0.f;
   __syncthreads();
-  const float* Rb = R + (int64_t)b * n_pad * bs;
+  const float* Rb = R + (int64_t)b * n_pad * bs + j0;
   const int32_t* Lb = labels + (int64_t)b * n_pad;
-  const bool vec4 = (bs & 3) == 0;  // rows are 16-byte aligned: R is [nblk][n_pad][bs] from an aligned base
+  // rows are 16-byte aligned: R is [nblk][n_pad][bs] from an aligned base
+  const bool vec4 = (bs & 3) == 0 && (j0 & 3) == 0 && (jn & 3) == 0;
   for (int base = i0 + threadIdx.x; base < i1; base += UP * blockDim.x) {
     int l[UP];
-    float x[UP][16];
 #pragma unroll
     for (int u = 0; u < UP; ++u) {
       const int i = base + u * blockDim.x;
       const int v = i < i1 ? Lb[i] : -1;
       l[u] = v < kb ? v : -1;  // a label outside [0, k) never indexes the accumulator
     }
-    if (bs <= 16) {
+    if (jn <= 16) {
+      float x[UP][16];
 #pragma unroll
       for (int u = 0; u < UP; ++u) {
         if (l[u] < 0) continue;
@@ -60,7 +67,7 @@ __global__ void __launch_bounds__(512) update_smem_kernel(const float* __restric
         if (vec4) {
 #pragma unroll
           for (int j = 0; j < 16; j += 4) {
-            if (j < bs) {
+            if (j < jn) {
               const float4 q = __ldg(reinterpret_cast<const float4*>(xr + j));
               x[u][j] = q.x; x[u][j + 1] = q.y; x[u][j + 2] = q.z; x[u][j + 3] = q.w;
             }
@@ -68,7 +75,7 @@ __global__ void __launch_bounds__(512) update_smem_kernel(const float* __restric
         } else {
 #pragma unroll
           for (int j = 0; j < 16; ++j)
-            if (j < bs) x[u][j] = __ldg(xr + j);
+            if (j < jn) x[u][j] = __ldg(xr + j);
         }
       }
 #pragma unroll
@@ -77,8 +84,8 @@ __global__ void __launch_bounds__(512) update_smem_kernel(const float* __restric
         float* row = acc + (size_t)l[u] * sp;
 #pragma unroll
         for (int j = 0; j < 16; ++j)
-          if (j < bs) atomicAdd(row + j, x[u][j]);
-        atomicAdd(reinterpret_cast<int*>(row + bs), 1);
+          if (j < jn) atomicAdd(row + j, x[u][j]);
+        if (counting) atomicAdd(reinterpret_cast<int*>(row + jn), 1);
       }
     } else {
 #pragma unroll
@@ -86,20 +93,25 @@ __global__ void __launch_bounds__(512) update_smem_kernel(const float* __restric
         if (l[u] < 0) continue;
         const float* xr = Rb + (int64_t)(base + u * blockDim.x) * bs;
         float* row = acc + (size_t)l[u] * sp;
-        for (int j = 0; j < bs; ++j) atomicAdd(row + j, xr[j]);
-        atomicAdd(reinterpret_cast<int*>(row + bs), 1);
+        for (int j = 0; j < jn; ++j) atomicAdd(row + j, xr[j]);
+        if (counting) atomicAdd(reinterpret_cast<int*>(row + jn), 1);
       }
     }
   }
   __syncthreads();
-  float* Sb = sums + (int64_t)b * k_pad * bs;
+  float* Sb = sums + (int64_t)b * k_pad * bs + j0;
   int32_t* Cb = counts + (int64_t)b * k_pad;
   for (int c = threadIdx.x; c < kb; c += blockDim.x) {
     const float* row = acc + (size_t)c * sp;
-    const int m = __float_as_int(row[bs]);
-    if (m == 0) continue;
-    atomicAdd(&Cb[c], m);
-    for (int j = 0; j < bs; ++j) atomicAdd(&Sb[c * bs + j], row[j]);
+    if (counting) {
+      const int m = __float_as_int(row[jn]);
+      if (m == 0) continue;
+      atomicAdd(&Cb[c], m);
+    }
+    for (int j = 0; j < jn; ++j) {
+      const float v = row[j];
+      if (v != 0.f || counting) atomicAdd(&Sb[(int64_t)c * bs + j], v);
+    }
   }
 }
 
@@ -351,13 +363,17 @@ extern "C" int skcq_update(const float* R, const int32_t* labels, int nblk, int 
   SKCQ_REQUIRE(R && labels && n && k && sums && counts, SKCQ_ERR_INVALID, "update: null pointer");
   SKCQ_REQUIRE(bs > 0 && bs <= 64, SKCQ_ERR_INVALID, "update: bad block size %d", bs);
   cudaStream_t s = (cudaStream_t)stream;
-  const size_t smem = (size_t)k_pad * update_row_stride(bs) * sizeof(float);
-  if (smem <= 160 * 1024 && nblk <= 65535) {
+  // columns per pass: all bs if a cluster row fits, else the widest split that does
+  int cpp = bs;
+  while (cpp > 1 && (size_t)k_pad * update_row_stride(cpp) * sizeof(float) > (size_t)UPDATE_SMEM) cpp = (cpp + 1) / 2;
+  const size_t smem = (size_t)k_pad * update_row_stride(cpp) * sizeof(float);
+  const int passes = (bs + cpp - 1) / cpp;
+  if (smem <= (size_t)UPDATE_SMEM && nblk <= 65535 && passes <= 8) {
     static thread_local int configured_dev = -1;
     int dev = 0;
     cudaGetDevice(&dev);
     if (configured_dev != dev) {
-      cudaError_t e = cudaFuncSetAttribute(update_smem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+      cudaError_t e = cudaFuncSetAttribute(update_smem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, UPDATE_SMEM);
       if (e != cudaSuccess) return set_error(SKCQ_ERR_CUDA, "update: %s", cudaGetErrorString(e));
       configured_dev = dev;
     }
@@ -368,8 +384,9 @@ extern "C" int skcq_update(const float* R, const int32_t* labels, int nblk, int 
     int64_t min_rpc = (int64_t)k_pad * 4;
     if (rpc < min_rpc) rpc = min_rpc;
     if (rpc > n_pad) rpc = n_pad;
-    dim3 grid((unsigned)((n_pad + rpc - 1) / rpc), nblk);
-    update_smem_kernel<<<grid, 512, smem, s>>>(R, labels, n_pad, k_pad, bs, n, active, k, (int)rpc, sums, counts);
+    dim3 grid((unsigned)((n_pad + rpc - 1) / rpc), nblk, passes);
+    update_smem_kernel<<<grid, 512, smem, s>>>(R, labels, n_pad, k_pad, bs, cpp, n, active, k, (int)rpc, sums,
+                                               counts);
     return check_launch("update (shared)");
   }
   int64_t work = (int64_t)nblk * n_pad;
