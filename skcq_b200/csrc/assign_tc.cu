@@ -28,9 +28,10 @@
 // while the tensor core is busy, not after both.
 // Operands are split-tf32 (hi/lo) so A.B reproduces the fp32 dot product to
 // ~2^-21 relative.
-// Kernel 2 -- refine: one thread per point re-scores the 32 centroids of its
-// winning group with the exact fp32 reference formula (first maximum wins),
-// reading the problem's centroid table from shared-memory slices.
+// Kernel 2 -- refine (both forms): one warp per point re-scores the 32
+// centroids of its winning group, one centroid per lane, with the exact fp32
+// reference formula (first maximum wins), reading the problem's centroid table
+// from transposed shared-memory slices.
 #include <algorithm>
 
 #include "assign_ss.cuh"
