@@ -119,7 +119,9 @@ int skcq_update(const float* R, const int32_t* labels, int nblk, int n_pad, int 
  * <x, c_label>; euclidean: largest ||x - c_label||^2; ties by point index)
  * are written, in that order, into the sums of the empty clusters in
  * ascending cluster order. n_empty[b] receives the count. `scratch` must hold
- * skcq_reseed_scratch_bytes(nblk, k_pad) bytes. */
+ * skcq_reseed_scratch_bytes(nblk, k_pad) bytes. k_pad must be a multiple of
+ * SKCQ_CENT_TILE and at most 1048576 (skcq_reseed_scratch_bytes returns 0
+ * beyond that). */
 size_t skcq_reseed_scratch_bytes(int nblk, int k_pad);
 int skcq_reseed(int metric, const float* X, const float* C, const int32_t* labels, int nblk, int n_pad, int k_pad,
                 int bs, const int32_t* n, const int32_t* k, const int32_t* active, float* sums,
@@ -132,7 +134,10 @@ int skcq_reseed(int metric, const float* X, const float* C, const int32_t* label
  * The scratch is a 16 MiB array compiled into the library, held by every GPU
  * that loads it until the process exits; problems with k_pad above 1048576
  * are rejected with SKCQ_ERR_INVALID. The first call on a device looks up the
- * array's device address (make that first call before any stream capture).
+ * array's device address (make that first call before any stream capture);
+ * the address is cached for the life of the process, so the entry point must
+ * not be used across a cudaDeviceReset. k_pad must be a multiple of
+ * SKCQ_CENT_TILE (as for skcq_reseed).
  * All calls share the array: the kernel writes every scratch word before
  * reading it, so no state carries over, but calls that overlap on the GPU
  * (e.g. on two streams) race and must be serialised by the caller. Allocates

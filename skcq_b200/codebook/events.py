@@ -103,38 +103,53 @@ class Experiment:
 
 
 class TqdmListener:
-    """Progress on stderr (events.py:109-151): one bar ticking per block for
-    per-block codebooks, one bar ticking per iteration for a shared codebook."""
+    """Console progress of k-means fits on stderr.
+
+    One bar per fit, measured in block-iterations: a per-block fit of
+    ``n_blocks`` problems gets ``n_blocks * max_iters`` units and advances by
+    each block's ``iters_run`` when it finishes (a block that converges early
+    skips its remaining units); a single (shared) problem advances by one unit
+    per Lloyd iteration. The postfix shows how many blocks converged, or the
+    last movement and empty-cluster count of a single problem. Register
+    ``on_start`` / ``on_iter`` / ``on_done`` for the three k-means events.
+    """
 
     def __init__(self) -> None:
-        self._pbar: tqdm | None = None
-        self._n_blocks = 1
-        self._block_mode = False
+        self._bar: tqdm | None = None
+        self._blocks_left = 0
+        self._blocks_total = 0
+        self._converged = 0
+        self._units_per_block = 0
+
+    def _finish(self) -> None:
+        if self._bar is not None:
+            self._bar.close()
+        self._bar = None
 
     def on_start(self, e: KmeansStartEvent) -> None:
-        if e.n_blocks > 1:
-            if self._pbar is not None:
-                return
-            self._block_mode, self._n_blocks = True, e.n_blocks
-            self._pbar = tqdm(total=e.n_blocks, desc=e.name.split(" blk=")[0], leave=True)
-        else:
-            self._block_mode = False
-            self._pbar = tqdm(total=e.max_iters, desc=e.name, leave=True)
+        if self._bar is not None and self._blocks_left > 0 and e.n_blocks == self._blocks_total:
+            return  # the next block of the fit whose bar is open
+        self._finish()
+        self._blocks_total = self._blocks_left = max(e.n_blocks, 1)
+        self._converged = 0
+        self._units_per_block = e.max_iters
+        title = e.name.partition(" blk=")[0]
+        self._bar = tqdm(total=self._blocks_total * e.max_iters, desc=title, unit="blk-it", leave=True)
 
     def on_iter(self, e: KmeansIterEvent) -> None:
-        if self._pbar is not None and not self._block_mode:
-            self._pbar.update(1)
-            self._pbar.set_postfix(moved=f"{e.moved:.6f}", empty=e.n_empty)
+        if self._bar is None or self._blocks_total > 1:
+            return
+        self._bar.update(1)
+        self._bar.set_postfix_str(f"moved {e.moved:.3g}, {e.n_empty} empty", refresh=False)
 
     def on_done(self, e: KmeansDoneEvent) -> None:
-        if self._pbar is None:
+        if self._bar is None:
             return
-        if self._block_mode:
-            self._pbar.update(1)
-            self._pbar.set_postfix(iters=e.iters_run, conv=int(e.converged), moved=f"{e.final_moved:.6f}")
-            if self._pbar.n >= self._n_blocks:
-                self._pbar.close()
-                self._pbar = None
-        else:
-            self._pbar.close()
-            self._pbar = None
+        self._converged += int(e.converged)
+        if self._blocks_total > 1:
+            # unused iterations of an early-converged block are skipped over
+            self._bar.update(self._units_per_block)
+            self._bar.set_postfix_str(f"{self._converged}/{self._blocks_total} converged", refresh=False)
+        self._blocks_left -= 1
+        if self._blocks_left <= 0:
+            self._finish()

@@ -11,6 +11,7 @@ on the GPU.
 
 from __future__ import annotations
 
+from dataclasses import dataclass
 from pathlib import Path
 from typing import Any
 
@@ -24,7 +25,8 @@ from skcq_b200.codebook.euclidean import EuclideanCodebook, EuclideanCodebookCon
 from skcq_b200.codebook.spherical import SphericalCodebook, SphericalCodebookConfig
 from skcq_b200.codebook.ssvq import SSVQCodebook
 
-__all__ = ["CodebookParams", "LayerOverride", "ExperimentConfig", "build_aqlm_codebook"]
+__all__ = ["CodebookParams", "LayerOverride", "ExperimentConfig", "build_aqlm_codebook", "CodecSpec",
+           "assemble_aqlm"]
 
 
 class CodebookParams(BaseModel):
@@ -118,6 +120,48 @@ def _resolve_residual_ss(residual_ss: bool | list[bool] | None, n_codebooks: int
     return list(residual_ss[:n_codebooks]) + [False] * (n_codebooks - len(residual_ss))
 
 
+@dataclass(frozen=True)
+class CodecSpec:
+    """One codebook of a composite: its metric ("cosine" = spherical directions
+    with per-row scales, "euclidean" = plain centroids), block size, K, SSVQ
+    sign split, and the options of its k-means fit."""
+
+    metric: str
+    block_size: int
+    K: int
+    sign_split: bool = False
+    skip_zeros: bool = True
+    shared: bool = False
+    max_train_samples: int = 0
+
+
+def make_codec(spec: CodecSpec, *, max_iters: int, norm_threshold: float, chunk_budget_mb: int,
+               device: torch.device | None) -> WeightsCodebookBase:
+    """The B200 codec a spec describes, SSVQ-wrapped when it is sign-split."""
+    cls, cfg_cls = ((SphericalCodebook, SphericalCodebookConfig) if spec.metric == "cosine"
+                    else (EuclideanCodebook, EuclideanCodebookConfig))
+    codec: WeightsCodebookBase = cls(cfg_cls(
+        block_size=spec.block_size, K=spec.K, shared=spec.shared, max_iters=max_iters,
+        norm_threshold=norm_threshold, skip_zeros=spec.skip_zeros, chunk_budget_mb=chunk_budget_mb, device=device,
+        max_train_samples=spec.max_train_samples,
+    ))
+    return SSVQCodebook(codec) if spec.sign_split else codec
+
+
+def assemble_aqlm(specs: list[CodecSpec], *, max_iters: int, norm_threshold: float, codebook_bits: int,
+                  out_dim: int | None, num_experts: int | None, device: torch.device | None = None,
+                  chunk_budget_mb: int = 2048) -> AQLMCodebook:
+    """A composite from its codebook specs, primary first."""
+    codecs = [make_codec(sp, max_iters=max_iters, norm_threshold=norm_threshold, chunk_budget_mb=chunk_budget_mb,
+                         device=device) for sp in specs]
+    return AQLMCodebook(
+        primary=codecs[0],
+        residuals=codecs[1:],
+        config=AQLMCodebookConfig(codebook_bits=codebook_bits, norm_threshold=norm_threshold, device=device,
+                                  out_dim=out_dim, num_experts=num_experts),
+    )
+
+
 def build_aqlm_codebook(
     params: CodebookParams,
     k: int,
@@ -129,27 +173,16 @@ def build_aqlm_codebook(
     device: torch.device | None = None,
     name: str = "",
 ) -> AQLMCodebook:
-    """One projection's AQLM codebook (config.py:137-197)."""
+    """One projection's AQLM codebook (config.py:137-197): a spherical primary
+    of block size in_dim // n_blocks (never sign-split), euclidean residuals
+    fitted with skip_zeros=False, 16-bit centroids."""
     primary_bs = in_dim // n_blocks if n_blocks > 0 else in_dim
     bs_list = _per_codebook(params.residual_block_sizes, primary_bs, n_codebooks)
     k_list = _per_codebook(params.residual_k, k, n_codebooks)
     ss_list = _resolve_residual_ss(params.residual_sign_split, n_codebooks)
-    primary = SphericalCodebook(SphericalCodebookConfig(
-        block_size=primary_bs, K=k, max_iters=params.max_iters, norm_threshold=params.norm_threshold,
-        skip_zeros=params.skip_zeros, chunk_budget_mb=params.chunk_budget_mb, device=device,
-    ))
-    residuals: list[WeightsCodebookBase] = []
-    for c in range(1, n_codebooks):
-        euc: WeightsCodebookBase = EuclideanCodebook(EuclideanCodebookConfig(
-            block_size=bs_list[c], K=k_list[c], max_iters=params.max_iters, norm_threshold=params.norm_threshold,
-            skip_zeros=False, chunk_budget_mb=params.chunk_budget_mb, device=device,
-        ))
-        if ss_list[c]:
-            euc = SSVQCodebook(euc)
-        residuals.append(euc)
-    return AQLMCodebook(
-        primary=primary,
-        residuals=residuals,
-        config=AQLMCodebookConfig(codebook_bits=16, norm_threshold=params.norm_threshold, device=device,
-                                  out_dim=out_dim, num_experts=num_experts or None),
-    )
+    specs = [CodecSpec("cosine", primary_bs, k, skip_zeros=params.skip_zeros)]
+    specs += [CodecSpec("euclidean", bs_list[c], k_list[c], sign_split=ss_list[c], skip_zeros=False)
+              for c in range(1, n_codebooks)]
+    return assemble_aqlm(specs, max_iters=params.max_iters, norm_threshold=params.norm_threshold, codebook_bits=16,
+                         out_dim=out_dim, num_experts=num_experts or None, device=device,
+                         chunk_budget_mb=params.chunk_budget_mb)

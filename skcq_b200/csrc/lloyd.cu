@@ -396,16 +396,21 @@ extern "C" int skcq_update(const float* R, const int32_t* labels, int nblk, int 
   return check_launch("update (global)");
 }
 
+// Largest centroid count a reseed accepts (the reseed's per-problem scratch
+// holds k_pad ids and a pow2(k_pad) sort list; beyond this the int arithmetic
+// below would overflow).
+constexpr int RESEED_MAX_KPAD = 1 << 20;
+
 static int pow2_at_least(int v) {
   int p = 1;
-  while (p < v) p <<= 1;
+  while (p < v && p < RESEED_MAX_KPAD) p <<= 1;
   return p;
 }
 
 static int reseed_grid(int nblk) { return nblk < 296 ? nblk : 296; }
 
 extern "C" size_t skcq_reseed_scratch_bytes(int nblk, int k_pad) {
-  if (nblk <= 0 || k_pad <= 0) return 0;
+  if (nblk <= 0 || k_pad <= 0 || k_pad > RESEED_MAX_KPAD) return 0;
   return (size_t)reseed_grid(nblk) * ((size_t)k_pad * 4 + (size_t)pow2_at_least(k_pad) * 8);
 }
 
@@ -415,6 +420,9 @@ extern "C" int skcq_reseed(int metric, const float* X, const float* C, const int
   SKCQ_REQUIRE(X && C && labels && n && k && sums && counts && n_empty && scratch, SKCQ_ERR_INVALID,
                "reseed: null pointer");
   SKCQ_REQUIRE(bs > 0 && bs <= 64, SKCQ_ERR_INVALID, "reseed: bad block size %d", bs);
+  SKCQ_REQUIRE(k_pad > 0 && k_pad <= RESEED_MAX_KPAD && k_pad % SKCQ_CENT_TILE == 0, SKCQ_ERR_INVALID,
+               "reseed: k_pad %d must be a positive multiple of %d, at most %d", k_pad, SKCQ_CENT_TILE,
+               RESEED_MAX_KPAD);
   SKCQ_REQUIRE(((uintptr_t)scratch & 7) == 0, SKCQ_ERR_INVALID, "reseed: scratch must be 8-byte aligned");
   int* err = device_error_word();
   SKCQ_REQUIRE(err != nullptr, SKCQ_ERR_CUDA, "reseed: no device error word");
@@ -434,6 +442,9 @@ extern "C" int skcq_reseed_candidates(int metric, const float* X, const float* C
   SKCQ_REQUIRE(X && C && labels && n && k && counts && gofs && keys && vecs && n_empty && scratch, SKCQ_ERR_INVALID,
                "reseed_candidates: null pointer");
   SKCQ_REQUIRE(bs > 0 && bs <= 64 && m_max > 0, SKCQ_ERR_INVALID, "reseed_candidates: bs %d, m_max %d", bs, m_max);
+  SKCQ_REQUIRE(k_pad > 0 && k_pad <= RESEED_MAX_KPAD && k_pad % SKCQ_CENT_TILE == 0, SKCQ_ERR_INVALID,
+               "reseed_candidates: k_pad %d must be a positive multiple of %d, at most %d", k_pad, SKCQ_CENT_TILE,
+               RESEED_MAX_KPAD);
   SKCQ_REQUIRE(((uintptr_t)scratch & 7) == 0, SKCQ_ERR_INVALID, "reseed_candidates: scratch must be 8-byte aligned");
   int* err = device_error_word();
   SKCQ_REQUIRE(err != nullptr, SKCQ_ERR_CUDA, "reseed_candidates: no device error word");
@@ -475,7 +486,9 @@ static __device__ __align__(256) uint8_t g_reseed_scratch[RESEED_STATIC_BYTES];
 
 // Device address of g_reseed_scratch on the current device. The host-side
 // symbol is only a stand-in, so the address is looked up once per device (with
-// that device current) and cached.
+// that device current) and cached for the life of the process. The cache is
+// not refreshed after cudaDeviceReset (or any re-creation of the device's
+// primary context): the entry point must not be used across a device reset.
 static int reseed_static_scratch(void** out) {
   static std::mutex mu;
   static void* addr[64] = {nullptr};
@@ -503,6 +516,12 @@ extern "C" int skcq_reseed_noalloc(int metric, const float* X, const float* C, c
                "reseed_noalloc: null pointer");
   SKCQ_REQUIRE(bs > 0 && bs <= 64, SKCQ_ERR_INVALID, "reseed_noalloc: bad block size %d", bs);
   SKCQ_REQUIRE(nblk > 0 && k_pad > 0, SKCQ_ERR_INVALID, "reseed_noalloc: empty problem set");
+  SKCQ_REQUIRE(k_pad % SKCQ_CENT_TILE == 0, SKCQ_ERR_INVALID, "reseed_noalloc: k_pad %d not a multiple of %d", k_pad,
+               SKCQ_CENT_TILE);
+  SKCQ_REQUIRE(k_pad <= RESEED_MAX_KPAD, SKCQ_ERR_INVALID,
+               "reseed_noalloc: k_pad %d over the static buffer's limit of %d centroids per problem; use "
+               "skcq_reseed with caller scratch",
+               k_pad, RESEED_MAX_KPAD);
   const size_t per_slot = (size_t)k_pad * 4 + (size_t)pow2_at_least(k_pad) * 8;
   SKCQ_REQUIRE(per_slot <= RESEED_STATIC_BYTES, SKCQ_ERR_INVALID,
                "reseed_noalloc: k_pad %d needs %zu scratch bytes per problem, over the %zu-byte static buffer "

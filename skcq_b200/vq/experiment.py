@@ -19,10 +19,9 @@ from dataclasses import dataclass
 
 import torch
 
-from skcq_b200.codebook.aqlm import AQLMCodebook, AQLMCodebookConfig
-from skcq_b200.codebook.base import DistanceMetric, WeightsCodebookBase
+from skcq_b200.codebook.aqlm import AQLMCodebook
+from skcq_b200.codebook.base import DistanceMetric
 from skcq_b200.codebook.cwr import SSVQCWR, SphericalCWR
-from skcq_b200.codebook.euclidean import EuclideanCodebook, EuclideanCodebookConfig
 from skcq_b200.codebook.events import (
     CodebookDoneEvent,
     CodebookIterEvent,
@@ -32,13 +31,9 @@ from skcq_b200.codebook.events import (
     KmeansIterEvent,
     KmeansStartEvent,
 )
-from skcq_b200.codebook.spherical import (
-    SphericalCodebook,
-    SphericalCodebookConfig,
-    quantize_spherical_scales,
-    scale_bits_per_elem,
-)
+from skcq_b200.codebook.spherical import SphericalCodebook, quantize_spherical_scales, scale_bits_per_elem
 from skcq_b200.codebook.ssvq import SSVQCodebook
+from skcq_b200.config import CodecSpec, _per_codebook, _resolve_residual_ss, assemble_aqlm
 from skcq_b200.vq.bpw import bits_per_weight_kmeans
 
 logger = logging.getLogger(__name__)
@@ -88,109 +83,123 @@ class VQRunConfig:
     cache_key_str: str | None = None
 
 
-def _per_residual(value, n: int, primary):
-    """Per-codebook values: the primary's, then residual c's from a scalar or a
-    list indexed c - 1 (experiment.py:97-125)."""
-    if value is None:
-        return [primary] * n
-    if isinstance(value, list):
-        return [primary if c == 0 else value[c - 1] for c in range(n)]
-    return [primary if c == 0 else value for c in range(n)]
+_CHILD_EVENTS = (CodebookStartEvent, CodebookIterEvent, CodebookDoneEvent, KmeansStartEvent, KmeansIterEvent,
+                 KmeansDoneEvent)
+_NORM_THRESHOLD = 0.001  # the sweep's zero-block threshold (experiment.py:181)
+_SHARED_TRAIN_SAMPLES = 1 << 23  # training subsample of a shared primary (experiment.py:183)
+
+
+@dataclass(frozen=True)
+class _Plan:
+    """What one sweep configuration fits: per-codebook specs (primary first)
+    and the figures its result row reports."""
+
+    specs: list[CodecSpec]
+    label: str
+    config_id: str
+    out_dim: int
+
+    @property
+    def block_sizes(self) -> list[int]:
+        return [sp.block_size for sp in self.specs]
+
+    @property
+    def ks(self) -> list[int]:
+        return [sp.K for sp in self.specs]
+
+    @property
+    def residual_sign_split(self) -> list[bool]:
+        return [sp.sign_split for sp in self.specs[1:]]
+
+
+def _plan(cfg: VQRunConfig) -> _Plan:
+    """Per-codebook block sizes, K and sign splits of a configuration. The
+    primary takes the configuration's own values; a residual takes its entry of
+    a per-codebook list, else the shared scalar, else the primary's. A zero
+    residual K means "same as the primary". Only a spherical primary is
+    sign-split; it alone skips zero blocks and subsamples when shared."""
+    n = cfg.n_codebooks
+    res_k = cfg.residual_k if isinstance(cfg.residual_k, list) else (cfg.residual_k or None)
+    ks = _per_codebook(res_k, cfg.K, n)
+    bss = _per_codebook(cfg.residual_block_sizes, cfg.block_size, n)
+    res_ss = _resolve_residual_ss(cfg.residual_sign_split, n - 1)
+    cosine = cfg.metric == "cosine"
+    specs = [CodecSpec(cfg.metric, cfg.block_size, cfg.K, sign_split=cosine and cfg.sign_split, skip_zeros=True,
+                       shared=cfg.shared_codebook,
+                       max_train_samples=_SHARED_TRAIN_SAMPLES if cfg.shared_codebook else 0)]
+    specs += [CodecSpec("euclidean", bss[c], ks[c], sign_split=res_ss[c - 1], skip_zeros=False,
+                        shared=cfg.shared_codebook) for c in range(1, n)]
+    # scheme label: the reference's naming, which sweep tables key on
+    parts = "-".join(f"cb{c}_b{sp.block_size}k{sp.K}" for c, sp in enumerate(specs))
+    tags = [cfg.metric[:3], "shared" if cfg.shared_codebook else "perblock", "ssvq" if cfg.sign_split else "nosign"]
+    label = f"kmeans_{parts}_" + "_".join(tags)
+    if cfg.scale_dtype != "bf16":
+        label += f"_{cfg.scale_dtype}"
+    if cfg.codebook_bits < 16:
+        label += f"_cb{cfg.codebook_bits}"
+    out_dim = cfg.hidden_size if cfg.projection == "down" else cfg.intermediate_size
+    return _Plan(specs, label, f"L{cfg.layer_idx}.{cfg.projection}.{label}", out_dim)
+
+
+def _spherical_primary(aqlm: AQLMCodebook, cwr) -> tuple[SphericalCodebook, SphericalCWR] | None:
+    """The spherical codec and payload under a (possibly sign-split) primary."""
+    codec, payload = aqlm.primary, cwr.primary
+    if isinstance(codec, SSVQCodebook):
+        codec = codec.inner
+        payload = payload.inner if isinstance(payload, SSVQCWR) else payload
+    if isinstance(codec, SphericalCodebook) and isinstance(payload, SphericalCWR):
+        return codec, payload
+    return None
 
 
 class VQRunExperiment(Experiment):
-    """One VQ configuration run (experiment.py:87-307)."""
+    """One VQ configuration run (experiment.py:87-307): fit, quantise the
+    primary scales, measure rel_fro_err and bits per weight, emit the row."""
 
     def __init__(self, config: VQRunConfig) -> None:
         super().__init__()
         self.config = config
         self._result: dict | None = None
 
-    def fit(self, W_raw: torch.Tensor) -> dict:  # noqa: N803
+    def _row(self, plan: _Plan, err: float, bpw: float) -> dict:
         cfg = self.config
-        device = cfg.device
-        n_rows = W_raw.shape[0]
-        w_norm = W_raw.float().norm().item()
-        n_blocks = cfg.in_dim // cfg.block_size
-        k_per = [cfg.K if c == 0 else (cfg.residual_k or cfg.K) for c in range(cfg.n_codebooks)] \
-            if isinstance(cfg.residual_k, int | None) else _per_residual(cfg.residual_k, cfg.n_codebooks, cfg.K)
-        bs_per = _per_residual(cfg.residual_block_sizes, cfg.n_codebooks, cfg.block_size)
-        if cfg.residual_sign_split is None:
-            res_ss = [False] * (cfg.n_codebooks - 1)
-        elif isinstance(cfg.residual_sign_split, bool):
-            res_ss = [cfg.residual_sign_split] * (cfg.n_codebooks - 1)
-        else:
-            res_ss = list(cfg.residual_sign_split[: cfg.n_codebooks - 1])
-            res_ss += [False] * (cfg.n_codebooks - 1 - len(res_ss))
-        sign_split = [cfg.sign_split, *res_ss]
-
-        cb_id = "-".join(f"cb{c}_b{bs_per[c]}k{k_per[c]}" for c in range(cfg.n_codebooks))
-        scale_tag = f"_{cfg.scale_dtype}" if cfg.scale_dtype != "bf16" else ""
-        cb_qtag = f"_cb{cfg.codebook_bits}" if cfg.codebook_bits < 16 else ""
-        label = (f"kmeans_{cb_id}_{cfg.metric[:3]}_{'shared' if cfg.shared_codebook else 'perblock'}_"
-                 f"{'ssvq' if cfg.sign_split else 'nosign'}{scale_tag}{cb_qtag}")
-        out_dim = cfg.intermediate_size if cfg.projection != "down" else cfg.hidden_size
-        config_id = f"L{cfg.layer_idx}.{cfg.projection}.{label}"
-        self._emit(VQStartEvent(config_id=config_id, projection=cfg.projection, block_size=cfg.block_size, K=cfg.K,
-                                n_codebooks=cfg.n_codebooks, metric=cfg.metric))
-
-        sub = 2**23 if cfg.shared_codebook else 0
-        primary: WeightsCodebookBase
-        if cfg.metric == "cosine":
-            primary = SphericalCodebook(SphericalCodebookConfig(
-                block_size=cfg.block_size, K=cfg.K, shared=cfg.shared_codebook, max_iters=cfg.max_iters,
-                norm_threshold=0.001, skip_zeros=True, chunk_budget_mb=cfg.chunk_budget_mb, device=device,
-                max_train_samples=sub))
-            if cfg.sign_split:
-                primary = SSVQCodebook(primary)
-        else:
-            primary = EuclideanCodebook(EuclideanCodebookConfig(
-                block_size=cfg.block_size, K=cfg.K, shared=cfg.shared_codebook, max_iters=cfg.max_iters,
-                norm_threshold=0.001, skip_zeros=True, chunk_budget_mb=cfg.chunk_budget_mb, device=device,
-                max_train_samples=sub))
-        residuals: list[WeightsCodebookBase] = []
-        for c in range(1, cfg.n_codebooks):
-            euc: WeightsCodebookBase = EuclideanCodebook(EuclideanCodebookConfig(
-                block_size=bs_per[c], K=k_per[c], shared=cfg.shared_codebook, max_iters=cfg.max_iters,
-                norm_threshold=0.001, skip_zeros=False, chunk_budget_mb=cfg.chunk_budget_mb, device=device))
-            if sign_split[c]:
-                euc = SSVQCodebook(euc)
-            residuals.append(euc)
-        aqlm = AQLMCodebook(primary=primary, residuals=residuals, config=AQLMCodebookConfig(
-            codebook_bits=cfg.codebook_bits, norm_threshold=0.001, device=device, out_dim=out_dim,
-            num_experts=cfg.num_experts))
-        for ev in (CodebookStartEvent, CodebookIterEvent, CodebookDoneEvent, KmeansStartEvent, KmeansIterEvent,
-                   KmeansDoneEvent):
-            self._forward_from(aqlm, ev)
-
-        cwr = aqlm.fit(W_raw.to(device) if device is not None else W_raw)
-        sc_bits = scale_bits_per_elem(cfg.scale_dtype)
-        if cfg.metric == "cosine":
-            cb, cwr_p = aqlm.primary, cwr.primary
-            if isinstance(cb, SSVQCodebook):
-                cb, cwr_p = cb.inner, cwr_p.inner if isinstance(cwr_p, SSVQCWR) else cwr_p
-            if isinstance(cb, SphericalCodebook) and isinstance(cwr_p, SphericalCWR):
-                quantize_spherical_scales(cwr_p, cb, cfg.scale_dtype)
-        w_recon = aqlm.reconstruct(cwr)
-        err = torch.norm(W_raw.float().to(w_recon.device) - w_recon).item() / w_norm
-        bpw = bits_per_weight_kmeans(
-            n_rows, cfg.in_dim, n_blocks, cfg.block_size, cfg.n_codebooks, k_per,
-            shared_codebook=cfg.shared_codebook, sign_split=cfg.sign_split, scale_bits_per_elem=sc_bits,
-            bs_per_codebook=bs_per, codebook_bits=cfg.codebook_bits, residual_sign_split=res_ss,
-            primary_metric=cfg.metric)
-        logger.info("  [%s] err=%.6f bpw=%.3f cr=%.2f", cfg.projection, err, bpw, 16.0 / bpw)
-        del cwr, w_recon
-        row = {
-            "projection": cfg.projection, "scheme": label, "block_size": cfg.block_size, "K": cfg.K,
+        extra_bs = [b for b in plan.block_sizes[1:] if b != cfg.block_size]
+        return {
+            "projection": cfg.projection, "scheme": plan.label, "block_size": cfg.block_size, "K": cfg.K,
             "n_codebooks": cfg.n_codebooks, "metric": cfg.metric, "shared": cfg.shared_codebook,
             "sign_split": cfg.sign_split, "scale_dtype": cfg.scale_dtype, "kmeans_iters": cfg.max_iters,
-            "residual_block_sizes": ([cfg.block_size] + [b for b in bs_per[1:] if b != cfg.block_size]
-                                     if any(b != cfg.block_size for b in bs_per[1:]) else []),
+            "residual_block_sizes": [cfg.block_size, *extra_bs] if extra_bs else [],
             "rel_fro_err": err, "bits_per_weight": bpw, "compression_ratio": 16.0 / bpw,
         }
-        self._result = row
-        self._emit(VQDoneEvent(config_id=config_id, row=row))
-        return row
+
+    def fit(self, W_raw: torch.Tensor) -> dict:  # noqa: N803
+        cfg = self.config
+        plan = _plan(cfg)
+        self._emit(VQStartEvent(config_id=plan.config_id, projection=cfg.projection, block_size=cfg.block_size,
+                                K=cfg.K, n_codebooks=cfg.n_codebooks, metric=cfg.metric))
+        aqlm = assemble_aqlm(plan.specs, max_iters=cfg.max_iters, norm_threshold=_NORM_THRESHOLD,
+                             codebook_bits=cfg.codebook_bits, out_dim=plan.out_dim, num_experts=cfg.num_experts,
+                             device=cfg.device, chunk_budget_mb=cfg.chunk_budget_mb)
+        for ev in _CHILD_EVENTS:
+            self._forward_from(aqlm, ev)
+        w = W_raw if cfg.device is None else W_raw.to(cfg.device)
+        cwr = aqlm.fit(w)
+        if cfg.metric == "cosine" and (sp := _spherical_primary(aqlm, cwr)) is not None:
+            quantize_spherical_scales(sp[1], sp[0], cfg.scale_dtype)
+        recon = aqlm.reconstruct(cwr)
+        ref = W_raw.float().to(recon.device)
+        err = (torch.linalg.vector_norm(ref - recon) / torch.linalg.vector_norm(ref)).item()
+        del cwr, recon, ref
+        bpw = bits_per_weight_kmeans(
+            W_raw.shape[0], cfg.in_dim, cfg.in_dim // cfg.block_size, cfg.block_size, cfg.n_codebooks, plan.ks,
+            shared_codebook=cfg.shared_codebook, sign_split=cfg.sign_split,
+            scale_bits_per_elem=scale_bits_per_elem(cfg.scale_dtype), bs_per_codebook=plan.block_sizes,
+            codebook_bits=cfg.codebook_bits, residual_sign_split=plan.residual_sign_split,
+            primary_metric=cfg.metric)
+        logger.info("  [%s] err=%.6f bpw=%.3f cr=%.2f", cfg.projection, err, bpw, 16.0 / bpw)
+        self._result = self._row(plan, err, bpw)
+        self._emit(VQDoneEvent(config_id=plan.config_id, row=self._result))
+        return self._result
 
     @property
     def result(self) -> dict:

@@ -2,7 +2,9 @@
 
 Run in a container where the reference source tree is present:
 
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py --ref <path of the reference checkout>
+
+(or set SKCQ_REFERENCE to that path).
 
 Writes ``tests/golden/*.npz``. Each case records the inputs, the random draws
 the reference consumed (every ``torch.randperm`` call, captured in order) and
@@ -14,6 +16,7 @@ time; only these fixtures are.
 from __future__ import annotations
 
 import argparse
+import os
 import sys
 from pathlib import Path
 
@@ -365,9 +368,12 @@ def case_metrics(out: Path, metrics, eval_model) -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("SKCQ_REFERENCE"),
+                    help="the reference checkout (default: $SKCQ_REFERENCE)")
     ap.add_argument("--only", default="")
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("give --ref or set SKCQ_REFERENCE")
     sys.path.insert(0, args.ref)
     torch.set_num_threads(8)
     import skcq.codebook as cb

@@ -75,3 +75,29 @@ def test_vq_run_matches_reference(name, monkeypatch):
     assert row["bits_per_weight"] == pytest.approx(float(g["bpw"][0]), rel=1e-12)
     assert row["rel_fro_err"] == pytest.approx(float(g["err"][0]), rel=0.05)
     assert done and done[0].row is row and exp.result is row
+
+
+@pytest.mark.parametrize("name", list(SPECS))
+def test_vq_plan_label_and_bits_match_reference(name):
+    """The configuration's scheme label, residual block-size list and bits per
+    weight (host logic only) equal the reference's row."""
+    from skcq_b200.vq.bpw import bits_per_weight_kmeans
+    from skcq_b200.codebook.spherical import scale_bits_per_elem
+    from skcq_b200.vq.experiment import VQRunConfig, VQRunExperiment, _plan
+
+    g = sub(load_golden("vq"), f"vq__{name}__")
+    proj, bs, K, ncb, metric, rk, rss, shared, ss, iters, sdt, rbs, cbits = SPECS[name]
+    n_rows, in_dim = g["w"].shape
+    cfg = VQRunConfig(projection=proj, in_dim=in_dim, num_experts=4, hidden_size=16, intermediate_size=8,
+                      block_size=bs, K=K, n_codebooks=ncb, metric=metric, residual_k=rk, residual_sign_split=rss,
+                      shared_codebook=shared, sign_split=ss, max_iters=iters, scale_dtype=sdt,
+                      residual_block_sizes=rbs, codebook_bits=cbits, layer_idx=3, device=None, chunk_budget_mb=64)
+    plan = _plan(cfg)
+    assert plan.label == str(g["scheme"][0])
+    row = VQRunExperiment(cfg)._row(plan, 0.0, 1.0)
+    assert row["residual_block_sizes"] == [int(v) for v in g["rbs"]]
+    bpw = bits_per_weight_kmeans(
+        n_rows, in_dim, in_dim // bs, bs, ncb, plan.ks, shared_codebook=shared, sign_split=ss,
+        scale_bits_per_elem=scale_bits_per_elem(sdt), bs_per_codebook=plan.block_sizes, codebook_bits=cbits,
+        residual_sign_split=plan.residual_sign_split, primary_metric=metric)
+    assert bpw == pytest.approx(float(g["bpw"][0]), rel=1e-12)

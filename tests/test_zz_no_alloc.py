@@ -68,10 +68,17 @@ def _reseed_both(metric: int, nblk: int, n: int, bs: int, K: int, seed: int):
 
 
 def test_noalloc_reseed_matches_reseed_on_two_calls_in_a_row():
-    # first call: cosine, 5 problems; second call: euclidean with different shapes
-    for metric, nblk, n, bs, K, seed in ((0, 5, 3000, 8, 2048, 1), (1, 3, 6000, 4, 4000, 2)):
+    # first call: cosine, 5 problems; second call: euclidean with different
+    # shapes; third: K = 65536 (768 KiB of scratch per problem, so only 21
+    # problems fit the static array at once and CTAs reuse their slot for
+    # several problems), with more empty clusters than the shared-memory sort
+    # holds, so the sort runs in the static array
+    for metric, nblk, n, bs, K, seed in ((0, 5, 3000, 8, 2048, 1), (1, 3, 6000, 4, 4000, 2),
+                                         (1, 32, 12000, 4, 65536, 3)):
         s_ref, s_new, e_ref, e_new = _reseed_both(metric, nblk, n, bs, K, seed)
         assert int(e_ref.min()) > 0, "the case must have empty clusters"
+        if K == 65536:
+            assert int(e_ref.min()) > 4096, "the case must reach the sort outside shared memory"
         assert torch.equal(e_ref, e_new)
         assert torch.equal(s_ref, s_new)  # same selection and order, bit for bit
 
