@@ -41,8 +41,28 @@ WORKLOADS = {
                   bits=8),
     "small": dict(experts=8, hidden=512, inter=192, prim=(8, 256), res=[(16, 256), (4, 2048)], iters=5, bits=8),
 }
+# One layer of the full-model build (48 layers of 128 experts in all): the
+# same expert shapes and distribution, a spherical primary of block size 12
+# (2048 = 170 blocks + 8 raw columns; 768 = 64 blocks) with K = 65536 and one
+# euclidean residual of block size 6 with K = 16384, 16-bit centroids, 25
+# iterations (the build's iteration count is not fixed by the workload).
+MODEL = dict(experts=128, hidden=2048, inter=768, prim=(12, 65536), res=[(6, 16384)], iters=25, bits=16,
+             layers_total=48)
 METRIC = "kmeans_mblock_iters_per_s"
+# DRAM bytes per split-operand byte of one assignment launch (ncu,
+# profiles/assign_tc_*.md): every operand byte is read from DRAM once.
+ASSIGN_DRAM_PER_OPERAND_BYTE = 1.0
 UNIT = "Mblock-iters/s"
+
+
+def bench_config(workload: str, wl: dict, world: int, rows_mode: bool) -> dict:
+    """The ``config`` object both arms print (same keys and values)."""
+    return {"workload": workload, "experts": wl["experts"], "hidden": wl["hidden"], "intermediate": wl["inter"],
+            "primary": list(wl["prim"]), "residuals": [list(r) for r in wl["res"]], "iters": wl["iters"],
+            "codebook_bits": wl["bits"], "step": "AQLM build of gate, up and down",
+            "l2": "inputs larger than L2 (bf16 weights 1.2 GB per layer; split operands > 3 GB)",
+            "parallelism": (f"row-sharded k-means x{world} (NCCL all-reduce of sums/counts)" if rows_mode
+                            else f"layer farm x{world}")}
 
 
 def projections(wl: dict) -> list[tuple[str, int, int]]:
@@ -110,6 +130,109 @@ def build_step(wl: dict, weights: dict[str, torch.Tensor], rel_err: bool = False
             keep[name] = (aqlm, cwr)
         del cwr, aqlm
     return total, errs
+
+
+def cwr_nbytes(obj) -> int:
+    """Bytes of every tensor in a CWR payload (nested dataclasses and lists)."""
+    import dataclasses
+
+    if isinstance(obj, torch.Tensor):
+        return obj.numel() * obj.element_size()
+    if isinstance(obj, (list, tuple)):
+        return sum(cwr_nbytes(o) for o in obj)
+    if dataclasses.is_dataclass(obj):
+        return sum(cwr_nbytes(getattr(obj, f.name)) for f in dataclasses.fields(obj))
+    return 0
+
+
+def model_aqlm(wl: dict, name: str, in_dim: int, out_dim: int):
+    """One projection of the full-model build, assembled by the package's own
+    build_aqlm_codebook (config.py:137-197) as the build driver does."""
+    from skcq_b200.config import CodebookParams, build_aqlm_codebook
+
+    bs0, k0 = wl["prim"]
+    (bs1, k1), = wl["res"]
+    n_blocks = in_dim // bs0
+    params = CodebookParams(k_gate=k0, k_up=k0, k_down=k0, n_blocks_gate_up=n_blocks, n_blocks_down=n_blocks,
+                            n_codebooks=2, max_iters=wl["iters"], residual_k=k1, residual_block_sizes=bs1)
+    return build_aqlm_codebook(params, k=k0, n_blocks=n_blocks, n_codebooks=2, in_dim=in_dim, out_dim=out_dim,
+                               num_experts=wl["experts"], name=f"model.{name}")
+
+
+def model_leg(world: int, rank: int, dev: str) -> dict:
+    """One layer of the full-model build per rank (the layer farm, weak
+    scaling): wall time of the layer on the device (max over ranks) and its
+    block-iteration rate over all ranks."""
+    wl = MODEL
+    weights = make_weights(wl, seed=5000 + rank, device=dev)
+    outs = {"gate": wl["inter"], "up": wl["inter"], "down": wl["hidden"]}
+    torch.cuda.synchronize()
+    barrier(world)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    total = 0
+    iters = {}
+    for name, _, in_dim in projections(wl):
+        aqlm = model_aqlm(wl, name, in_dim, outs[name])
+        cnt = BlockIterCounter(aqlm)
+        aqlm.fit(weights[name])
+        total += cnt.total
+        iters[name] = cnt.total
+        del aqlm
+    b.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(a.elapsed_time(b), world)
+    all_bi = sum_over_ranks(total, world)
+    del weights
+    torch.cuda.empty_cache()
+    return {"value": all_bi / (ms / 1e3) / 1e6, "unit": UNIT, "ms_per_layer": ms, "layers": world,
+            "layers_per_rank": 1, "block_iters_per_rank": total,
+            "shapes": "primary spherical bs=12 K=65536 (2048 = 170 blocks + 8 raw columns; 768 = 64 blocks), "
+                      "residual euclidean bs=6 K=16384, 25 iterations, 16-bit centroids",
+            "full_model_s_at_this_n": ms / 1e3 * wl["layers_total"] / world}
+
+
+def rows_leg(wl: dict, world: int, rank: int, dev: str) -> dict:
+    """One layer of the benchmark workload row-sharded over all ranks (strong
+    scaling): every iteration all-reduces the n_blocks x K x bs sums and
+    n_blocks x K counts of every problem (NCCL)."""
+    from skcq_b200 import _engine, distributed
+
+    full = make_weights(wl, seed=1234, device=dev)
+    weights = {}
+    for name, rows, _ in projections(wl):
+        r0, r1 = distributed.expert_row_range(wl["experts"], rows // wl["experts"], world, rank)
+        weights[name] = full[name][r0:r1].contiguous()
+    del full
+
+    def step():
+        with distributed.row_sharded():
+            torch.manual_seed(99)  # identical Forgy draws on every rank
+            return build_step(wl, weights)
+
+    step()  # warm-up
+    torch.cuda.synchronize()
+    barrier(world)
+    _engine.TIMER.reset()
+    _engine.TIMER.enabled = True
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    n, _ = step()
+    b.record()
+    torch.cuda.synchronize()
+    _engine.TIMER.enabled = False
+    ks = _engine.TIMER.summary()
+    ms = max_over_ranks(a.elapsed_time(b), world)
+    ar = ks.get("allreduce", {"ms": 0.0, "work": 0.0, "launches": 0})
+    ar_ms = max_over_ranks(ar["ms"], world)
+    del weights
+    torch.cuda.empty_cache()
+    return {"value": n / (ms / 1e3) / 1e6, "unit": UNIT, "ms_per_layer": ms, "scaling": "strong",
+            "allreduce_ms": ar_ms, "allreduce_share": ar_ms / ms if ms else None,
+            "allreduce_calls": int(ar["launches"]), "allreduce_gb": ar["work"] / 1e9,
+            "allreduce_busbw_gbs": (2 * (world - 1) / world * ar["work"] / (ar["ms"] / 1e3) / 1e9
+                                    if ar["ms"] else None),
+            "collective": "NCCL all_reduce (sum) of centroid sums and counts, every Lloyd iteration"}
 
 
 # ---------------------------------------------------------------------------
@@ -199,8 +322,8 @@ def forward_bench(wl: dict, fits: dict, dev: str, peaks: dict) -> dict:
     outs = {"gate": I, "up": I, "down": H}
     mods, dense = {}, {}
     for name, (aqlm, cwr) in fits.items():
-        mods[name] = CodebookModule.from_cwr(aqlm, cwr, out_dim=outs[name]).to(torch.bfloat16)
-        w = aqlm.reconstruct(cwr).to(torch.bfloat16)
+        mods[name] = CodebookModule.from_cwr(aqlm, cwr, out_dim=outs[name]).to(device=dev, dtype=torch.bfloat16)
+        w = aqlm.reconstruct(cwr).to(device=dev, dtype=torch.bfloat16)
         dense[name] = w.reshape(E, outs[name], w.shape[1]).transpose(1, 2)  # (E, in, out) view
         del w
     ex = CodebookExperts(mods["gate"], mods["up"], mods["down"], E, torch.nn.functional.silu)
@@ -366,7 +489,16 @@ def ep_forward_bench(wl: dict, world: int, rank: int, dev: str, iters: int = 3) 
 def cpu_rate(wl: dict, seconds_hint: float = 15.0) -> dict:
     """Time one Lloyd iteration (assign + update) and one assignment of each
     codebook kind on sampled points of one full-size block with the numpy
-    oracle, then scale to the whole layer's block-iterations."""
+    oracle, then scale to the whole layer's block-iterations. BLAS uses every
+    host core (torchrun limits the process to one thread; that limit is lifted
+    for this leg)."""
+    from threadpoolctl import threadpool_limits
+
+    with threadpool_limits(limits=os.cpu_count()):
+        return _cpu_rate(wl)
+
+
+def _cpu_rate(wl: dict) -> dict:
     from oracle import kmeans as ok
 
     rng = np.random.default_rng(0)
@@ -479,7 +611,7 @@ def run_reference(args, wl, world, rank) -> None:
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": args.workload, **{k: (list(map(list, v)) if k == "res" else v) for k, v in wl.items()}},
+        "config": bench_config(args.workload, wl, world, args.mode == "rows" and world > 1),
         "cpu_baseline": {k: v[-1][k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "wall_s": time.perf_counter() - t0,
@@ -497,6 +629,8 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg")
     ap.add_argument("--no-forward", action="store_true", help="skip the codebook-expert forward leg")
+    ap.add_argument("--no-legs", action="store_true",
+                    help="skip the full-model layer leg and (N > 1) the row-sharded leg")
     ap.add_argument("--mode", default="farm", choices=["farm", "rows"],
                     help="N > 1: farm = one layer per rank (weak scaling); rows = one layer row-sharded (strong)")
     args = ap.parse_args()
@@ -566,6 +700,9 @@ def main() -> None:
     ksum = _engine.TIMER.summary()
 
     # ---- end to end through the public API with host buffers --------------
+    # AQLMCodebook.fit on the pinned host weights: the fit copies them to the
+    # device and returns the CWR payload (indices, scales, signs, remainders)
+    # on the host, as the reference's API does for a host input.
     e2e = None
     fits: dict = {}
     if not args.no_e2e:
@@ -579,18 +716,29 @@ def main() -> None:
         bi = 0
         d2h = 0
         for _ in range(args.steps):
-            dev_w = {k: v.to(dev, non_blocking=True) for k, v in host.items()}
             fits.clear()
-            n, errs = step(dev_w, rel_err=True, keep=fits)
-            vals = torch.stack(errs).cpu()
-            d2h += vals.numel() * vals.element_size()
+            n, _ = step(host, keep=fits)
+            d2h += sum(cwr_nbytes(cwr) for _, cwr in fits.values())
             bi += n
-            del dev_w
         torch.cuda.synchronize()
         e2e_s = max_over_ranks(time.perf_counter() - t0, world)
+        errs = []
+        for name, (aqlm, cwr) in fits.items():  # quality of the last step's fits, outside the timed region
+            wf = host[name].to(dev).float()
+            errs.append(float(torch.linalg.vector_norm(wf - aqlm.reconstruct(cwr).to(dev)) /
+                              torch.linalg.vector_norm(wf)))
         e2e = {"value": (bi if rows_mode else sum_over_ranks(bi, world)) / e2e_s / 1e6, "unit": UNIT,
-               "h2d_bytes_per_step": h2d,
-               "d2h_bytes_per_step": d2h // max(args.steps, 1), "rel_fro_err": [float(x) for x in vals]}
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h // max(args.steps, 1),
+               "api": "AQLMCodebook.fit(host bf16 weights) -> AQLMCWR on the host", "rel_fro_err": errs}
+    rows = None
+    model = None
+    if world > 1 and not rows_mode and not args.no_legs:
+        weights = None
+        torch.cuda.empty_cache()
+        rows = rows_leg(wl, world, rank, dev)
+    if not args.no_legs and args.workload == "layer":
+        torch.cuda.empty_cache()
+        model = model_leg(world, rank, dev)
 
     peaks, peak_kind = measured_peaks()
     fwd = None
@@ -605,10 +753,20 @@ def main() -> None:
     a = ksum.get("assign", {"ms": 0.0, "work": 0.0, "launches": 0, "padded": 0.0})
     achieved = a["work"] / (a["ms"] / 1e3) / 1e12 if a["ms"] > 0 else 0.0
     issued = a["padded"] / (a["ms"] / 1e3) / 1e12 if a["ms"] > 0 else 0.0
+    # The assignment runs inside a seconds-long build step, so the sustained
+    # (power-capped) bf16 figure is its denominator; the burst figure is kept
+    # beside it. traffic: DRAM bytes per launch, the operand bytes the launch
+    # reads scaled by the DRAM-to-operand ratio ncu measured for this kernel
+    # (profiles/assign_tc_*.md: dram__bytes_read + write equal the split
+    # operands, ratio 1.00 on all three codebook shapes).
+    sustained = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
     roofline = {
         "bound": "tensor", "kernel": "skcq_assign (tensor-core pass + exact re-score)", "achieved": achieved,
-        "peak": peaks["bf16_tflops"], "peak_kind": f"{peak_kind} bf16 dense (burst)", "unit": "TFLOP/s",
-        "frac": achieved / peaks["bf16_tflops"], "traffic": None,
+        "peak": sustained, "peak_kind": f"{peak_kind} bf16 dense, sustained", "unit": "TFLOP/s",
+        "frac": achieved / sustained, "peak_burst": peaks["bf16_tflops"],
+        "frac_of_burst": achieved / peaks["bf16_tflops"],
+        "traffic": ASSIGN_DRAM_PER_OPERAND_BYTE * a["bytes"] / a["launches"] if a.get("launches") else None,
+        "traffic_unit": "bytes per launch",
         "issued_tf32_tflops": issued,
         "assign_share_of_step": a["ms"] / ms if ms else None,
         "kernel_ms": {k: round(v["ms"], 2) for k, v in ksum.items()},
@@ -620,17 +778,13 @@ def main() -> None:
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
             "scaling": "strong" if rows_mode else "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": args.workload, "experts": wl["experts"], "hidden": wl["hidden"],
-                       "intermediate": wl["inter"], "primary": list(wl["prim"]),
-                       "residuals": [list(r) for r in wl["res"]], "iters": wl["iters"],
-                       "codebook_bits": wl["bits"], "step": "AQLM build of gate, up and down",
-                       "l2": "inputs larger than L2 (bf16 weights 1.2 GB per layer; split operands > 3 GB)",
-                       "parallelism": f"row-sharded k-means x{world} (NCCL all-reduce of sums/counts)"
-                       if rows_mode else f"layer farm x{world}"},
+            "config": bench_config(args.workload, wl, world, rows_mode),
             "block_iters_per_step": total_block_iters / args.steps,
             "roofline": roofline, "clocks": clocks.summary(), "gpu_launches": launches, "e2e": e2e,
             "forward": fwd,
             "forward_expert_parallel": fwd_ep,
+            "rows_sharded": rows,
+            "model_layer_farm": model,
         }
         if not args.no_cpu and world == 1:
             line["cpu_baseline"] = {k: v for k, v in cpu_rate(wl).items() if k != "est_layer_s"}

@@ -31,12 +31,12 @@ class KernelTimer:
 
     def __init__(self) -> None:
         self.enabled = False
-        self.records: list[tuple[str, torch.cuda.Event, torch.cuda.Event, float, float]] = []
+        self.records: list[tuple[str, torch.cuda.Event, torch.cuda.Event, float, float, float]] = []
 
     def reset(self) -> None:
         self.records = []
 
-    def run(self, name: str, fn, work: float = 0.0, padded: float = 0.0) -> None:
+    def run(self, name: str, fn, work: float = 0.0, padded: float = 0.0, nbytes: float = 0.0) -> None:
         if not self.enabled:
             fn()
             return
@@ -45,17 +45,18 @@ class KernelTimer:
         s.record()
         fn()
         e.record()
-        self.records.append((name, s, e, work, padded))
+        self.records.append((name, s, e, work, padded, nbytes))
 
     def summary(self) -> dict[str, dict[str, float]]:
         torch.cuda.synchronize()
         out: dict[str, dict[str, float]] = {}
-        for name, s, e, work, padded in self.records:
-            d = out.setdefault(name, {"launches": 0, "ms": 0.0, "work": 0.0, "padded": 0.0})
+        for name, s, e, work, padded, nbytes in self.records:
+            d = out.setdefault(name, {"launches": 0, "ms": 0.0, "work": 0.0, "padded": 0.0, "bytes": 0.0})
             d["launches"] += 1
             d["ms"] += s.elapsed_time(e)
             d["work"] += work
             d["padded"] += padded
+            d["bytes"] += nbytes
         return out
 
 
@@ -249,14 +250,16 @@ def lloyd(
     T = TIMER
     nk = np.array(pts.n_host, dtype=np.float64) * np.array(k_host, dtype=np.float64)
     for it in range(max_iters):
-        work = padded = 0.0
+        work = padded = nbytes = 0.0
         if T.enabled:  # algorithmic work of this iteration: 2*n*k*bs flops over active problems
             act = active.cpu().numpy().astype(bool)
             work = 2.0 * bs * float(nk[act].sum())
             padded = work * kp / bs
+            # the split operands each active problem's tensor-core pass reads once
+            nbytes = 4.0 * kp * float(act.sum()) * (n_pad + k_pad)
         T.run("pack_centroids", lambda: call("skcq_pack_centroids", metric, ptr(C), nblk, k_pad, bs, ptr(k_dev),
                                              ptr(active), ptr(B), ptr(cnorm), s))
-        T.run("assign", lambda: assign_call(pts, B, C, cnorm, k_pad, k_dev, active, labels), work, padded)
+        T.run("assign", lambda: assign_call(pts, B, C, cnorm, k_pad, k_dev, active, labels), work, padded, nbytes)
         T.run("update", lambda: call("skcq_update", ptr(pts.R), ptr(labels), nblk, n_pad, k_pad, bs, ptr(pts.n),
                                      ptr(k_dev), ptr(active), ptr(sums), ptr(counts), s))
         if shard is None:
@@ -276,7 +279,8 @@ def lloyd(
     # final assignment with the final centroids (kmeans.py:190 / 246)
     call("skcq_pack_centroids", metric, ptr(C), nblk, k_pad, bs, ptr(k_dev), None, ptr(B), ptr(cnorm), s)
     work = 2.0 * bs * float(nk.sum())
-    T.run("assign", lambda: assign_call(pts, B, C, cnorm, k_pad, k_dev, None, labels), work, work * kp / bs)
+    T.run("assign", lambda: assign_call(pts, B, C, cnorm, k_pad, k_dev, None, labels), work, work * kp / bs,
+          4.0 * kp * nblk * (n_pad + k_pad))
     return KmeansRun(
         C=C, k_pad=k_pad, k_host=k_host, labels=labels,
         iters_run=[int(v) for v in iters_run.cpu().tolist()],

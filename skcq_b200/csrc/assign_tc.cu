@@ -1,66 +1,73 @@
 // Nearest-centroid assignment on the 5th-generation tensor cores
 // (skcq/codebook/kmeans.py:25-66, assign_cosine / assign_l2).
 //
-// Kernel 1 (packed widths of at most two MMA k-steps, kp <= 16: l2 with
-// bs <= 4, cosine with bs <= 5; wider ones run the shared-memory-operand form
-// in assign_ss.cu) -- one persistent CTA per SM, warp-specialised:
+// Kernel 1 -- one persistent CTA per SM, warp-specialised:
 //   warp 0      producer: 1-D bulk copies (TMA engine) of the work unit's
-//               256 points and a ring of centroid tiles (N = 224 centroids);
-//   warp 1      issues the tensor-core work: at the start of each unit
-//               tcgen05.cp moves the two 128-point row tiles from shared into
-//               tensor memory, then for every centroid tile one chain of
-//               tcgen05.mma kind::tf32 (M=128, N, K=8, A from tensor memory,
-//               B from shared memory) per row tile;
-//   warps 2-17  epilogue: 8 warps per row tile tcgen05.ld the fp32 scores of
-//               their (lane quarter, column half) two groups of 32 at a time,
-//               release the accumulator after the last read, and keep a
-//               running (best value, best group of 32 centroids) per point
-//               with 3-input max; the distance matrix never leaves the SM.
-// Tensor memory holds one accumulator per row tile and the two A tiles. The
-// row tiles alternate: while the epilogue drains one accumulator the tensor
-// core fills the other, so an accumulator's turnaround (MMA completion,
-// epilogue read, release) overlaps the other row tile's chain. Wide N keeps
-// each MMA long enough to run near the tensor pipe's rate (N=128
-// instructions at K=8 run at about a third of it), and A in tensor memory
-// halves the shared-memory operand traffic. tcgen05.mma issue blocks the
-// issuing thread until the tensor core accepts the instruction, so the MMA
-// thread checks the next tile's operands between the two row-tile chains,
-// while the tensor core is busy, not after both.
+//               256 points and a ring of centroid tiles;
+//   warps 1, 2  issue the tensor-core work, one thread per row tile: at the
+//               start of each unit tcgen05.cp moves the thread's 128-point row
+//               tile from shared into tensor memory, then for every centroid
+//               tile one chain of tcgen05.mma kind::tf32 (M=128, N, K=8, A
+//               from tensor memory, B from shared memory) into the next of
+//               three accumulator slots (items alternate between the two
+//               threads: (tile 0, row tile 0), (tile 0, row tile 1), ...);
+//   warps 3..   epilogue, one set of warps per row tile: a warp owns a TMEM
+//               lane quarter and a pair of 32-centroid groups of every tile
+//               of its row tile. For every item it tcgen05.lds its 64 scores
+//               per point, releases the slot at once and folds the groups
+//               into a running (best value, best group) per point with
+//               3-input max; the distance matrix never leaves the SM.
+// What bounds this kernel is issue and hand-off latency, not the tensor
+// pipe. Measured on B200: a tcgen05.mma issue stalls its thread ~64 clocks,
+// a tcgen05.commit ~90 and an mbarrier try_wait ~130, so one thread needs
+// ~350 clocks per item while a 128 x 128 item at two k-steps is 128 clocks
+// of tensor work. Two issuing threads halve that; every slot is released
+// after one tcgen05.ld round per epilogue warp (no ALU work in between); and
+// three slots of N = 128 keep the tensor core busy while the epilogue drains
+// the others.
 // Operands are split-tf32 (hi/lo) so A.B reproduces the fp32 dot product to
 // ~2^-21 relative.
-// Kernel 2 -- refine (both forms): one warp per point re-scores the 32
-// centroids of its winning group, one centroid per lane, with the exact fp32
-// reference formula (first maximum wins), reading the problem's centroid table
-// from transposed shared-memory slices.
+// Kernel 2 -- refine: one warp per point re-scores the 32 centroids of its
+// winning group, one centroid per lane, with the exact fp32 reference formula
+// (first maximum wins), reading the problem's centroid table from transposed
+// shared-memory slices.
 #include <algorithm>
 
-#include "assign_ss.cuh"
 #include "common.cuh"
 
 namespace skcq {
 
-constexpr int TC_BM = 128;                       // points per MMA (TMEM lanes)
-constexpr int TC_RT = 2;                         // row tiles per work unit
-constexpr int TC_ROWS = TC_BM * TC_RT;           // points per work unit
-constexpr int TC_STAGES = 16;                    // max centroid tile ring depth (as many as shared memory holds)
-constexpr int TC_EPI_WARPS = 8 * TC_RT;          // one warp per (row tile, lane quarter, column half)
-constexpr int TC_THREADS = (2 + TC_EPI_WARPS) * 32;
-constexpr int TC_TMEM_COLS = 512;                // accumulators (2 x N) + A tiles (2 x kp)
-constexpr size_t TC_MIN_SMEM = 116 * 1024;       // keeps one CTA (and one TMEM owner) per SM
-constexpr int TC_MAX_KSTEPS = 8;                 // kp <= 64 (both forms): bs <= 20 (l2) / 21 (cosine)
-constexpr int GROUP = 32;                        // centroids per re-scored group
-
-// This form serves packed widths of at most TC_TS_MAX_KSTEPS MMA k-steps
-// (kp <= 16); wider ones go to the shared-memory-operand form in
-// assign_ss.cu, which measured faster once a tile's MMA chain is long.
-constexpr int TC_TS_MAX_KSTEPS = 2;
-// Centroids per tile: the widest N (a multiple of 32) with 2 N + 2 kp <= 512
-// tensor-memory columns.
-constexpr int TC_BN = 224;
+constexpr int TC_BM = 128;                // points per MMA (TMEM lanes)
+constexpr int TC_RT = 2;                  // row tiles per work unit
+constexpr int TC_ROWS = TC_BM * TC_RT;    // points per work unit
+constexpr int TC_STAGES = 16;             // max centroid tile ring depth (as many as shared memory holds)
+constexpr int TC_SLOTS = 3;               // accumulators in flight
+constexpr int TC_TMEM_COLS = 512;
+constexpr size_t TC_MIN_SMEM = 116 * 1024;  // keeps one CTA (and one TMEM owner) per SM
+constexpr int TC_MAX_KSTEPS = 8;          // kp <= 64: bs <= 20 (l2) / 21 (cosine)
+constexpr int GROUP = 32;                 // centroids per re-scored group
 
 static_assert(TC_ROWS == SKCQ_ROWS_PER_UNIT, "work unit size is part of the ABI");
-static_assert(2 * TC_BN + 2 * 8 * TC_TS_MAX_KSTEPS <= TC_TMEM_COLS, "accumulators and A tiles must fit tensor memory");
-static_assert(TC_BN % GROUP == 0, "tiles hold whole groups");
+
+// Shapes of the kernel for KSTEPS k-steps (kp = 8 KSTEPS): N centroids per
+// tile, the accumulator slots at tensor-memory columns [0, SLOTS N) and the
+// unit's two A tiles at [SLOTS N, SLOTS N + 2 kp).
+template <int KSTEPS>
+struct TcShape {
+  static constexpr int KP = KSTEPS * 8;
+  static constexpr int N = 128;
+  static constexpr int NG = N / GROUP;             // groups per tile
+  static constexpr int GPW = 2;                    // groups one epilogue warp loads per item
+  static constexpr int WPQ = NG / GPW;             // warps per lane quarter per row tile
+  static constexpr int EPI_PER_RT = 4 * WPQ;       // epilogue warps of one row tile
+  static constexpr int EPI_WARPS = TC_RT * EPI_PER_RT;
+  static constexpr int EPI_WARP0 = 1 + TC_RT;       // producer, one MMA warp per row tile, epilogue
+  static constexpr int THREADS = (EPI_WARP0 + EPI_WARPS) * 32;
+  static constexpr int A_COL = TC_SLOTS * N;
+  static_assert(A_COL + TC_RT * KP <= TC_TMEM_COLS, "slots and A tiles must fit tensor memory");
+  static_assert(N % GROUP == 0 && N % 16 == 0 && N <= 256, "MMA N");
+  static_assert(NG % GPW == 0, "whole group pairs");
+};
 
 struct TcParams {
   const float* A;  // [nblk][n_pad/8][kp/4][8][4]
@@ -78,11 +85,14 @@ struct TcSmem {
   float* b;
   uint64_t* a_full;
   uint64_t* a_empty;
+  uint64_t* a_tmem_free;  // [TC_RT] the row tile's MMAs of the previous unit done: its A columns reusable
   uint64_t* b_full;
   uint64_t* b_empty;
-  uint64_t* acc_full;   // [TC_RT]
-  uint64_t* acc_empty;  // [TC_RT]
+  uint64_t* acc_full;   // [TC_SLOTS]
+  uint64_t* acc_empty;  // [TC_SLOTS]
   uint32_t* tmem_slot;
+  float* m_best;        // [TC_RT][NG][TC_BM] per-warp candidates, merged per unit
+  int* m_group;
   uint32_t a_bytes, b_stage_bytes;
 };
 
@@ -106,15 +116,17 @@ struct Ring {
   }
 };
 
-// D(tmem) (+)= A(tmem) * B(smem desc), kind::tf32, fp32 accumulate.
-__device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
-                                            uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
+// D(tmem) = A(tmem) * B(smem desc), kind::tf32, fp32 accumulate; the
+// accumulate flag is a constant of the instruction (first k-step overwrites).
+__device__ __forceinline__ void mma_tf32_ts_first(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc) {
+  asm volatile("tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, 0;" ::"r"(d_tmem), "r"(a_tmem),
+               "l"(b_desc), "r"(idesc)
+               : "memory");
+}
+__device__ __forceinline__ void mma_tf32_ts_acc(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc) {
+  asm volatile("tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, 1;" ::"r"(d_tmem), "r"(a_tmem),
+               "l"(b_desc), "r"(idesc)
+               : "memory");
 }
 
 // 128 rows x 256 bits (eight fp32 columns) of a no-swizzle K-major shared
@@ -126,7 +138,7 @@ __device__ __forceinline__ void tmem_cp_128x256b(uint32_t taddr, uint64_t s_desc
 
 template <int KSTEPS>
 __device__ void tc_producer(const TcParams& p, const TcSmem& s) {
-  constexpr int N = TC_BN;
+  constexpr int N = TcShape<KSTEPS>::N;
   const int upb = p.n_pad / TC_ROWS;
   const int64_t n_units = (int64_t)p.nblk * upb;
   const int64_t tile_floats = (int64_t)N * p.kp;
@@ -153,59 +165,58 @@ __device__ void tc_producer(const TcParams& p, const TcSmem& s) {
   }
 }
 
+// Issues row tile rt's items. Item t = 2 * (tiles issued so far by this
+// CTA) + rt goes to accumulator slot t % 3, on that slot's (t / 3)-th use;
+// the epilogue consumes items in t order.
 template <int KSTEPS>
-__device__ void tc_mma(const TcParams& p, const TcSmem& s, uint32_t tmem_base) {
-  constexpr int N = TC_BN;
-  constexpr int KP = KSTEPS * 8;
+__device__ void tc_mma(const TcParams& p, const TcSmem& s, uint32_t tmem_base, int rt) {
+  using S = TcShape<KSTEPS>;
+  constexpr int N = S::N;
+  constexpr int KP = S::KP;
   constexpr uint32_t idesc = idesc_tf32(TC_BM, N);
   const int upb = p.n_pad / TC_ROWS;
   const int64_t n_units = (int64_t)p.nblk * upb;
   const uint32_t sbo = (uint32_t)KP * 32;  // bytes between 8-row core-matrix groups
   // Descriptors advance by (bytes >> 4) in their start-address field.
-  const uint64_t a0 = smem_desc(smem_u32(s.a), 128, sbo);
+  const uint64_t a0 = smem_desc(smem_u32(s.a), 128, sbo) + (((uint64_t)(TC_BM * KP * 4) >> 4) * rt);
   const uint64_t b0 = smem_desc(smem_u32(s.b), 128, sbo);
-  const uint64_t a_rt = (uint64_t)(TC_BM * KP * 4) >> 4;
   const uint64_t b_st = (uint64_t)s.b_stage_bytes >> 4;
+  const uint32_t a_tm = tmem_base + S::A_COL + rt * KP;
   Ring ar, br;
-  uint32_t acc_phase = 0;
+  uint32_t item = (uint32_t)rt;
+  uint32_t a_free_phase = 0;
+  bool first = true;
   for (int64_t u = blockIdx.x; u < n_units; u += gridDim.x) {
     int b, r0;
     if (!unit_live(p, u, upb, &b, &r0)) continue;
     const int nbt = ceil_div(p.k[b], N);
     if (!mbar_wait(s.a_full, ar.phase, p.err, 13)) return;
-    tc_fence_after();
-    uint64_t bd = b0 + br.idx * b_st;
-    if (nbt > 0 && !mbar_wait(s.b_full + br.idx, br.phase, p.err, 14)) return;
-    for (int i = 0; i < nbt; ++i) {
-#pragma unroll
-      for (int rt = 0; rt < TC_RT; ++rt) {
-        // the accumulator is free once the epilogue has read it; that also
-        // means the MMAs that read this row tile's A have completed
-        if (!mbar_wait(s.acc_empty + rt, acc_phase ^ 1, p.err, 15)) return;
-        tc_fence_after();
-        const uint32_t a_tm = tmem_base + 2 * N + rt * KP;
-        if (i == 0) {
-#pragma unroll
-          for (int ks = 0; ks < KSTEPS; ++ks) tmem_cp_128x256b(a_tm + ks * 8, a0 + rt * a_rt + 16 * ks);
-        }
-#pragma unroll
-        for (int ks = 0; ks < KSTEPS; ++ks)
-          mma_tf32_ts(tmem_base + rt * N, a_tm + ks * 8, bd + 16 * ks, idesc, ks > 0 ? 1u : 0u);
-        tc_commit(s.acc_full + rt);
-        if (rt == 0 && i + 1 < nbt) {
-          // next tile's centroids: waited for here, while row tile 0's chain runs
-          Ring nx = br;
-          nx.next(p.stages);
-          if (!mbar_wait(s.b_full + nx.idx, nx.phase, p.err, 14)) return;
-        }
-      }
-      if (i == 0) tc_commit(s.a_empty);  // the points are in tensor memory: shared copy reusable
-      tc_commit(s.b_empty + br.idx);
-      acc_phase ^= 1;
-      br.next(p.stages);
-      bd = br.idx == 0 ? b0 : bd + b_st;
+    if (!first) {
+      // this row tile's MMAs of the previous unit read the A columns until they complete
+      if (!mbar_wait(s.a_tmem_free + rt, a_free_phase, p.err, 17)) return;
+      a_free_phase ^= 1;
     }
-    if (nbt == 0) tc_commit(s.a_empty);  // nothing issued: release the points at once
+    first = false;
+    tc_fence_after();
+#pragma unroll
+    for (int ks = 0; ks < KSTEPS; ++ks) tmem_cp_128x256b(a_tm + ks * 8, a0 + 16 * ks);
+    tc_commit(s.a_empty);  // one of the two arrivals that free the shared copy
+    for (int i = 0; i < nbt; ++i, item += TC_RT) {
+      if (!mbar_wait(s.b_full + br.idx, br.phase, p.err, 14)) return;
+      const uint32_t slot = item % TC_SLOTS;
+      const uint32_t use = item / TC_SLOTS;
+      if (!mbar_wait(s.acc_empty + slot, (use & 1) ^ 1, p.err, 15)) return;
+      tc_fence_after();
+      const uint64_t bd = b0 + br.idx * b_st;
+      const uint32_t d = tmem_base + slot * N;
+      mma_tf32_ts_first(d, a_tm, bd, idesc);
+#pragma unroll
+      for (int ks = 1; ks < KSTEPS; ++ks) mma_tf32_ts_acc(d, a_tm + ks * 8, bd + 16 * ks, idesc);
+      tc_commit(s.acc_full + slot);
+      tc_commit(s.b_empty + br.idx);  // one of the two arrivals that free the stage
+      br.next(p.stages);
+    }
+    tc_commit(s.a_tmem_free + rt);
     ar.next(1);
   }
 }
@@ -237,30 +248,34 @@ __device__ __forceinline__ void mask_group(float (&v)[32], int cbase, int kb) {
   }
 }
 
-// Epilogue warp e = warp - 2 owns TMEM lane quarter warp % 4 (hardware rule),
-// row tile (e >> 2) & 1 and column half e >> 3 of every N-column tile (the
-// first half takes the extra group when N / 32 is odd). It reads its groups
-// two at a time, releases the accumulator after the last read, and folds
-// each group into a running (best, group); tiles arrive in index order, so
-// a strictly larger maximum is needed to move to a later group. The two
-// halves of a row keep separate pairs, merged through shared memory at the
-// end of each work unit (larger value, then lower group, wins).
+// Epilogue warps 3.. form one set per row tile; warp e = warp - 3 serves row
+// tile rt = e / EPI_PER_RT, TMEM lane quarter warp % 4 (hardware rule) and
+// the group pair h = (e / 4) % WPQ of every tile, i.e. the items
+// t = 2 j + rt of tiles j, which arrive in accumulator slot t % 3. For each
+// it loads both groups' scores, waits for the loads, releases the slot (one
+// arrival per warp) and only then reduces, so a slot is held for one
+// tensor-memory load round; the two row tiles' sets work on alternate items,
+// one loading while the other reduces. Each thread keeps a running (best,
+// group) per point; tiles arrive in index order, so a strictly larger
+// maximum is needed to move to a later group. At the end of a work unit the
+// WPQ candidates of each row are merged through shared memory (larger value,
+// then lower group, wins).
 template <int KSTEPS>
-__device__ void tc_epilogue(const TcParams& p, const TcSmem& s, uint32_t tmem_base, int warp, int lane,
-                            float* m_best, int* m_group) {
-  constexpr int N = TC_BN;
-  constexpr int NG = N / GROUP;
+__device__ void tc_epilogue(const TcParams& p, const TcSmem& s, uint32_t tmem_base, int warp, int lane) {
+  using S = TcShape<KSTEPS>;
+  constexpr int N = S::N;
+  constexpr int NG = S::NG;
+  constexpr int GPW = S::GPW;
+  constexpr int WPQ = S::WPQ;
   const int upb = p.n_pad / TC_ROWS;
   const int64_t n_units = (int64_t)p.nblk * upb;
-  const int e = warp - 2;
+  const int e = warp - S::EPI_WARP0;
+  const int rt = e / S::EPI_PER_RT;
   const int q = warp & 3;
-  const int rt = (e >> 2) & 1;
-  const int half = e >> 3;
-  const int g0 = half ? (NG + 1) / 2 : 0;
-  const int g1 = half ? NG : (NG + 1) / 2;
-  const int lrow = rt * TC_BM + q * 32 + lane;  // row within the unit
-  const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + rt * N;
-  uint32_t acc_phase = 0;
+  const int h = (e >> 2) % WPQ;
+  const int qrow = q * 32 + lane;  // row within the row tile
+  const uint32_t tq = tmem_base + ((uint32_t)(q * 32) << 16) + h * GPW * GROUP;
+  uint32_t item = (uint32_t)rt;
   // After a failed wait a warp stops touching tensor memory but keeps joining
   // the named barriers below, so its partner warps are never left waiting.
   bool failed = false;
@@ -271,89 +286,94 @@ __device__ void tc_epilogue(const TcParams& p, const TcSmem& s, uint32_t tmem_ba
     const int nbt = ceil_div(kb, N);
     float best = -INFINITY;
     int bestg = 0x7fffffff;
-    for (int j = 0; j < nbt; ++j) {
+    for (int j = 0; j < nbt; ++j, item += TC_RT) {
       if (failed) continue;
-      const bool ok = mbar_wait(s.acc_full + rt, acc_phase, p.err, 16);
-      acc_phase ^= 1;
+      const uint32_t slot = item % TC_SLOTS;
+      const bool ok = mbar_wait(s.acc_full + slot, (item / TC_SLOTS) & 1, p.err, 16);
       if (!__all_sync(0xffffffffu, ok)) {
         failed = true;
         continue;
       }
       tc_fence_after();
-#pragma unroll
-      for (int g = g0; g < g1; g += 2) {
-        float v0[32], v1[32];
-        const bool pair = g + 1 < g1;
-        tmem_ld32(taddr + g * GROUP, v0);
-        if (pair) tmem_ld32(taddr + (g + 1) * GROUP, v1);
-        tmem_wait_ld();
-        if (g + 2 >= g1) {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(s.acc_empty + rt);  // one arrival per warp
-        }
-        const int gg = j * NG + g;  // global group index
+      float v0[32], v1[32];
+      tmem_ld32(tq + slot * N, v0);
+      tmem_ld32(tq + slot * N + GROUP, v1);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(s.acc_empty + slot);  // one arrival per warp
+      const int gg = j * NG + h * GPW;  // global index of the first group
+      if ((j + 1) * N > kb) {  // only the problem's last tile has columns past k
         mask_group(v0, gg * GROUP, kb);
-        float m = group_max32(v0);
-        if (m > best) { best = m; bestg = gg; }
-        if (pair) {
-          mask_group(v1, (gg + 1) * GROUP, kb);
-          m = group_max32(v1);
-          if (m > best) { best = m; bestg = gg + 1; }
+        mask_group(v1, (gg + 1) * GROUP, kb);
+      }
+      // one compare per group pair; the pair's winner (lower group on a tie,
+      // NaN never wins) only when the running best moves, as two sequential
+      // strictly-greater updates would choose
+      const float m0 = group_max32(v0), m1 = group_max32(v1);
+      const float m = fmaxf(m0, m1);
+      if (m > best) {
+        best = m;
+        bestg = m0 >= m1 ? gg : gg + 1;
+      }
+    }
+    // merge the WPQ candidates of each row (epilogue warps only: named barrier 1)
+    s.m_best[(rt * WPQ + h) * TC_BM + qrow] = best;
+    s.m_group[(rt * WPQ + h) * TC_BM + qrow] = bestg;
+    asm volatile("bar.sync 1, %0;" ::"n"(S::EPI_WARPS * 32) : "memory");
+    if (h == 0) {
+      float bv = best;
+      int bg = bestg;
+#pragma unroll
+      for (int o = 1; o < WPQ; ++o) {
+        const float ov = s.m_best[(rt * WPQ + o) * TC_BM + qrow];
+        const int og = s.m_group[(rt * WPQ + o) * TC_BM + qrow];
+        if (ov > bv || (ov == bv && og < bg)) {
+          bv = ov;
+          bg = og;
         }
       }
+      if (bg == 0x7fffffff) bg = 0;  // no finite score in any group (all masked or NaN)
+      const int row = r0 + rt * TC_BM + qrow;
+      if (row < nb && !failed && nbt > 0) p.group[(int64_t)b * p.n_pad + row] = -(bg + 1);  // negative: not yet refined
     }
-    // merge the two column halves of each row (epilogue warps only: named barrier 1)
-    if (half == 1) {
-      m_best[lrow] = best;
-      m_group[lrow] = bestg;
-    }
-    asm volatile("bar.sync 1, %0;" ::"n"(TC_EPI_WARPS * 32) : "memory");
-    if (half == 0) {
-      const float ob = m_best[lrow];
-      const int og = m_group[lrow];
-      if (ob > best || (ob == best && og < bestg)) {
-        best = ob;
-        bestg = og;
-      }
-      const int row = r0 + lrow;
-      if (row < nb && !failed && nbt > 0) p.group[(int64_t)b * p.n_pad + row] = -(bestg + 1);  // negative: not yet refined
-    }
-    asm volatile("bar.sync 1, %0;" ::"n"(TC_EPI_WARPS * 32) : "memory");
+    asm volatile("bar.sync 1, %0;" ::"n"(S::EPI_WARPS * 32) : "memory");
   }
 }
 
 template <int KSTEPS>
-__global__ void __launch_bounds__(TC_THREADS, 1) assign_tc_kernel(TcParams p) {
-  constexpr int N = TC_BN;
+__global__ void __launch_bounds__(TcShape<KSTEPS>::THREADS, 1) assign_tc_kernel(TcParams p) {
+  using S = TcShape<KSTEPS>;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   TcSmem s;
   s.a_bytes = (uint32_t)TC_ROWS * p.kp * 4;
-  s.b_stage_bytes = (uint32_t)N * p.kp * 4;
+  s.b_stage_bytes = (uint32_t)S::N * p.kp * 4;
   s.a = reinterpret_cast<float*>(smem_raw);
   s.b = reinterpret_cast<float*>(smem_raw + (size_t)s.a_bytes);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw + (size_t)s.a_bytes + (size_t)p.stages * s.b_stage_bytes);
   s.a_full = bars;
   s.a_empty = bars + 1;
-  s.b_full = bars + 2;
+  s.a_tmem_free = bars + 2;
+  s.b_full = bars + 2 + TC_RT;
   s.b_empty = s.b_full + TC_STAGES;
   s.acc_full = s.b_empty + TC_STAGES;
-  s.acc_empty = s.acc_full + TC_RT;
-  s.tmem_slot = reinterpret_cast<uint32_t*>(s.acc_empty + TC_RT);
-  float* m_best = reinterpret_cast<float*>(s.tmem_slot + 4);  // [TC_ROWS] half-row merge
-  int* m_group = reinterpret_cast<int*>(m_best + TC_ROWS);      // [TC_ROWS]
+  s.acc_empty = s.acc_full + TC_SLOTS;
+  s.tmem_slot = reinterpret_cast<uint32_t*>(s.acc_empty + TC_SLOTS);
+  s.m_best = reinterpret_cast<float*>(s.tmem_slot + 4);
+  s.m_group = reinterpret_cast<int*>(s.m_best + TC_RT * S::WPQ * TC_BM);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     mbar_init(s.a_full, 1);
-    mbar_init(s.a_empty, 1);
+    mbar_init(s.a_empty, TC_RT);  // both MMA threads' copies
+    for (int i = 0; i < TC_RT; ++i) mbar_init(s.a_tmem_free + i, 1);
     for (int i = 0; i < p.stages; ++i) {
       mbar_init(s.b_full + i, 1);
-      mbar_init(s.b_empty + i, 1);
+      mbar_init(s.b_empty + i, TC_RT);  // both row tiles' MMAs
     }
-    for (int i = 0; i < TC_RT; ++i) {
+    for (int i = 0; i < TC_SLOTS; ++i) {
       mbar_init(s.acc_full + i, 1);
-      mbar_init(s.acc_empty + i, TC_EPI_WARPS / TC_RT);
+      mbar_init(s.acc_empty + i, S::EPI_PER_RT);  // the warps of the item's row tile
     }
     fence_barrier_init();
   }
@@ -368,10 +388,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) assign_tc_kernel(TcParams p) {
 
   if (warp == 0) {
     if (lane == 0) tc_producer<KSTEPS>(p, s);
-  } else if (warp == 1) {
-    if (lane == 0) tc_mma<KSTEPS>(p, s, tmem_base);
+  } else if (warp < S::EPI_WARP0) {
+    if (lane == 0) tc_mma<KSTEPS>(p, s, tmem_base, warp - 1);
   } else {
-    tc_epilogue<KSTEPS>(p, s, tmem_base, warp, lane, m_best, m_group);
+    tc_epilogue<KSTEPS>(p, s, tmem_base, warp, lane);
   }
   tc_fence_before();
   __syncthreads();
@@ -379,6 +399,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) assign_tc_kernel(TcParams p) {
     tc_fence_after();
     tmem_dealloc(tmem_base, TC_TMEM_COLS);
   }
+}
+
+// Shared memory of one CTA for `stages` centroid tiles.
+template <int KSTEPS>
+static size_t tc_smem_bytes(int kp, int stages) {
+  using S = TcShape<KSTEPS>;
+  const size_t bars = (2 + TC_RT + 2 * TC_STAGES + 2 * TC_SLOTS) * sizeof(uint64_t) + 16;
+  const size_t merge = (size_t)2 * TC_RT * S::WPQ * TC_BM * 4;
+  return (size_t)TC_ROWS * kp * 4 + (size_t)stages * S::N * kp * 4 + bars + merge;
 }
 
 // Exact re-score of the winning group. On entry labels[b][i] = -(g + 1) for
@@ -529,7 +558,8 @@ static int num_sms() {
 }
 
 template <int KSTEPS>
-static cudaError_t launch_tc(const TcParams& p, int grid, size_t smem, cudaStream_t s) {
+static cudaError_t launch_tc(const TcParams& p0, int grid, cudaStream_t s) {
+  using S = TcShape<KSTEPS>;
   static thread_local int configured_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -539,7 +569,14 @@ static cudaError_t launch_tc(const TcParams& p, int grid, size_t smem, cudaStrea
     if (e != cudaSuccess) return e;
     configured_dev = dev;
   }
-  assign_tc_kernel<KSTEPS><<<grid, TC_THREADS, smem, s>>>(p);
+  TcParams p = p0;
+  int stages = TC_STAGES;
+  while (stages > 2 && tc_smem_bytes<KSTEPS>(p.kp, stages) > 227 * 1024) --stages;
+  size_t smem = tc_smem_bytes<KSTEPS>(p.kp, stages);
+  if (smem > 227 * 1024) return cudaErrorInvalidValue;
+  if (smem < TC_MIN_SMEM) smem = TC_MIN_SMEM;
+  p.stages = stages;
+  assign_tc_kernel<KSTEPS><<<grid, S::THREADS, smem, s>>>(p);
   return cudaGetLastError();
 }
 
@@ -598,18 +635,17 @@ extern "C" int skcq_assign(int metric, const float* A, const float* B, const flo
   const int64_t n_units = (int64_t)nblk * (n_pad / TC_ROWS);
   const int grid = (int)(n_units < num_sms() ? n_units : num_sms());
   cudaStream_t s = (cudaStream_t)stream;
+  TcParams p{A, B, nblk, n_pad, k_pad, kp, 0, n, k, active, labels, err};
   cudaError_t e;
-  if (kp / 8 > TC_TS_MAX_KSTEPS) {
-    e = assign_ss_launch(A, B, nblk, n_pad, k_pad, kp, n, k, active, labels, err, grid, s);
-  } else {
-    const size_t bar_bytes = (2 + 2 * TC_STAGES + 2 * TC_RT) * sizeof(uint64_t) + 16 + 2 * TC_ROWS * 4;
-    int stages = TC_STAGES;
-    auto smem_for = [&](int st) { return (size_t)TC_ROWS * kp * 4 + (size_t)st * TC_BN * kp * 4 + bar_bytes; };
-    while (stages > 2 && smem_for(stages) > 227 * 1024) --stages;
-    size_t smem = smem_for(stages);
-    if (smem < TC_MIN_SMEM) smem = TC_MIN_SMEM;
-    TcParams p{A, B, nblk, n_pad, k_pad, kp, stages, n, k, active, labels, err};
-    e = kp / 8 == 1 ? launch_tc<1>(p, grid, smem, s) : launch_tc<2>(p, grid, smem, s);
+  switch (kp / 8) {
+    case 1: e = launch_tc<1>(p, grid, s); break;
+    case 2: e = launch_tc<2>(p, grid, s); break;
+    case 3: e = launch_tc<3>(p, grid, s); break;
+    case 4: e = launch_tc<4>(p, grid, s); break;
+    case 5: e = launch_tc<5>(p, grid, s); break;
+    case 6: e = launch_tc<6>(p, grid, s); break;
+    case 7: e = launch_tc<7>(p, grid, s); break;
+    default: e = launch_tc<8>(p, grid, s); break;
   }
   if (e != cudaSuccess) return set_error(SKCQ_ERR_CUDA, "assign: %s", cudaGetErrorString(e));
   SKCQ_REQUIRE(nblk <= 65535, SKCQ_ERR_INVALID, "assign: %d problems exceed 65535", nblk);

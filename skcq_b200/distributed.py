@@ -52,8 +52,12 @@ class RowShard:
         return t.cpu() if self.host_staged and t.is_cuda else t
 
     def all_reduce_sum_(self, t: torch.Tensor) -> torch.Tensor:
+        from skcq_b200._engine import TIMER
+
         s = self._stage(t)
-        dist.all_reduce(s, op=dist.ReduceOp.SUM, group=self.group)
+        # the timer (off unless a benchmark enables it) records the bytes reduced
+        TIMER.run("allreduce", lambda: dist.all_reduce(s, op=dist.ReduceOp.SUM, group=self.group),
+                  work=float(s.numel() * s.element_size()))
         if s is not t:
             t.copy_(s)
         return t

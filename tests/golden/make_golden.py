@@ -246,8 +246,24 @@ def case_config1(out: Path, cb, bpw_mod) -> None:
     residual = cb.EuclideanCodebook(cb.EuclideanCodebookConfig(block_size=4, K=256, max_iters=20, skip_zeros=False))
     aqlm = cb.AQLMCodebook(primary, [residual], cb.AQLMCodebookConfig())
     log = EventLog(aqlm, __import__("skcq.codebook.events", fromlist=["x"]))
-    with RandpermRecorder() as rec:
-        cwr = aqlm.fit(w)
+    # every 16th primary block and every 32nd residual block: the k-means input
+    # and the reference's final fp32 centroids and labels, so the GPU
+    # assignment can be checked against the reference on its own centroids
+    km_cls = __import__("skcq.codebook.kmeans", fromlist=["x"]).KmeansExperiment
+    orig_fit = km_cls.fit
+    fits: list[tuple] = []
+
+    def recording_fit(self, data):
+        c, lab = orig_fit(self, data)
+        fits.append((data.detach().clone(), c.detach().clone(), lab.detach().clone()))
+        return c, lab
+
+    km_cls.fit = recording_fit
+    try:
+        with RandpermRecorder() as rec:
+            cwr = aqlm.fit(w)
+    finally:
+        km_cls.fit = orig_fit
     recon = aqlm.reconstruct(cwr)
     wf = w.float()
     rel = ((wf - recon).norm() / wf.norm()).item()
@@ -264,6 +280,13 @@ def case_config1(out: Path, cb, bpw_mod) -> None:
     res["c0_cent_bf16"] = bf16_bits(aqlm.primary.centroids_tensor)
     res["c1_idxs"] = cwr.residuals[0].idxs.numpy().astype(np.uint8)
     res["c1_cent_bf16"] = bf16_bits(aqlm.residuals[0].centroids_tensor)
+    assert len(fits) == 256 + 512
+    for tag, first, step, count in (("c0", 0, 16, 16), ("c1", 256, 32, 16)):
+        pick = [fits[first + i * step] for i in range(count)]
+        res[f"{tag}_fit_blocks"] = np.arange(count, dtype=np.int64) * step
+        res[f"{tag}_fit_data"] = np.stack([f[0].numpy() for f in pick]).astype(np.float32)
+        res[f"{tag}_fit_cent"] = np.stack([f[1].numpy() for f in pick]).astype(np.float32)
+        res[f"{tag}_fit_labels"] = np.stack([f[2].numpy() for f in pick]).astype(np.int16)
     np.savez_compressed(out / "config1.npz", **res)
     print(f"config1: rel_fro_err={rel:.5f} bpw={bpw:.3f}")
 
@@ -366,6 +389,47 @@ def case_metrics(out: Path, metrics, eval_model) -> None:
     np.savez_compressed(out / "metrics.npz", **res)
 
 
+def fake_moe(n_layers: int = 1, E: int = 4, H: int = 12, I: int = 8, seed: int = 0):
+    """A Hugging-Face-layout MoE holding only what the build driver reads:
+    config.text_config sizes and model.language_model.layers[i].mlp.experts
+    with gate_up_proj (E, 2I, H) and down_proj (E, H, I)."""
+    import types
+
+    g = torch.Generator().manual_seed(seed)
+    layers = []
+    for _ in range(n_layers):
+        experts = types.SimpleNamespace(gate_up_proj=torch.nn.Parameter(torch.randn(E, 2 * I, H, generator=g) * 0.1),
+                                        down_proj=torch.nn.Parameter(torch.randn(E, H, I, generator=g) * 0.1))
+        layers.append(types.SimpleNamespace(mlp=types.SimpleNamespace(experts=experts)))
+    text = types.SimpleNamespace(layers=layers)
+    cfg = types.SimpleNamespace(text_config=types.SimpleNamespace(moe_intermediate_size=I, hidden_size=H,
+                                                                  num_experts=E))
+    return types.SimpleNamespace(config=cfg, model=types.SimpleNamespace(language_model=text))
+
+
+def case_extract(out: Path, quantize_mod, config_mod) -> None:
+    """The build driver (skcq/quantize.py extract_and_build_codebooks) over a
+    one-layer MoE of 4 experts (hidden 12, intermediate 8): spherical primary
+    K=16 (3 blocks for gate/up, 2 for down) and a euclidean residual K=8,
+    5 iterations, every randperm draw recorded."""
+    torch.manual_seed(3)
+    model = fake_moe(n_layers=1)
+    params = config_mod.CodebookParams(k_gate=16, k_up=16, k_down=16, n_blocks_gate_up=3, n_blocks_down=2,
+                                       max_iters=5, norm_threshold=1e-9, skip_zeros=False, residual_k=8)
+    with RandpermRecorder() as rec:
+        res = quantize_mod.extract_and_build_codebooks(model, params, progress=False)
+    ex = model.model.language_model.layers[0].mlp.experts
+    out_d = {"gate_up": ex.gate_up_proj.data.numpy(), "down": ex.down_proj.data.numpy(), **pack_perms(rec.perms)}
+    for name, (aqlm, cwr) in res[0].items():
+        out_d[f"{name}__recon"] = aqlm.reconstruct(cwr).numpy()
+        out_d[f"{name}__c0_idxs"] = cwr.primary.idxs.numpy()
+        out_d[f"{name}__c1_idxs"] = cwr.residuals[0].idxs.numpy()
+        out_d[f"{name}__c0_cent_bf16"] = bf16_bits(aqlm.primary.centroids_tensor)
+        out_d[f"{name}__c1_cent_bf16"] = bf16_bits(aqlm.residuals[0].centroids_tensor)
+    np.savez_compressed(out / "extract.npz", **out_d)
+    print("extract: " + ", ".join(f"{k}" for k in res[0]))
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("SKCQ_REFERENCE"),
@@ -380,14 +444,16 @@ def main() -> None:
     import skcq.codebook.events as events
     import skcq.codebook.kmeans as km
     import skcq.codebook_experts as experts_mod
+    import skcq.config as config_mod
     import skcq.eval_model as eval_model
     import skcq.metrics as metrics
+    import skcq.quantize as quantize_mod
     import skcq.vq.bpw as bpw_mod
     import skcq.vq.experiment as vq_experiment
     import skcq.vq.runner as vq_runner
 
     todo = (args.only.split(",") if args.only
-            else ["assign", "kmeans", "codecs", "experts", "config1", "vq", "metrics"])
+            else ["assign", "kmeans", "codecs", "experts", "config1", "vq", "metrics", "extract"])
     if "assign" in todo:
         case_assign(HERE, km)
     if "kmeans" in todo:
@@ -402,6 +468,8 @@ def main() -> None:
         case_vq(HERE, vq_experiment, vq_runner)
     if "metrics" in todo:
         case_metrics(HERE, metrics, eval_model)
+    if "extract" in todo:
+        case_extract(HERE, quantize_mod, config_mod)
 
 
 if __name__ == "__main__":

@@ -134,3 +134,41 @@ def test_extract_and_build_on_gpu():
         err = ((recon - rows.float()).norm() / rows.float().norm()).item()
         assert err < 0.6, (name, err)
         assert cwr.primary.idxs.shape[1] == rows.shape[0]
+
+
+@pytest.mark.gpu
+def test_extract_and_build_matches_reference(monkeypatch):
+    """The build driver over a one-layer MoE (4 experts, hidden 12,
+    intermediate 8; spherical K=16 primary + euclidean K=8 residual, 5
+    iterations) against the reference's own extract_and_build_codebooks on
+    the same weights and the same recorded randperm draws: every projection's
+    reconstruction within 2e-3 and rel_fro_err within 1e-3 relative, and the
+    same primary and residual indices (the oracle finds every k-means
+    trajectory of this case tie-free)."""
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    import numpy as np
+
+    from _helpers import PermReplay, load_golden
+    from skcq_b200.quantize import extract_and_build_codebooks
+
+    g = load_golden("extract")
+    model = _fake_moe(n_layers=1)
+    ex = model.model.language_model.layers[0].mlp.experts
+    ex.gate_up_proj.data.copy_(torch.from_numpy(g["gate_up"]))
+    ex.down_proj.data.copy_(torch.from_numpy(g["down"]))
+    monkeypatch.setattr(torch, "randperm", PermReplay.from_case(g).torch_patch())
+    params = CodebookParams(k_gate=16, k_up=16, k_down=16, n_blocks_gate_up=3, n_blocks_down=2, max_iters=5,
+                            norm_threshold=1e-9, skip_zeros=False, residual_k=8)
+    res = extract_and_build_codebooks(model, params, device=torch.device("cuda"), progress=False)
+    rows = dict((n, r) for n, r, _ in projection_rows(ex, 8, 12))
+    for name, (aqlm, cwr) in res[0].items():
+        w = rows[name].double().numpy()
+        recon = aqlm.reconstruct(cwr).double().cpu().numpy()
+        ref = g[f"{name}__recon"].astype(np.float64)
+        e_gpu = np.linalg.norm(w - recon) / np.linalg.norm(w)
+        e_ref = np.linalg.norm(w - ref) / np.linalg.norm(w)
+        assert abs(e_gpu - e_ref) <= 1e-3 * e_ref, (name, e_gpu, e_ref)
+        assert np.linalg.norm(recon - ref) / np.linalg.norm(ref) < 2e-3, name
+        assert np.array_equal(cwr.primary.idxs.cpu().numpy(), g[f"{name}__c0_idxs"]), name
+        assert np.array_equal(cwr.residuals[0].idxs.cpu().numpy(), g[f"{name}__c1_idxs"]), name

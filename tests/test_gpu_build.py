@@ -244,3 +244,121 @@ def test_reconstruct_bit_exact_vs_oracle(monkeypatch):
     for x in parts[1:]:
         ref = ref + x
     assert np.array_equal(recon, ref)
+
+
+def _realistic_problem(metric: int, nblk: int, n: int, bs: int, K: int, seed: int):
+    """Student-t(5) block rows at std 0.02 (the benchmark layer's distribution);
+    centroids are K of the problem's own points (Forgy-style, as k-means
+    starts and stays near), slightly perturbed, so top-2 margins are as small
+    as a real fit makes them."""
+    from skcq_b200 import _engine
+
+    g = torch.Generator().manual_seed(seed)
+    z = torch.randn(n, nblk * bs, generator=g)
+    chi2 = torch.randn(5, n, nblk * bs, generator=g).square().sum(0)
+    w = z / torch.sqrt(chi2 / 5.0) * (0.02 / (5.0 / 3.0) ** 0.5)
+    pts = _engine.gather_block_points(w.cuda(), bs, nblk, False, 0.0, False, metric)
+    C = torch.empty(nblk, K, bs)
+    for b in range(nblk):
+        idx = torch.randperm(n, generator=g)[:K]
+        C[b] = w[idx, b * bs:(b + 1) * bs] * (1.0 + 0.01 * torch.randn(K, bs, generator=g))
+    if metric == _engine.COSINE:
+        C = torch.nn.functional.normalize(C, dim=-1)
+    return w, pts, C
+
+
+def _oracle_check_rows(metric, x, c, lab, rows):
+    """(mismatches above the 1e-5 relative margin, rows below it) for the
+    sampled rows, against the oracle's fp32 scores."""
+    xs = x[rows]
+    if metric == 0:
+        s = ok.scores_cosine(ok.normalize_rows(xs), c.T)
+        ref, sm = s.argmax(1), s
+    else:
+        s = ok.scores_l2(xs, c.T)
+        ref, sm = s.argmin(1), -s
+    part = np.partition(sm, -2, axis=1)[:, -2:]
+    rel = (part[:, 1] - part[:, 0]) / (np.abs(part[:, 1]) + np.abs(part[:, 0]) + 1e-30)
+    m = rel > 1e-5
+    return int((lab[rows][m] != ref[m]).sum()), int((~m).sum())
+
+
+@pytest.mark.parametrize("metric,bs,K,nblk", [
+    (1, 4, 65536, 2),   # second residual of the benchmark layer
+    (0, 8, 4096, 2),    # its primary
+    (1, 16, 4096, 2),   # its first residual
+    (0, 12, 65536, 1),  # full-model primary (non-dividing block size 12)
+    (1, 6, 16384, 2),   # full-model residual
+])
+def test_assign_bench_shapes_match_oracle(metric, bs, K, nblk):
+    """The benchmark's assignment shapes at 98,304 points per problem: labels
+    bit-exact against the oracle on 2,048 sampled rows per problem wherever
+    the relative top-2 margin exceeds 1e-5 (rows below it are counted)."""
+    n = 98304
+    w, pts, C = _realistic_problem(metric, nblk, n, bs, K, seed=bs * 131 + K + metric)
+    lab = _labels(pts, C, exact=False)
+    rng = np.random.default_rng(K + bs)
+    near_ties = 0
+    for b in range(nblk):
+        rows = np.sort(rng.choice(n, 2048, replace=False))
+        x = w[:, b * bs:(b + 1) * bs].numpy()
+        bad, ties = _oracle_check_rows(metric, x, C[b].numpy(), lab[b], rows)
+        near_ties += ties
+        assert bad == 0, f"block {b}: {bad} labels differ above the margin"
+    print(f"metric={metric} bs={bs} K={K}: {near_ties} of {2048 * nblk} sampled rows below the 1e-5 margin")
+
+
+def test_config1_assign_on_reference_centroids():
+    """Config 1 (768 x 2048, SSVQ spherical bs=8 K=256 + euclidean bs=4 K=256):
+    for 16 primary and 16 residual blocks the reference's k-means input and
+    final fp32 centroids are replayed through the GPU assignment; labels equal
+    the reference's own final labels wherever the relative top-2 margin
+    exceeds 1e-5."""
+    from skcq_b200 import _engine
+
+    g = load_golden("config1")
+    for tag, metric in (("c0", _engine.COSINE), ("c1", _engine.L2)):
+        data, cent, ref_lab = g[f"{tag}_fit_data"], g[f"{tag}_fit_cent"], g[f"{tag}_fit_labels"].astype(np.int64)
+        nblk, n, bs = data.shape
+        w = torch.from_numpy(np.ascontiguousarray(data.transpose(1, 0, 2).reshape(n, nblk * bs)))
+        pts = _engine.gather_block_points(w.cuda(), bs, nblk, False, 0.0, False, metric)
+        lab = _labels(pts, torch.from_numpy(cent), exact=False)
+        total_ties = 0
+        for b in range(nblk):
+            x, c = data[b], cent[b]
+            if metric == _engine.COSINE:
+                s = ok.scores_cosine(ok.normalize_rows(x), c.T)
+                sm = s
+            else:
+                s = ok.scores_l2(x, c.T)
+                sm = -s
+            part = np.partition(sm, -2, axis=1)[:, -2:]
+            rel = (part[:, 1] - part[:, 0]) / (np.abs(part[:, 1]) + np.abs(part[:, 0]) + 1e-30)
+            m = rel > 1e-5
+            total_ties += int((~m).sum())
+            assert (lab[b][m] == ref_lab[b][m]).all(), (tag, b, int((lab[b][m] != ref_lab[b][m]).sum()))
+        print(f"config1 {tag}: {total_ties} of {nblk * n} rows below the 1e-5 margin")
+
+
+def test_quantize_spherical_scales_matches_oracle():
+    """int<N> scale quantisation (spherical.py:45-71) on the GPU equals the
+    oracle bit for bit: the same q_scale and the same rounded levels, for the
+    fitted scales of a reference case and for signed random scales with
+    zeros, at 4, 8 and 16 bits."""
+    import test_oracle_golden as T
+    from skcq_b200 import _engine
+
+    g = sub(load_golden("codecs"), "sq8__")
+    prim, res, _, _ = T._spec("base", 1)
+    primary, _, cwr = oc.aqlm_fit(prim, res, g["w"], sobol_np, PermReplay.from_case(g), norm_threshold=1e-9)
+    fitted = cwr["primary"]["scales"].astype(np.float32)
+    rnd = np.random.default_rng(5).standard_normal((300, 70)).astype(np.float32) * 0.03
+    rnd[::7] = 0.0
+    for scales in (fitted, rnd):
+        for bits in (4, 8, 16):
+            oc_cwr = {"scales": scales.copy()}
+            codec = oc.Codec("spherical", oc.SphericalCfg(4, 16))
+            oc.quantize_scales(oc_cwr, codec, f"int{bits}")
+            q, q_scale = _engine.quantize_scales_int(torch.from_numpy(scales).cuda(), bits)
+            assert float(q_scale) == codec.q_scale
+            assert np.array_equal(q.cpu().numpy(), oc_cwr["scales"])

@@ -124,9 +124,10 @@ def test_bf16_module_within_bf16_tolerance(monkeypatch):
         assert b16.dtype == torch.bfloat16
         b = b16.double()
         cos = torch.nn.functional.cosine_similarity(a.flatten(), b.flatten(), dim=0).item()
-        # tolerance: bf16 inputs, codebook and output (8 mantissa bits)
-        assert (a - b).abs().max().item() <= 2e-2 * a.abs().max().item() + 1e-3
-        assert cos >= 0.999
+        # the forward tolerance for bf16 (bf16 inputs, scales and output):
+        # max error <= 1e-2 of the output's max, cosine >= 0.9999
+        assert (a - b).abs().max().item() <= 1e-2 * a.abs().max().item()
+        assert cos >= 0.9999
 
 
 def test_state_dict_round_trip(monkeypatch):
