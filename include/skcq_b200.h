@@ -281,7 +281,23 @@ typedef struct skcq_fwd_layer {
   const void* remainder;        /* (E, out, rem), f32 | bf16 */
   int rem_dtype, rem;
   const uint32_t* sign_mask;    /* (E, n_blocks, out) bit j: column b*bs+j negated, or NULL */
+  /* Per-token lookup table of this layer (the reference's matmul_gather
+   * mode, codebook_experts.py:57-60), or NULL: lut[(b * K + k) * lut_tokens + t]
+   * = <x_b(t), C_b[k]> for the lut_tokens rows t of x (skcq_lut_build). When
+   * set, skcq_codebook_forward reads each block's dot from it instead of
+   * gathering the centroid; the arithmetic is the same, so the output is
+   * bit-identical. Requires sign_mask == NULL. */
+  const float* lut;
+  int lut_tokens;
 } skcq_fwd_layer;
+
+/* The lookup table of skcq_fwd_layer.lut for one layer: for every block b,
+ * centroid k and row t < T of x (f32 | bf16, row stride x_ld),
+ * lut[(b * K + k) * T + t] = sum over j in order of fma(x[t][b*bs + j],
+ * C_b[k][j]) (the block dot the decode kernel forms; no signs).
+ * lut holds n_blocks * K * T floats. */
+int skcq_lut_build(const skcq_fwd_layer* layer, const void* x, int x_dtype, int64_t x_ld, int T, float* lut,
+                   void* stream);
 
 /* out[i] = (uint16) idx[i] for the reference's int64 assignments
  * (codebook_experts.py:95); an index outside [0, K) is stored as 0 and sets the

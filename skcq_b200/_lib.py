@@ -67,6 +67,7 @@ _SIGS: dict[str, list] = {
     "skcq_pack_indices16": [P, L, I, P, P],
     "skcq_transpose_codebook": [P, I, I, I, I, P, P],
     "skcq_pack_sign_masks": [P, I, I, L, I, I, P, P],
+    "skcq_lut_build": [P, P, I, L, I, P, P],
     "skcq_route_sort": [P, I, I, I, P, P, P, P, P, C.c_size_t, P],
     "skcq_route_sort_scratch_bytes": [I, I, I],
     "skcq_codebook_forward": [P, I, P, I, L, P, I, P, P, P, I, I, I, I, I, I, P, L, P],
@@ -121,6 +122,7 @@ _KERNELS_PER_CALL = {
     "skcq_row_zero_mask": 1, "skcq_spherical_scales": 1, "skcq_centroids_to_bf16": 1, "skcq_copy_remainder": 1,
     "skcq_ssvq_fold": 1, "skcq_quantize_centroids": 1, "skcq_quantize_scales": 3, "skcq_reconstruct": 1,
     "skcq_refit_scales": 1, "skcq_pack_indices16": 1, "skcq_transpose_codebook": 1, "skcq_pack_sign_masks": 1,
+    "skcq_lut_build": 1,
     "skcq_route_sort": 1, "skcq_sum_splits": 1, "skcq_swiglu": 1, "skcq_combine": 1,
     "skcq_prefill_plan": 1, "skcq_prefill_pack": 1, "skcq_prefill_dequant": 1, "skcq_prefill_gemm": 1,
     "skcq_prefill_gemm_swiglu": 1,

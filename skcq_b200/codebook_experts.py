@@ -179,6 +179,7 @@ class FwdLayer(_lib.C.Structure):
         ("scales", _lib.P), ("scale_dtype", _lib.I), ("q_scale", _lib.F),
         ("remainder", _lib.P), ("rem_dtype", _lib.I), ("rem", _lib.I),
         ("sign_mask", _lib.P),
+        ("lut", _lib.P), ("lut_tokens", _lib.I),
     ]
 
 
@@ -337,19 +338,37 @@ class CodebookModule(nn.Module):
                      n_seg: int, *, row_token: torch.Tensor | None = None, T: int = 0,
                      active: torch.Tensor | None = None, max_active: int | None = None,
                      n_rows: int | None = None, n_split: int | None = None,
-                     rows_hint: int | None = None) -> tuple[torch.Tensor, int]:
+                     rows_hint: int | None = None,
+                     lut_layers: list[bool] | None = None) -> tuple[torch.Tensor, int]:
         """Grouped forward over expert segments of rows (device tensors).
 
         Row r of segment s (expert ``seg_expert[s]``, or s) reads
-        ``x[row_token[r] % T]`` (``x[r]`` without a token map). Returns the
-        ``(n_split, n_rows, out_dim)`` f32 partial sums and ``n_split``; their
-        sum over the first axis is the module output."""
+        ``x[row_token[r] % T]`` (``x[r]`` without a token map). Layers flagged
+        in ``lut_layers`` (and without signs) read their block dots from a
+        per-row lookup table built here (codebook_experts.py:57-60); the
+        result is the same. Returns the ``(n_split, n_rows, out_dim)`` f32
+        partial sums and ``n_split``; their sum over the first axis is the
+        module output."""
         x = _as_rows(x)
         dev = x.device
         P = int(n_rows if n_rows is not None else (row_token.numel() if row_token is not None else x.shape[0]))
         max_active = n_seg if max_active is None else max_active
         S = n_split or _choose_splits(max_active, self.out_dim, self.min_blocks, P)
         descs = [layer.descriptor(dev, primary=(i == 0)) for i, layer in enumerate(self.layers)]
+        luts = []
+        if lut_layers is not None:
+            # the reference's matmul_gather mode for these layers: per-row tables
+            # of block dots over x's rows, read by the forward instead of
+            # gathering centroids (identical results)
+            n_tok = T if row_token is not None else x.shape[0]
+            for d, use in zip(descs, lut_layers, strict=False):
+                if not use or d.sign_mask:
+                    continue
+                lut = torch.empty(d.n_blocks * d.K * n_tok, dtype=torch.float32, device=dev)
+                call("skcq_lut_build", _lib.C.addressof(d), ptr(x), _DTYPE[x.dtype], x.stride(0), n_tok, ptr(lut),
+                     stream())
+                d.lut, d.lut_tokens = ptr(lut), n_tok
+                luts.append(lut)
         arr = (FwdLayer * len(descs))(*descs)
         part = torch.empty(S, P, self.out_dim, dtype=torch.float32, device=dev)
         hint = rows_hint if rows_hint is not None else -(-P // max(1, max_active))
@@ -458,6 +477,13 @@ class CodebookExperts(nn.Module):
     # bf16 batches with at least this many (token, slot) rows per expert on
     # average take the tensor-core prefill path
     prefill_min_rows: int = 32
+    # Decode lookup tables (the reference's matmul_gather mode): "off";
+    # "on" for every sign-free layer of the three projections; "auto" for the
+    # sign-free layers whose table build (one block dot per token and
+    # centroid) does less work than the gathers it replaces (one per routed
+    # row and output) and whose table stays below lut_max_bytes.
+    decode_lut: str = "auto"
+    lut_max_bytes: int = 64 << 20
 
     def __init__(self, gate: CodebookModule, up: CodebookModule, down: CodebookModule, num_experts: int,
                  act_fn: Callable[[torch.Tensor], torch.Tensor]) -> None:
@@ -500,21 +526,37 @@ class CodebookExperts(nn.Module):
         S = _choose_splits(max_active, I, min(self.gate.min_blocks, self.up.min_blocks), P)
         # rows per expert: at most T when a token's k experts are distinct
         seg_kw = {"active": active, "max_active": max_active, "n_rows": P, "rows_hint": min(T, 8)}
-        g, _ = self.gate.run_segments(h, seg, None, E, row_token=perm, T=T, n_split=S, **seg_kw)
-        u, _ = self.up.run_segments(h, seg, None, E, row_token=perm, T=T, n_split=S, **seg_kw)
+        g, _ = self.gate.run_segments(h, seg, None, E, row_token=perm, T=T, n_split=S,
+                                      lut_layers=self._lut_layers(self.gate, T, P), **seg_kw)
+        u, _ = self.up.run_segments(h, seg, None, E, row_token=perm, T=T, n_split=S,
+                                    lut_layers=self._lut_layers(self.up, T, P), **seg_kw)
         inter = torch.empty(P, I, dtype=torch.float32, device=dev)
         if _is_silu(self.intermediate.act_fn):
             call("skcq_swiglu", ptr(g), ptr(u), S, P * I, ptr(inter), stream())
         else:
             gs, us = g.sum(0), u.sum(0)
             inter.copy_(self.intermediate(gs, us))
-        d, Sd = self.down.run_segments(inter, seg, None, E, **seg_kw)
+        d, Sd = self.down.run_segments(inter, seg, None, E, lut_layers=self._lut_layers(self.down, P, P), **seg_kw)
         out = torch.empty(T, H, dtype=h.dtype, device=dev)
         call("skcq_combine", ptr(d), _DTYPE[d.dtype], Sd, P, ptr(inv), ptr(topk), ptr(w), _DTYPE[w.dtype], T, k, H,
              ptr(out), _DTYPE[out.dtype], stream())
         if self.check_errors:
             _lib.poll_device_error()
         return out.to(device=hidden_states.device, dtype=hidden_states.dtype)
+
+    def _lut_layers(self, mod: CodebookModule, n_tok: int, P: int) -> list[bool] | None:
+        """Which layers of ``mod`` read a lookup table: x has ``n_tok`` rows and
+        ``P`` routed rows are computed."""
+        if self.decode_lut == "off":
+            return None
+        use = []
+        for lay in mod.layers:
+            table = lay.n_blocks * lay.k * n_tok * 4
+            ok = lay.signs is None and table <= self.lut_max_bytes and lay.block_size in (4, 6, 8, 12, 16)
+            if self.decode_lut == "auto":
+                ok = ok and n_tok * lay.k < P * mod.out_dim
+            use.append(ok)
+        return use if any(use) else None
 
     def _use_prefill(self, h: torch.Tensor, P: int, max_active: int) -> bool:
         mods = (self.gate, self.up, self.down)

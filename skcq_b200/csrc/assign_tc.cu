@@ -88,8 +88,14 @@ struct TcSmem {
   uint64_t* a_tmem_free;  // [TC_RT] the row tile's MMAs of the previous unit done: its A columns reusable
   uint64_t* b_full;
   uint64_t* b_empty;
-  uint64_t* acc_full;   // [TC_SLOTS]
-  uint64_t* acc_empty;  // [TC_SLOTS]
+  // [TC_SLOTS][2]: use u of slot s signals on barrier (s, u & 1). Consecutive
+  // uses of a slot belong to alternating row tiles (three slots, two row
+  // tiles), so each barrier object has one signalling and one waiting party
+  // and sees its phases strictly in order; with one barrier per slot a party
+  // running ahead could meet a barrier two phases behind and pass its parity
+  // test early.
+  uint64_t* acc_full;
+  uint64_t* acc_empty;
   uint32_t* tmem_slot;
   float* m_best;        // [TC_RT][NG][TC_BM] per-warp candidates, merged per unit
   int* m_group;
@@ -205,14 +211,18 @@ __device__ void tc_mma(const TcParams& p, const TcSmem& s, uint32_t tmem_base, i
       if (!mbar_wait(s.b_full + br.idx, br.phase, p.err, 14)) return;
       const uint32_t slot = item % TC_SLOTS;
       const uint32_t use = item / TC_SLOTS;
-      if (!mbar_wait(s.acc_empty + slot, (use & 1) ^ 1, p.err, 15)) return;
+      if (use > 0) {
+        // the slot's previous use (the other row tile's item) has been read
+        const uint32_t prev = use - 1;
+        if (!mbar_wait(s.acc_empty + 2 * slot + (prev & 1), (prev >> 1) & 1, p.err, 15)) return;
+      }
       tc_fence_after();
       const uint64_t bd = b0 + br.idx * b_st;
       const uint32_t d = tmem_base + slot * N;
       mma_tf32_ts_first(d, a_tm, bd, idesc);
 #pragma unroll
       for (int ks = 1; ks < KSTEPS; ++ks) mma_tf32_ts_acc(d, a_tm + ks * 8, bd + 16 * ks, idesc);
-      tc_commit(s.acc_full + slot);
+      tc_commit(s.acc_full + 2 * slot + (use & 1));
       tc_commit(s.b_empty + br.idx);  // one of the two arrivals that free the stage
       br.next(p.stages);
     }
@@ -289,7 +299,9 @@ __device__ void tc_epilogue(const TcParams& p, const TcSmem& s, uint32_t tmem_ba
     for (int j = 0; j < nbt; ++j, item += TC_RT) {
       if (failed) continue;
       const uint32_t slot = item % TC_SLOTS;
-      const bool ok = mbar_wait(s.acc_full + slot, (item / TC_SLOTS) & 1, p.err, 16);
+      const uint32_t use = item / TC_SLOTS;
+      const uint32_t bar = 2 * slot + (use & 1);
+      const bool ok = mbar_wait(s.acc_full + bar, (use >> 1) & 1, p.err, 16);
       if (!__all_sync(0xffffffffu, ok)) {
         failed = true;
         continue;
@@ -301,7 +313,7 @@ __device__ void tc_epilogue(const TcParams& p, const TcSmem& s, uint32_t tmem_ba
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(s.acc_empty + slot);  // one arrival per warp
+      if (lane == 0) mbar_arrive(s.acc_empty + bar);  // one arrival per warp
       const int gg = j * NG + h * GPW;  // global index of the first group
       if ((j + 1) * N > kb) {  // only the problem's last tile has columns past k
         mask_group(v0, gg * GROUP, kb);
@@ -357,8 +369,8 @@ __global__ void __launch_bounds__(TcShape<KSTEPS>::THREADS, 1) assign_tc_kernel(
   s.b_full = bars + 2 + TC_RT;
   s.b_empty = s.b_full + TC_STAGES;
   s.acc_full = s.b_empty + TC_STAGES;
-  s.acc_empty = s.acc_full + TC_SLOTS;
-  s.tmem_slot = reinterpret_cast<uint32_t*>(s.acc_empty + TC_SLOTS);
+  s.acc_empty = s.acc_full + 2 * TC_SLOTS;
+  s.tmem_slot = reinterpret_cast<uint32_t*>(s.acc_empty + 2 * TC_SLOTS);
   s.m_best = reinterpret_cast<float*>(s.tmem_slot + 4);
   s.m_group = reinterpret_cast<int*>(s.m_best + TC_RT * S::WPQ * TC_BM);
 
@@ -371,7 +383,7 @@ __global__ void __launch_bounds__(TcShape<KSTEPS>::THREADS, 1) assign_tc_kernel(
       mbar_init(s.b_full + i, 1);
       mbar_init(s.b_empty + i, TC_RT);  // both row tiles' MMAs
     }
-    for (int i = 0; i < TC_SLOTS; ++i) {
+    for (int i = 0; i < 2 * TC_SLOTS; ++i) {
       mbar_init(s.acc_full + i, 1);
       mbar_init(s.acc_empty + i, S::EPI_PER_RT);  // the warps of the item's row tile
     }
@@ -405,7 +417,7 @@ __global__ void __launch_bounds__(TcShape<KSTEPS>::THREADS, 1) assign_tc_kernel(
 template <int KSTEPS>
 static size_t tc_smem_bytes(int kp, int stages) {
   using S = TcShape<KSTEPS>;
-  const size_t bars = (2 + TC_RT + 2 * TC_STAGES + 2 * TC_SLOTS) * sizeof(uint64_t) + 16;
+  const size_t bars = (2 + TC_RT + 2 * TC_STAGES + 4 * TC_SLOTS) * sizeof(uint64_t) + 16;
   const size_t merge = (size_t)2 * TC_RT * S::WPQ * TC_BM * 4;
   return (size_t)TC_ROWS * kp * 4 + (size_t)stages * S::N * kp * 4 + bars + merge;
 }

@@ -488,6 +488,158 @@ __global__ void __launch_bounds__(FW_THREADS) fwd_layer_kernel(FwdArgs a, skcq_f
   }
 }
 
+// ---------------------------------------------------------------------------
+// Lookup-table decode (the reference's matmul_gather mode,
+// codebook_experts.py:57-60): the per-token table of block dots is built once
+// per layer and the forward reads one float per (row, block, output) instead
+// of gathering a centroid vector. Each table entry is the block dot the gather
+// kernel forms (same fused multiply-adds in the same order), so both paths
+// produce identical bits.
+// ---------------------------------------------------------------------------
+
+constexpr int LUT_THREADS = 256;
+
+// lut[(b K + k) T + t] = <x_b(t), C_b[k]>. One CTA per (block, 256 centroids);
+// the block's columns of every row of x are staged in shared memory.
+template <int BS, typename T>
+__global__ void __launch_bounds__(LUT_THREADS) lut_build_kernel(skcq_fwd_layer L, const void* __restrict__ x,
+                                                                int x_dtype, int64_t x_ld, int n_tok,
+                                                                float* __restrict__ lut) {
+  extern __shared__ float xb[];  // [n_tok][BS]
+  const int b = blockIdx.y;
+  for (int i = threadIdx.x; i < n_tok * BS; i += LUT_THREADS) {
+    const int t = i / BS, j = i - t * BS;
+    xb[i] = ld_any(x, (int64_t)t * x_ld + (int64_t)b * BS + j, x_dtype);
+  }
+  __syncthreads();
+  const int k = blockIdx.x * LUT_THREADS + threadIdx.x;
+  if (k >= L.K) return;
+  float w[BS];
+  load_centroid<BS, T>(static_cast<const T*>(L.table) + ((int64_t)b * L.K + k) * BS, w);
+  float* dst = lut + ((int64_t)b * L.K + k) * n_tok;
+  for (int t = 0; t < n_tok; ++t) {
+    float d = 0.f;
+#pragma unroll
+    for (int j = 0; j < BS; ++j) d = __fmaf_rn(xb[t * BS + j], w[j], d);
+    dst[t] = d;
+  }
+}
+
+// The forward of fwd_layer_kernel (same grid, rows, splits and partial sums)
+// reading block dots from the layer's lookup table.
+constexpr int LUT_UNROLL = 8;
+
+template <int R>
+__global__ void __launch_bounds__(FW_THREADS) fwd_lut_kernel(FwdArgs a, skcq_fwd_layer L) {
+  extern __shared__ float xs[];  // [R][rem] remainder columns (last split)
+  __shared__ int tok[R];
+  const int out = a.out_dim;
+  const int tiles = (out + FW_THREADS - 1) / FW_THREADS;
+  const int n_act = a.active ? a.active[0] : a.n_seg;
+  const int per_split = n_act * tiles;
+  const int item = blockIdx.x;
+  if (item >= per_split * a.n_split) return;
+  const int split = item / per_split;
+  const int rest = item - split * per_split;
+  const int ai = rest / tiles, tile = rest - ai * tiles;
+  const int s = a.active ? a.active[1 + ai] : ai;
+  const int r0 = a.seg[s], r1 = a.seg[s + 1];
+  if (r0 >= r1) return;
+  const int e = a.seg_expert ? a.seg_expert[s] : s;
+  const int nb = L.n_blocks;
+  const int b0 = (int)((int64_t)nb * split / a.n_split), b1 = (int)((int64_t)nb * (split + 1) / a.n_split);
+  const bool last = split == a.n_split - 1;
+  const int cov = nb * L.bs;
+  const int rem = last ? L.rem : 0;
+  const int o = tile * FW_THREADS + threadIdx.x;
+  const bool live = o < out;
+  const int64_t K = L.K;
+  const int nt = L.lut_tokens;
+  for (int rc = r0; rc < r1; rc += R) {
+    const int nr = min(R, r1 - rc);
+    __syncthreads();
+    if (threadIdx.x < R) {
+      const int row = rc + min((int)threadIdx.x, nr - 1);
+      tok[threadIdx.x] = a.row_token ? (int)(a.row_token[row] % a.T) : row;
+    }
+    for (int i = threadIdx.x; i < R * rem; i += FW_THREADS) {
+      const int rr = i / rem, c = i - rr * rem;
+      float v = 0.f;
+      if (rr < nr) {
+        const int row = rc + rr;
+        const int64_t tk = a.row_token ? (int64_t)(a.row_token[row] % a.T) : (int64_t)row;
+        v = ld_any(a.x, tk * a.x_ld + cov + c, a.x_dtype);
+      }
+      xs[i] = v;
+    }
+    __syncthreads();
+    if (!live) continue;
+    int tr[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) tr[r] = tok[r];
+    float acc[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) acc[r] = 0.f;
+    const uint16_t* ix = L.idx16 + (int64_t)e * nb * out + o;
+    const bool scaled = L.scales != nullptr;
+    int b = b0;
+    for (; b + LUT_UNROLL <= b1; b += LUT_UNROLL) {
+      int idx[LUT_UNROLL];
+#pragma unroll
+      for (int u = 0; u < LUT_UNROLL; ++u) idx[u] = __ldg(ix + (int64_t)(b + u) * out);
+      float d[LUT_UNROLL][R];
+#pragma unroll
+      for (int u = 0; u < LUT_UNROLL; ++u) {
+        const float* base = L.lut + ((int64_t)(b + u) * K + idx[u]) * nt;
+#pragma unroll
+        for (int r = 0; r < R; ++r) d[u][r] = __ldg(base + tr[r]);
+      }
+#pragma unroll
+      for (int u = 0; u < LUT_UNROLL; ++u) {
+        const float sc =
+            scaled ? ld_scale(L.scales, ((int64_t)e * nb + b + u) * out + o, L.scale_dtype, L.q_scale) : 1.f;
+#pragma unroll
+        for (int r = 0; r < R; ++r) acc[r] = scaled ? __fmaf_rn(d[u][r], sc, acc[r]) : acc[r] + d[u][r];
+      }
+    }
+    for (; b < b1; ++b) {
+      const int idx = __ldg(ix + (int64_t)b * out);
+      const float* base = L.lut + ((int64_t)b * K + idx) * nt;
+      const float sc = scaled ? ld_scale(L.scales, ((int64_t)e * nb + b) * out + o, L.scale_dtype, L.q_scale) : 1.f;
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const float d = __ldg(base + tr[r]);
+        acc[r] = scaled ? __fmaf_rn(d, sc, acc[r]) : acc[r] + d;
+      }
+    }
+    // raw remainder columns x[:, cov:cov+rem] @ rem_w[e].T (codebook_experts.py:64-74)
+    for (int c = 0; c < rem; ++c) {
+      const float wv = ld_any(L.remainder, ((int64_t)e * out + o) * L.rem + c, L.rem_dtype);
+#pragma unroll
+      for (int r = 0; r < R; ++r) acc[r] = __fmaf_rn(xs[r * rem + c], wv, acc[r]);
+    }
+    float* dst = a.part + ((int64_t)split * a.P + rc) * out + o;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      if (r < nr) {
+        float v = acc[r];
+        if (a.accumulate) v += dst[(int64_t)r * out];
+        dst[(int64_t)r * out] = v;
+      }
+    }
+  }
+}
+
+static void launch_lut(const FwdArgs& a, const skcq_fwd_layer& L, int R, int grid, cudaStream_t s) {
+  const size_t smem = (size_t)R * L.rem * sizeof(float);
+  switch (R) {
+    case 1: fwd_lut_kernel<1><<<grid, FW_THREADS, smem, s>>>(a, L); break;
+    case 2: fwd_lut_kernel<2><<<grid, FW_THREADS, smem, s>>>(a, L); break;
+    case 4: fwd_lut_kernel<4><<<grid, FW_THREADS, smem, s>>>(a, L); break;
+    default: fwd_lut_kernel<8><<<grid, FW_THREADS, smem, s>>>(a, L); break;
+  }
+}
+
 template <int BS, int R>
 void launch_layer_r(const FwdArgs& a, const skcq_fwd_layer& L, int grid, size_t smem, cudaStream_t s) {
   if (L.table_dtype == SKCQ_DTYPE_BF16)
@@ -709,6 +861,16 @@ extern "C" int skcq_codebook_forward(const skcq_fwd_layer* layers, int n_layers,
     SKCQ_REQUIRE(L.rem == 0 || L.remainder, SKCQ_ERR_INVALID, "codebook_forward: layer %d remainder missing", i);
     SKCQ_REQUIRE(L.rem == 0 || L.rem_dtype == SKCQ_DTYPE_F32 || L.rem_dtype == SKCQ_DTYPE_BF16, SKCQ_ERR_INVALID,
                  "codebook_forward: layer %d remainder dtype %d", i, L.rem_dtype);
+    if (L.lut) {
+      SKCQ_REQUIRE(L.sign_mask == nullptr, SKCQ_ERR_INVALID,
+                   "codebook_forward: layer %d has signs; its lookup table cannot apply them", i);
+      SKCQ_REQUIRE(row_token ? L.lut_tokens == T : L.lut_tokens >= P, SKCQ_ERR_INVALID,
+                   "codebook_forward: layer %d lookup table covers %d rows of x (need %lld)", i, L.lut_tokens,
+                   row_token ? (long long)T : (long long)P);
+      SKCQ_REQUIRE((size_t)R * L.rem * sizeof(float) <= 48 * 1024, SKCQ_ERR_INVALID,
+                   "codebook_forward: layer %d remainder of %d columns too wide for the lookup path", i, L.rem);
+      continue;
+    }
     const int per = (L.n_blocks + n_split - 1) / n_split;
     const size_t smem = (size_t)R * (per * L.bs + L.rem) * sizeof(float);
     if (smem > smem_max) smem_max = smem;
@@ -738,6 +900,12 @@ extern "C" int skcq_codebook_forward(const skcq_fwd_layer* layers, int n_layers,
     const int per = (L.n_blocks + n_split - 1) / n_split;
     const size_t smem = (size_t)R * (per * L.bs + L.rem) * sizeof(float);
     a.accumulate = i > 0;
+    if (L.lut) {
+      launch_lut(a, L, R, (int)grid64, s);
+      int rc = check_launch("codebook_forward (lookup table)");
+      if (rc != SKCQ_OK) return rc;
+      continue;
+    }
     switch (L.bs) {
       case 4: launch_layer<4>(a, L, R, (int)grid64, smem, s); break;
       case 6: launch_layer<6>(a, L, R, (int)grid64, smem, s); break;
@@ -750,6 +918,51 @@ extern "C" int skcq_codebook_forward(const skcq_fwd_layer* layers, int n_layers,
     if (rc != SKCQ_OK) return rc;
   }
   return SKCQ_OK;
+}
+
+extern "C" int skcq_lut_build(const skcq_fwd_layer* layer, const void* x, int x_dtype, int64_t x_ld, int T, float* lut,
+                              void* stream) {
+  SKCQ_REQUIRE(layer && x && lut, SKCQ_ERR_INVALID, "lut_build: null pointer");
+  const skcq_fwd_layer& L = *layer;
+  SKCQ_REQUIRE(L.table && L.bs > 0 && L.bs <= 32 && L.K > 0 && L.n_blocks >= 0, SKCQ_ERR_INVALID,
+               "lut_build: layer incomplete or bs %d / K %d out of range", L.bs, L.K);
+  SKCQ_REQUIRE(L.table_dtype == SKCQ_DTYPE_F32 || L.table_dtype == SKCQ_DTYPE_BF16, SKCQ_ERR_INVALID,
+               "lut_build: table dtype %d", L.table_dtype);
+  SKCQ_REQUIRE(x_dtype == SKCQ_DTYPE_F32 || x_dtype == SKCQ_DTYPE_BF16, SKCQ_ERR_INVALID, "lut_build: x dtype %d",
+               x_dtype);
+  SKCQ_REQUIRE(T >= 1, SKCQ_ERR_INVALID, "lut_build: %d rows", T);
+  const size_t smem = (size_t)T * L.bs * sizeof(float);
+  SKCQ_REQUIRE(smem <= 96 * 1024, SKCQ_ERR_INVALID, "lut_build: %d rows of block size %d exceed shared memory", T,
+               L.bs);
+  SKCQ_REQUIRE(L.n_blocks <= 65535, SKCQ_ERR_INVALID, "lut_build: %d blocks", L.n_blocks);
+  if (L.n_blocks == 0) return SKCQ_OK;
+  const dim3 grid((unsigned)ceil_div(L.K, LUT_THREADS), (unsigned)L.n_blocks);
+  cudaStream_t s = (cudaStream_t)stream;
+  const bool bf = L.table_dtype == SKCQ_DTYPE_BF16;
+#define SKCQ_LUT_CASE(BSV)                                                                                   \
+  case BSV:                                                                                                  \
+    if (bf) {                                                                                                \
+      cudaFuncSetAttribute(lut_build_kernel<BSV, __nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                           96 * 1024);                                                                       \
+      lut_build_kernel<BSV, __nv_bfloat16><<<grid, LUT_THREADS, smem, s>>>(L, x, x_dtype, x_ld, T, lut);     \
+    } else {                                                                                                 \
+      cudaFuncSetAttribute(lut_build_kernel<BSV, float>, cudaFuncAttributeMaxDynamicSharedMemorySize,         \
+                           96 * 1024);                                                                       \
+      lut_build_kernel<BSV, float><<<grid, LUT_THREADS, smem, s>>>(L, x, x_dtype, x_ld, T, lut);             \
+    }                                                                                                        \
+    break;
+  switch (L.bs) {
+    SKCQ_LUT_CASE(4)
+    SKCQ_LUT_CASE(6)
+    SKCQ_LUT_CASE(8)
+    SKCQ_LUT_CASE(12)
+    SKCQ_LUT_CASE(16)
+    default:
+      return set_error(SKCQ_ERR_INVALID, "lut_build: block size %d has no lookup-table kernel (4, 6, 8, 12, 16)",
+                       L.bs);
+  }
+#undef SKCQ_LUT_CASE
+  return check_launch("lut_build");
 }
 
 extern "C" int skcq_sum_splits(const float* part, int n_split, int64_t P, int out_dim, void* y, int y_dtype,

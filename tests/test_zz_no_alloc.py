@@ -72,9 +72,9 @@ def test_noalloc_reseed_matches_reseed_on_two_calls_in_a_row():
     # shapes; third: K = 65536 (768 KiB of scratch per problem, so only 21
     # problems fit the static array at once and CTAs reuse their slot for
     # several problems), with more empty clusters than the shared-memory sort
-    # holds, so the sort runs in the static array
+    # holds, so the sort runs in the static array (n >= K, as in any fit)
     for metric, nblk, n, bs, K, seed in ((0, 5, 3000, 8, 2048, 1), (1, 3, 6000, 4, 4000, 2),
-                                         (1, 32, 12000, 4, 65536, 3)):
+                                         (1, 32, 70000, 4, 65536, 3)):
         s_ref, s_new, e_ref, e_new = _reseed_both(metric, nblk, n, bs, K, seed)
         assert int(e_ref.min()) > 0, "the case must have empty clusters"
         if K == 65536:
