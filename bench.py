@@ -334,16 +334,10 @@ def forward_bench(wl: dict, fits: dict, dev: str, peaks: dict) -> dict:
     res = {"decode": [], "prefill": None}
     from skcq_b200.codebook_experts import GraphedExperts
 
-    for T in (1, 8, 64):
+    for T in (1, 2, 4, 8, 16, 32, 64):
         x = torch.randn(T, H, generator=gen, device=dev).to(torch.bfloat16)
         topi, topw = _route(T, E, 8, gen, dev)
-        y, yd = ex(x, topi, topw).float(), dfwd(x, topi, topw).float()
-        cos = torch.nn.functional.cosine_similarity(y.flatten(), yd.flatten(), dim=0).item()
-        ms_eager = _time_ms(lambda: ex(x, topi, topw), 20, flush)
-        gex = GraphedExperts(ex, T, 8)
-        yg = gex(x, topi, topw).float()
-        graph_exact = bool(torch.equal(yg, y))
-        ms = _time_ms(lambda: gex(x, topi, topw), 20, flush)
+        yd = dfwd(x, topi, topw).float()
         md_eager = _time_ms(lambda: dfwd(x, topi, topw), 20, flush)
         try:  # the dense comparator gets the same launch-overhead treatment
             sx, si, sw = x.clone(), topi.clone(), topw.clone()
@@ -356,17 +350,40 @@ def forward_bench(wl: dict, fits: dict, dev: str, peaks: dict) -> dict:
             dense_graph = True
         except Exception:  # noqa: BLE001
             md, dense_graph = md_eager, False
+        row = {"tokens": T, "active_experts": int(torch.unique(topi).numel()), "dense_ms": md,
+               "dense_ms_eager": md_eager, "dense_cuda_graph": dense_graph,
+               "dense_bf16_tokens_per_s": T / (md / 1e3), "dense_bytes": int(torch.unique(topi).numel()) * 3 * H * I * 2}
+        # two decode variants: gather-dequant of every layer ("gather"), and
+        # per-token lookup tables for the sign-free layers whose tables fit
+        # ("lut", the reference's matmul_gather mode); identical results
+        y0 = None
+        for variant, mode in (("gather", "off"), ("lut", "on")):
+            ex.decode_lut = mode
+            y = ex(x, topi, topw).float()
+            if y0 is None:
+                y0 = y
+            ms_eager = _time_ms(lambda: ex(x, topi, topw), 20, flush)
+            gex = GraphedExperts(ex, T, 8)
+            yg = gex(x, topi, topw).float()
+            ms = _time_ms(lambda: gex(x, topi, topw), 20, flush)
+            del gex
+            row[variant] = {"ms": ms, "ms_eager": ms_eager, "tokens_per_s": T / (ms / 1e3),
+                            "graph_matches_eager": bool(torch.equal(yg, y)),
+                            "matches_gather": bool(torch.equal(y, y0)), "vs_dense": md / ms,
+                            "lut_layers": {m: ex._lut_layers(getattr(ex, m), T if m != "down" else T * 8, T * 8)
+                                           for m in ("gate", "up", "down")} if mode != "off" else None}
+        ex.decode_lut = "auto"
+        best = min(("gather", "lut"), key=lambda v: row[v]["ms"])
         nbytes = _decode_bytes(ex, topi)
-        n_act = int(torch.unique(topi).numel())
-        res["decode"].append({
-            "tokens": T, "active_experts": n_act, "tokens_per_s": T / (ms / 1e3), "ms": ms, "ms_eager": ms_eager,
-            "cuda_graph": True, "graph_matches_eager": graph_exact,
-            "dense_bf16_tokens_per_s": T / (md / 1e3), "dense_ms": md, "dense_ms_eager": md_eager,
-            "dense_cuda_graph": dense_graph, "cos_vs_dense": cos,
-            "algorithmic_bytes": nbytes, "achieved_gbs": nbytes / (ms / 1e3) / 1e9,
-            "frac_hbm": nbytes / (ms / 1e3) / 1e9 / peaks["hbm_gbs"],
-            "dense_bytes": n_act * 3 * H * I * 2,
-        })
+        row.update({"best": best, "ms": row[best]["ms"], "tokens_per_s": row[best]["tokens_per_s"],
+                    "cos_vs_dense": torch.nn.functional.cosine_similarity(y0.flatten(), yd.flatten(), dim=0).item(),
+                    "algorithmic_bytes": nbytes, "achieved_gbs": nbytes / (row[best]["ms"] / 1e3) / 1e9,
+                    "frac_hbm": nbytes / (row[best]["ms"] / 1e3) / 1e9 / peaks["hbm_gbs"]})
+        res["decode"].append(row)
+    faster = [r["tokens"] for r in res["decode"] if r["ms"] < r["dense_ms"]]
+    res["decode_crossover"] = {"faster_than_dense_at_tokens": faster,
+                               "lut_faster_than_gather_at_tokens": [r["tokens"] for r in res["decode"]
+                                                                    if r["lut"]["ms"] < r["gather"]["ms"]]}
     T = 16384
     x = torch.randn(T, H, generator=gen, device=dev).to(torch.bfloat16)
     topi, topw = _route(T, E, 8, gen, dev, zipf=1.1)

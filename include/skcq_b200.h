@@ -50,6 +50,19 @@ extern "C" {
 int skcq_last_error(char* buf, size_t len);
 /* ABI version of this library (bumped on any signature change). */
 int skcq_abi_version(void);
+
+/* Device error codes of skcq_poll_device_error whose cause is a bounded wait
+ * that ran out (a pipeline partner that did not arrive within ~2 s): a
+ * tensor-core assignment wait (11-17), a prefill GEMM wait (51-54) or the
+ * self-test below. The kernel returned; the context stays usable. */
+#define SKCQ_DEVICE_CODE_SELFTEST 90
+
+/* Self-test of that path: launches one thread that waits on a barrier nothing
+ * arrives on, for at most limit_clocks SM clocks (<= 4e9), through the same
+ * bounded wait the kernels use; it records SKCQ_DEVICE_CODE_SELFTEST and
+ * returns. A later skcq_poll_device_error reports SKCQ_ERR_DEVICE with that
+ * code and clears it. */
+int skcq_selftest_wait_timeout(long long limit_clocks, void* stream);
 /* Synchronises `stream`, then returns SKCQ_ERR_DEVICE (and clears the word) if
  * any kernel recorded a device-side failure (a bounded wait that gave up, an
  * inconsistent reseed selection), else SKCQ_OK. */
@@ -241,6 +254,11 @@ typedef struct skcq_codec_desc {
   const int8_t* signs;   /* int8 +-1 (n_rows, sign_ld) or NULL (SSVQ) */
   int sign_cols;         /* signed columns: min(in_dim, signs width) */
   int64_t sign_ld;
+  /* Optional bf16 (shared ? 1 : n_blocks, K, bs) copy of cent with each
+   * centroid's values contiguous (skcq_transpose_codebook), or NULL. When
+   * given, the decode reads it: one memory sector per gathered centroid
+   * instead of one per coordinate; the values are the same. */
+  const uint16_t* cent_t;
 } skcq_codec_desc;
 
 #define SKCQ_MAX_CODECS 8

@@ -395,6 +395,11 @@ def quantize_scales_int(scales: torch.Tensor, bits: int) -> tuple[torch.Tensor |
 _SCALE_CODES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2, torch.int8: 3, torch.int16: 4}
 
 
+def _lib_dtype(dt: torch.dtype) -> int:
+    """SKCQ_DTYPE_* of a float tensor dtype (f32 or bf16)."""
+    return {torch.float32: 0, torch.bfloat16: 1}[dt]
+
+
 @dataclass
 class CodecView:
     """Device tensors of one codebook of a composite, ready for the C ABI."""
@@ -411,6 +416,17 @@ class CodecView:
     rem: torch.Tensor | None = None  # bf16 (n_rows, rem) contiguous
     signs: torch.Tensor | None = None  # int8 (n_rows, >= sign_cols)
     sign_cols: int = 0
+    cent_t: torch.Tensor | None = None  # bf16 (n_cb, K, bs): centroid values contiguous
+
+    def transposed(self) -> torch.Tensor:
+        """(n_cb, K, bs) copy of ``cent`` (built once per view) for the decode's
+        one-sector centroid gathers."""
+        if self.cent_t is None:
+            n_cb = self.cent.shape[0]
+            self.cent_t = torch.empty(n_cb, self.K, self.bs, dtype=self.cent.dtype, device=self.cent.device)
+            call("skcq_transpose_codebook", ptr(self.cent), _lib_dtype(self.cent.dtype), n_cb, self.bs, self.K,
+                 ptr(self.cent_t), stream())
+        return self.cent_t
 
     def desc(self) -> _lib.CodecDesc:
         d = _lib.CodecDesc()
@@ -430,6 +446,8 @@ class CodecView:
             d.signs = ptr(self.signs)
             d.sign_cols = self.sign_cols
             d.sign_ld = self.signs.stride(0)
+        if self.cent_t is not None:
+            d.cent_t = ptr(self.cent_t)
         return d
 
 
@@ -439,6 +457,9 @@ def reconstruct(views: list[CodecView], n_rows: int, in_dim: int, raw: torch.Ten
     dev = views[0].cent.device
     if out is None:
         out = torch.empty(n_rows, in_dim, dtype=torch.float32, device=dev)
+    for v in views:
+        if v.cent.dtype == torch.bfloat16 and v.K > 1:
+            v.transposed()
     arr = (_lib.CodecDesc * len(views))(*[v.desc() for v in views])
     call("skcq_reconstruct", _lib.C.cast(arr, _lib.C.c_void_p), len(views), n_rows, in_dim,
          ptr(raw), raw.stride(0) if raw is not None else 0, ptr(out), out.stride(0), stream())

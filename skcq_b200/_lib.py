@@ -9,6 +9,7 @@ from __future__ import annotations
 
 import ctypes as C
 import os
+import re
 from pathlib import Path
 
 import torch
@@ -30,6 +31,7 @@ class CodecDesc(C.Structure):
         ("scales", P), ("scale_dtype", I), ("q_scale", F), ("scale_ld", L),
         ("rem", P), ("rem_cols", I),
         ("signs", P), ("sign_cols", I), ("sign_ld", L),
+        ("cent_t", P),
     ]
 
 
@@ -68,6 +70,7 @@ _SIGS: dict[str, list] = {
     "skcq_transpose_codebook": [P, I, I, I, I, P, P],
     "skcq_pack_sign_masks": [P, I, I, L, I, I, P, P],
     "skcq_lut_build": [P, P, I, L, I, P, P],
+    "skcq_selftest_wait_timeout": [C.c_longlong, P],
     "skcq_route_sort": [P, I, I, I, P, P, P, P, P, C.c_size_t, P],
     "skcq_route_sort_scratch_bytes": [I, I, I],
     "skcq_codebook_forward": [P, I, P, I, L, P, I, P, P, P, I, I, I, I, I, I, P, L, P],
@@ -122,7 +125,7 @@ _KERNELS_PER_CALL = {
     "skcq_row_zero_mask": 1, "skcq_spherical_scales": 1, "skcq_centroids_to_bf16": 1, "skcq_copy_remainder": 1,
     "skcq_ssvq_fold": 1, "skcq_quantize_centroids": 1, "skcq_quantize_scales": 3, "skcq_reconstruct": 1,
     "skcq_refit_scales": 1, "skcq_pack_indices16": 1, "skcq_transpose_codebook": 1, "skcq_pack_sign_masks": 1,
-    "skcq_lut_build": 1,
+    "skcq_lut_build": 1, "skcq_selftest_wait_timeout": 1,
     "skcq_route_sort": 1, "skcq_sum_splits": 1, "skcq_swiglu": 1, "skcq_combine": 1,
     "skcq_prefill_plan": 1, "skcq_prefill_pack": 1, "skcq_prefill_dequant": 1, "skcq_prefill_gemm": 1,
     "skcq_prefill_gemm_swiglu": 1,
@@ -175,4 +178,17 @@ def stream() -> int:
 
 
 def poll_device_error() -> None:
-    call("skcq_poll_device_error", stream())
+    """Raise if a kernel recorded a device-side error since the last poll:
+    ``DeviceTimeoutError`` when a bounded wait ran out (the job may be retried),
+    ``RuntimeError`` for a failed data check (a bug or invalid input)."""
+    from skcq_b200.errors import WAIT_TIMEOUT_CODES, DeviceTimeoutError
+
+    rc = load().skcq_poll_device_error(stream())
+    if rc == 0:
+        return
+    msg = last_error()
+    m = re.search(r"\(code (\d+)\)", msg)
+    code = int(m.group(1)) if m else -1
+    if rc == -3 and code in WAIT_TIMEOUT_CODES:
+        raise DeviceTimeoutError(f"skcq_poll_device_error: {msg}", code)
+    raise RuntimeError(f"skcq_poll_device_error failed ({rc}): {msg}")

@@ -477,12 +477,14 @@ class CodebookExperts(nn.Module):
     # bf16 batches with at least this many (token, slot) rows per expert on
     # average take the tensor-core prefill path
     prefill_min_rows: int = 32
-    # Decode lookup tables (the reference's matmul_gather mode): "off";
-    # "on" for every sign-free layer of the three projections; "auto" for the
-    # sign-free layers whose table build (one block dot per token and
-    # centroid) does less work than the gathers it replaces (one per routed
-    # row and output) and whose table stays below lut_max_bytes.
-    decode_lut: str = "auto"
+    # Decode lookup tables (the reference's matmul_gather mode): "off" (the
+    # default: on B200 the gather path measured faster at every batch of 1 to
+    # 64 tokens but 2 on the benchmark layer); "on" for every sign-free layer
+    # of the three projections whose table stays below lut_max_bytes; "auto"
+    # for those whose table build (one block dot per token and centroid) also
+    # does less work than the gathers it replaces (one per routed row and
+    # output). All three give the same bits.
+    decode_lut: str = "off"
     lut_max_bytes: int = 64 << 20
 
     def __init__(self, gate: CodebookModule, up: CodebookModule, down: CodebookModule, num_experts: int,

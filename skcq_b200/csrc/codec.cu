@@ -205,7 +205,8 @@ __device__ __forceinline__ float codec_value(const skcq_codec_desc& d, int64_t r
   if (col < cov) {
     const int b = col / d.bs, j = col - b * d.bs;
     const int64_t idx = d.idxs[(int64_t)b * d.idx_ld + r];
-    v = bf16_to_f32(d.cent[((int64_t)(d.shared ? 0 : b) * d.bs + j) * d.K + idx]);
+    const int64_t cb = d.shared ? 0 : b;
+    v = bf16_to_f32(d.cent_t ? d.cent_t[(cb * d.K + idx) * d.bs + j] : d.cent[(cb * d.bs + j) * d.K + idx]);
     if (d.kind == 0) v = __fmul_rn(load_scale(d, r, b), v);
   } else {
     v = d.rem ? bf16_to_f32(d.rem[r * d.rem_cols + (col - cov)]) : 0.f;

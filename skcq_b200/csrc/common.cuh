@@ -156,19 +156,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // an error. Every spin in these kernels goes through this, so a lost arrival
 // turns into an error status instead of a hung GPU. try_wait itself suspends
 // the thread in hardware until the phase flips or a short timeout passes.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity, int* err, int code,
+                                                long long limit_clocks) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 255) == 0) {
       if (*(volatile int*)err) return false;
-      if (clock64() - t0 > 4000000000ll) break;
+      if (clock64() - t0 > limit_clocks) break;
       if (i > 4096) __nanosleep(64);
     }
   }
   atomicCAS(err, 0, code);
   return false;
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+  return mbar_wait_limit(bar, parity, err, code, 4000000000ll);
 }
 
 // 1-D bulk copy global -> shared, completion counted on `bar` in bytes.

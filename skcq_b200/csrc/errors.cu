@@ -73,3 +73,24 @@ extern "C" int skcq_poll_device_error(void* stream) {
   }
   return SKCQ_OK;
 }
+
+// Self-test of the bounded device waits: one thread waits on a shared-memory
+// mbarrier that nothing arrives on, with the given clock limit, through the
+// same wait the kernels use. The wait runs out, records SKCQ_DEVICE_CODE_SELFTEST
+// in the device error word and the kernel returns; nothing faults or hangs.
+__global__ void selftest_wait_kernel(long long limit_clocks, int* err) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x != 0) return;
+  skcq::mbar_init(&bar, 1);
+  skcq::fence_barrier_init();
+  skcq::mbar_wait_limit(&bar, 0, err, SKCQ_DEVICE_CODE_SELFTEST, limit_clocks);
+}
+
+extern "C" int skcq_selftest_wait_timeout(long long limit_clocks, void* stream) {
+  SKCQ_REQUIRE(limit_clocks > 0 && limit_clocks <= 4000000000ll, SKCQ_ERR_INVALID,
+               "selftest_wait_timeout: limit %lld clocks outside (0, 4e9]", limit_clocks);
+  int* err = skcq::device_error_word();
+  if (err == nullptr) return skcq::set_error(SKCQ_ERR_CUDA, "selftest_wait_timeout: no device error word");
+  selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(limit_clocks, err);
+  return skcq::check_launch("selftest_wait_timeout");
+}

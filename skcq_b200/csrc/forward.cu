@@ -500,28 +500,32 @@ __global__ void __launch_bounds__(FW_THREADS) fwd_layer_kernel(FwdArgs a, skcq_f
 constexpr int LUT_THREADS = 256;
 
 // lut[(b K + k) T + t] = <x_b(t), C_b[k]>. One CTA per (block, 256 centroids);
-// the block's columns of every row of x are staged in shared memory.
+// the block's columns of x are staged in shared memory, `chunk` rows at a time.
 template <int BS, typename T>
 __global__ void __launch_bounds__(LUT_THREADS) lut_build_kernel(skcq_fwd_layer L, const void* __restrict__ x,
-                                                                int x_dtype, int64_t x_ld, int n_tok,
+                                                                int x_dtype, int64_t x_ld, int n_tok, int chunk,
                                                                 float* __restrict__ lut) {
-  extern __shared__ float xb[];  // [n_tok][BS]
+  extern __shared__ float xb[];  // [chunk][BS]
   const int b = blockIdx.y;
-  for (int i = threadIdx.x; i < n_tok * BS; i += LUT_THREADS) {
-    const int t = i / BS, j = i - t * BS;
-    xb[i] = ld_any(x, (int64_t)t * x_ld + (int64_t)b * BS + j, x_dtype);
-  }
-  __syncthreads();
   const int k = blockIdx.x * LUT_THREADS + threadIdx.x;
-  if (k >= L.K) return;
   float w[BS];
-  load_centroid<BS, T>(static_cast<const T*>(L.table) + ((int64_t)b * L.K + k) * BS, w);
+  if (k < L.K) load_centroid<BS, T>(static_cast<const T*>(L.table) + ((int64_t)b * L.K + k) * BS, w);
   float* dst = lut + ((int64_t)b * L.K + k) * n_tok;
-  for (int t = 0; t < n_tok; ++t) {
-    float d = 0.f;
+  for (int t0 = 0; t0 < n_tok; t0 += chunk) {
+    const int nt = min(chunk, n_tok - t0);
+    __syncthreads();
+    for (int i = threadIdx.x; i < nt * BS; i += LUT_THREADS) {
+      const int t = i / BS, j = i - t * BS;
+      xb[i] = ld_any(x, (int64_t)(t0 + t) * x_ld + (int64_t)b * BS + j, x_dtype);
+    }
+    __syncthreads();
+    if (k >= L.K) continue;
+    for (int t = 0; t < nt; ++t) {
+      float d = 0.f;
 #pragma unroll
-    for (int j = 0; j < BS; ++j) d = __fmaf_rn(xb[t * BS + j], w[j], d);
-    dst[t] = d;
+      for (int j = 0; j < BS; ++j) d = __fmaf_rn(xb[t * BS + j], w[j], d);
+      dst[t0 + t] = d;
+    }
   }
 }
 
@@ -931,9 +935,8 @@ extern "C" int skcq_lut_build(const skcq_fwd_layer* layer, const void* x, int x_
   SKCQ_REQUIRE(x_dtype == SKCQ_DTYPE_F32 || x_dtype == SKCQ_DTYPE_BF16, SKCQ_ERR_INVALID, "lut_build: x dtype %d",
                x_dtype);
   SKCQ_REQUIRE(T >= 1, SKCQ_ERR_INVALID, "lut_build: %d rows", T);
-  const size_t smem = (size_t)T * L.bs * sizeof(float);
-  SKCQ_REQUIRE(smem <= 96 * 1024, SKCQ_ERR_INVALID, "lut_build: %d rows of block size %d exceed shared memory", T,
-               L.bs);
+  const int chunk = T < 1024 ? T : 1024;  // rows staged at a time (<= 128 KB at bs 32)
+  const size_t smem = (size_t)chunk * L.bs * sizeof(float);
   SKCQ_REQUIRE(L.n_blocks <= 65535, SKCQ_ERR_INVALID, "lut_build: %d blocks", L.n_blocks);
   if (L.n_blocks == 0) return SKCQ_OK;
   const dim3 grid((unsigned)ceil_div(L.K, LUT_THREADS), (unsigned)L.n_blocks);
@@ -943,12 +946,12 @@ extern "C" int skcq_lut_build(const skcq_fwd_layer* layer, const void* x, int x_
   case BSV:                                                                                                  \
     if (bf) {                                                                                                \
       cudaFuncSetAttribute(lut_build_kernel<BSV, __nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                           96 * 1024);                                                                       \
-      lut_build_kernel<BSV, __nv_bfloat16><<<grid, LUT_THREADS, smem, s>>>(L, x, x_dtype, x_ld, T, lut);     \
+                           160 * 1024);                                                                      \
+      lut_build_kernel<BSV, __nv_bfloat16><<<grid, LUT_THREADS, smem, s>>>(L, x, x_dtype, x_ld, T, chunk, lut); \
     } else {                                                                                                 \
       cudaFuncSetAttribute(lut_build_kernel<BSV, float>, cudaFuncAttributeMaxDynamicSharedMemorySize,         \
-                           96 * 1024);                                                                       \
-      lut_build_kernel<BSV, float><<<grid, LUT_THREADS, smem, s>>>(L, x, x_dtype, x_ld, T, lut);             \
+                           160 * 1024);                                                                      \
+      lut_build_kernel<BSV, float><<<grid, LUT_THREADS, smem, s>>>(L, x, x_dtype, x_ld, T, chunk, lut);      \
     }                                                                                                        \
     break;
   switch (L.bs) {

@@ -17,13 +17,17 @@ gate, up and down, via ``build_aqlm_codebook``), with no communication.
 from __future__ import annotations
 
 import json
+import logging
 from pathlib import Path
 
 import torch
 from safetensors import safe_open
 
 from skcq_b200.config import CodebookParams, LayerOverride, build_aqlm_codebook
+from skcq_b200.errors import InfrastructureError
 from skcq_b200.quantize import layer_params
+
+logger = logging.getLogger(__name__)
 
 LayerShardMap = dict[int, dict[str, str]]
 ProjectionRows = dict[str, torch.Tensor]
@@ -104,11 +108,17 @@ def farm_assignment(num_layers: int, world: int, rank: int) -> list[int]:
 def farm_layers(model_dir: Path | str, params: CodebookParams, num_layers: int, num_experts: int,
                 hidden_size: int, intermediate_size: int, *, rank: int = 0, world: int = 1,
                 layer_overrides: dict[int, LayerOverride] | None = None, device: str | torch.device = "cuda",
-                ) -> dict[int, dict[str, tuple]]:
+                retries: int = 2) -> dict[int, dict[str, tuple]]:
     """Fit this rank's layers: {layer: {proj: (AQLMCodebook, AQLMCWR)}}.
 
     Rows are read straight onto ``device``; each projection is fitted as in
-    quantize.py:63-101 (k and n_blocks per projection, per-layer overrides)."""
+    quantize.py:63-101 (k and n_blocks per projection, per-layer overrides).
+    A (layer, projection) job that fails with an ``InfrastructureError`` (a
+    device wait that ran out) is fitted again from a fresh codebook, up to
+    ``retries`` more times, as the reference's workers report such a job back
+    for another attempt (worker.py:256-258); after that the error propagates
+    with the job in its context. Bugs (``RuntimeError``, ``ValueError``) are
+    never retried."""
     shards = build_layer_shard_map(model_dir)
     out: dict[int, dict[str, tuple]] = {}
     for layer in farm_assignment(num_layers, world, rank):
@@ -121,9 +131,20 @@ def farm_layers(model_dir: Path | str, params: CodebookParams, num_layers: int, 
         for name in ("gate", "up", "down"):
             k, n_blocks, out_dim = ks[name]
             w = rows[name]
-            aqlm = build_aqlm_codebook(lp, k=k, n_blocks=n_blocks, n_codebooks=lp.n_codebooks, in_dim=w.shape[1],
-                                       out_dim=out_dim, num_experts=num_experts, name=f"L{layer}.{name}")
-            result[name] = (aqlm, aqlm.fit(w))
+            for attempt in range(retries + 1):
+                aqlm = build_aqlm_codebook(lp, k=k, n_blocks=n_blocks, n_codebooks=lp.n_codebooks,
+                                           in_dim=w.shape[1], out_dim=out_dim, num_experts=num_experts,
+                                           name=f"L{layer}.{name}")
+                try:
+                    result[name] = (aqlm, aqlm.fit(w))
+                    break
+                except InfrastructureError as e:
+                    if attempt == retries:
+                        raise InfrastructureError(f"layer {layer} {name}: {e}",
+                                                  context={"layer": layer, "projection": name,
+                                                           "attempts": attempt + 1, **e.context}) from e
+                    logger.warning("layer %d %s: %s; fitting again (attempt %d of %d)", layer, name, e,
+                                   attempt + 2, retries + 1)
         out[layer] = result
         del rows
     return out

@@ -513,3 +513,62 @@ def test_prefill_persistent_gemm_many_tiles():
     cos = torch.nn.functional.cosine_similarity(y_tc.flatten(), y_ref.flatten(), dim=0).item()
     assert cos >= 0.9999, cos
     assert (y_tc - y_ref).abs().max().item() <= 1e-2 * y_ref.abs().max().item()
+
+
+@pytest.mark.parametrize("T", [1, 3, 8, 24])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_decode_lookup_table_is_bit_identical(T, dtype):
+    """The lookup-table decode (codebook_experts.py:57-60, matmul_gather) reads
+    per-token block dots built with the same fused multiply-adds the gather
+    path forms, so the MoE block's output is the same bits with the tables on
+    every sign-free layer, on none, or where the automatic policy puts them;
+    the last codebook carries a 13-column remainder."""
+    from skcq_b200.codebook_experts import CodebookExperts
+
+    E, H, I, k = 8, 2061, 96, 4
+    specs = [(8, 256, True), (16, 512, False), (4, 1024, False)]
+    ex = CodebookExperts(_random_module(E, I, H, specs, seed=11, dtype=dtype),
+                         _random_module(E, I, H, specs, seed=12, dtype=dtype),
+                         _random_module(E, H, I, [(8, 256, True), (4, 512, False)], seed=13, dtype=dtype), E,
+                         torch.nn.functional.silu)
+    g = torch.Generator().manual_seed(T)
+    x = torch.randn(T, H, generator=g).to(dtype).cuda()
+    topi = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)]).cuda()
+    topw = torch.softmax(torch.randn(T, k, generator=g), -1).cuda()
+    outs = {}
+    for mode in ("off", "on", "auto"):
+        ex.decode_lut = mode
+        outs[mode] = ex(x, topi, topw)
+    assert torch.equal(outs["on"], outs["off"])
+    assert torch.equal(outs["auto"], outs["off"])
+    ex.decode_lut = "on"
+    assert ex._lut_layers(ex.gate, T, T * k) == [True, True, True]
+
+
+def test_decode_lookup_table_skips_signed_layers():
+    """A layer with SSVQ signs cannot use a table of plain dots (the reference
+    switches such layers to gather_matmul, codebook_experts.py:50-51): the
+    policy leaves it out, and the C ABI rejects a signed layer that carries
+    one."""
+    from skcq_b200 import _lib
+    from skcq_b200._lib import ptr, stream
+    from skcq_b200.codebook_experts import CodebookExperts, FwdLayer
+
+    E, H, I = 4, 64, 32
+    gate = _random_module(E, I, H, [(8, 64, True)], seed=21)
+    gate.layers[0].signs = torch.where(torch.rand(E, I, H, generator=torch.Generator().manual_seed(2)) < 0.5, -1,
+                                       1).to(torch.int8).cuda()
+    ex = CodebookExperts(gate, _random_module(E, I, H, [(8, 64, True)], seed=22),
+                         _random_module(E, H, I, [(8, 64, True)], seed=23), E, torch.nn.functional.silu)
+    ex.decode_lut = "on"
+    assert ex._lut_layers(ex.gate, 2, 8) is None
+    d = gate.layers[0].descriptor(torch.device("cuda"), primary=True)
+    lut = torch.zeros(8 * 64 * 2, device="cuda")
+    d.lut, d.lut_tokens = ptr(lut), 2
+    arr = (FwdLayer * 1)(d)
+    x = torch.randn(2, H, device="cuda")
+    seg = torch.tensor([0, 2], dtype=torch.int32, device="cuda")
+    part = torch.empty(1, 2, I, device="cuda")
+    rc = _lib.load().skcq_codebook_forward(_lib.C.cast(arr, _lib.C.c_void_p), 1, ptr(x), 0, x.stride(0), None, 2,
+                                           ptr(seg), None, None, 1, 1, H, I, 1, 2, ptr(part), 2, stream())
+    assert rc != 0 and "signs" in _lib.last_error()

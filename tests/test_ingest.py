@@ -77,3 +77,82 @@ def test_farm_fits_tiny_model(tmp_path):
     w = weights[1][1].reshape(-1, I).float()
     rel = (aqlm.reconstruct(cwr).cpu() - w).norm() / w.norm()
     assert rel < 0.6
+
+
+class _FlakyCodebook:
+    """Stand-in for an AQLM codebook whose fit fails with a device wait that
+    ran out on the first ``fail`` attempts of each job (host-side injection:
+    nothing runs on a GPU)."""
+
+    attempts: dict[str, int] = {}
+    fail = 1
+
+    def __init__(self, name: str) -> None:
+        self.name = name
+
+    def fit(self, w):
+        from skcq_b200.errors import DeviceTimeoutError
+
+        n = _FlakyCodebook.attempts.get(self.name, 0) + 1
+        _FlakyCodebook.attempts[self.name] = n
+        if n <= _FlakyCodebook.fail:
+            raise DeviceTimeoutError(f"{self.name}: device-side check failed (code 15)", 15)
+        return ("cwr", self.name, n)
+
+
+def _flaky_builder(*args, name="", **kw):
+    return _FlakyCodebook(name)
+
+
+def test_farm_retries_a_job_after_a_device_timeout(tmp_path, monkeypatch):
+    """A (layer, projection) job whose fit raises DeviceTimeoutError is fitted
+    again from a fresh codebook and the farm completes (worker.py:256-258
+    reports such a job for another attempt)."""
+    import skcq_b200.ingest as ingest
+    from skcq_b200.config import CodebookParams
+
+    d, _ = _model_dir(tmp_path)
+    monkeypatch.setattr(ingest, "build_aqlm_codebook", _flaky_builder)
+    _FlakyCodebook.attempts, _FlakyCodebook.fail = {}, 1
+    res = farm_layers(d, CodebookParams(), L, E, H, I, rank=0, world=2, device="cpu", retries=2)
+    assert sorted(res) == [0, 2]
+    for layer in (0, 2):
+        for proj in ("gate", "up", "down"):
+            assert res[layer][proj][1] == ("cwr", f"L{layer}.{proj}", 2)
+    assert all(n == 2 for n in _FlakyCodebook.attempts.values())
+
+
+def test_farm_gives_up_after_the_retries_with_the_job_in_context(tmp_path, monkeypatch):
+    import skcq_b200.ingest as ingest
+    from skcq_b200.config import CodebookParams
+    from skcq_b200.errors import InfrastructureError
+
+    d, _ = _model_dir(tmp_path)
+    monkeypatch.setattr(ingest, "build_aqlm_codebook", _flaky_builder)
+    _FlakyCodebook.attempts, _FlakyCodebook.fail = {}, 5
+    with pytest.raises(InfrastructureError) as ei:
+        farm_layers(d, CodebookParams(), L, E, H, I, rank=0, world=1, device="cpu", retries=2)
+    assert ei.value.context["layer"] == 0 and ei.value.context["projection"] == "gate"
+    assert ei.value.context["attempts"] == 3 and ei.value.context["device_code"] == 15
+    assert _FlakyCodebook.attempts == {"L0.gate": 3}
+
+
+def test_farm_does_not_retry_bugs(tmp_path, monkeypatch):
+    import skcq_b200.ingest as ingest
+    from skcq_b200.config import CodebookParams
+
+    calls = []
+
+    class Broken:
+        def __init__(self, name):
+            self.name = name
+
+        def fit(self, w):
+            calls.append(self.name)
+            raise RuntimeError("a bug")
+
+    d, _ = _model_dir(tmp_path)
+    monkeypatch.setattr(ingest, "build_aqlm_codebook", lambda *a, name="", **k: Broken(name))
+    with pytest.raises(RuntimeError, match="a bug"):
+        farm_layers(d, CodebookParams(), L, E, H, I, rank=0, world=1, device="cpu", retries=3)
+    assert calls == ["L0.gate"]
