@@ -52,16 +52,18 @@ __global__ void pack_idx16_kernel(const int64_t* __restrict__ src, int64_t n, in
   }
 }
 
-// table[b][k][j] = cb[b][j][k] (element size esz bytes: 2 or 4)
+// table[b][k][j] = cb[b][j][k] (element size 2 or 4 bytes). One thread per
+// centroid (b, k): its bs reads are each part of a warp-wide read of 32
+// consecutive centroids of one coordinate row, and its bs values are written
+// as one contiguous run.
 template <typename T>
 __global__ void transpose_cb_kernel(const T* __restrict__ cb, int64_t nb, int bs, int64_t K, T* __restrict__ table) {
-  const int64_t total = nb * bs * K;
+  const int64_t total = nb * K;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    // i indexes the output: (b, k, j)
-    const int j = (int)(i % bs);
-    const int64_t bk = i / bs;
-    const int64_t k = bk % K, b = bk / K;
-    table[i] = cb[(b * bs + j) * K + k];
+    const int64_t b = i / K, k = i - b * K;
+    const T* src = cb + b * bs * K + k;
+    T* dst = table + i * bs;
+    for (int j = 0; j < bs; ++j) dst[j] = src[(int64_t)j * K];
   }
 }
 
@@ -775,7 +777,7 @@ extern "C" int skcq_transpose_codebook(const void* cb, int dtype, int n_blocks, 
   SKCQ_REQUIRE(dtype == SKCQ_DTYPE_F32 || dtype == SKCQ_DTYPE_BF16, SKCQ_ERR_INVALID,
                "transpose_codebook: dtype %d is not f32 or bf16", dtype);
   SKCQ_REQUIRE(n_blocks >= 0 && bs > 0 && K > 0, SKCQ_ERR_INVALID, "transpose_codebook: bad sizes");
-  const int64_t total = (int64_t)n_blocks * bs * K;
+  const int64_t total = (int64_t)n_blocks * K;
   if (total == 0) return SKCQ_OK;
   cudaStream_t s = (cudaStream_t)stream;
   if (dtype == SKCQ_DTYPE_BF16)

@@ -141,6 +141,9 @@ def test_kmeans_experiment_matches_reference(name, monkeypatch):
 
 
 CODEC_CASES = ["base", "single", "ssvq", "noncomm", "asym", "shared", "int8cb", "skipz", "ressign", "rem13"]
+# cases of test_aqlm_fit_matches_reference that passed through a near-tie and
+# were held only to the quality tolerance (reported by the test after them)
+LOOSE_CASES: list[str] = []
 
 
 def _product_aqlm(name):
@@ -191,10 +194,20 @@ def test_aqlm_fit_matches_reference(name, monkeypatch):
     e_ref = np.linalg.norm(wn - g["recon"]) / np.linalg.norm(wn)
     e_gpu = np.linalg.norm(wn - recon) / np.linalg.norm(wn)
     if not all(lg.min_margin > TIE for lg in logs):
+        # the reference's own trajectory passes a near-tie: its result depends
+        # on rounding order, so only the quality is compared
+        LOOSE_CASES.append(name)
         assert abs(e_gpu - e_ref) <= 0.15 * e_ref
         return
     assert abs(e_gpu - e_ref) <= 1e-3 * e_ref + 1e-7
     assert rel_err(recon, g["recon"]) < 2e-3
+
+
+def test_loose_branch_count():
+    """At most two of the ten reference configurations pass a near-tie (the
+    oracle's logs decide, not the GPU result); the rest were held to 1e-3."""
+    print(f"codec cases on the near-tie branch: {len(LOOSE_CASES)} of {len(CODEC_CASES)} {sorted(LOOSE_CASES)}")
+    assert len(LOOSE_CASES) <= 2, sorted(LOOSE_CASES)
 
 
 def test_config1_matches_reference(monkeypatch):
