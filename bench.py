@@ -458,44 +458,84 @@ def measured_peaks() -> tuple[dict, str]:
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
-def ep_forward_bench(wl: dict, world: int, rank: int, dev: str, iters: int = 3) -> dict:
-    """Config-5 prefill expert-parallel over the ranks: 16384 tokens in all
-    (16384 / world per rank), top-8 with Zipf(1.1) expert load, experts split
-    across ranks, NCCL all-to-all dispatch and return. The modules carry the
-    layer's codebook shapes with random centroids and uniform indices (built
-    identically on every rank); max over ranks of the device time."""
+def ep_forward_bench(wl: dict, fits: dict, world: int, rank: int, dev: str, iters: int = 5) -> dict:
+    """Prefill of 16384 tokens (top-8, Zipf(1.1) expert load) expert-parallel
+    over the ranks, 16384 / world tokens per rank, on the fitted layer: rank 0's
+    gate / up / down modules, broadcast to every rank. Rows travel over peer
+    memory (skcq_ep_dispatch / skcq_ep_return). Reported: max over ranks of the
+    device time of one forward, of its phases, and the single-GPU forward of
+    the whole batch on the same modules for comparison."""
+    import torch.distributed as dist
+
+    from skcq_b200.codebook_experts import CodebookExperts, CodebookModule
     from skcq_b200.expert_parallel import ExpertParallelExperts
-    from skcq_b200.kernel_bench import _random_module
 
     E, H, I = wl["experts"], wl["hidden"], wl["inter"]
-    g = torch.Generator(device=dev).manual_seed(777)
-    mods = [_random_module(E, I, H, g), _random_module(E, I, H, g), _random_module(E, H, I, g)]
-    ep = ExpertParallelExperts(*mods, E, torch.nn.functional.silu)
+    outs = {"gate": I, "up": I, "down": H}
+    mods = {}
+    for name, (aqlm, cwr) in fits.items():
+        m = CodebookModule.from_cwr(aqlm, cwr, out_dim=outs[name]).to(device=dev, dtype=torch.bfloat16)
+        with torch.no_grad():  # rank 0's layer on every rank: codebooks and scales too
+            for t in list(m.parameters()) + list(m.buffers()):
+                dist.broadcast(t.data, src=0)
+        mods[name] = m
     T_all = 16384
     T = T_all // world
-    gt = torch.Generator(device=dev).manual_seed(1000 + rank)
-    ranks = torch.randperm(E, generator=torch.Generator(device=dev).manual_seed(4321), device=dev).float() + 1
-    u = torch.rand(T, E, generator=gt, device=dev).clamp_(1e-20, 1)
-    topw, topi = torch.topk(torch.softmax(-1.1 * torch.log(ranks)[None] - torch.log(-torch.log(u)), -1), 8, dim=-1)
-    x = torch.randn(T, H, generator=gt, device=dev).to(torch.bfloat16)
-    for _ in range(2):
-        ep(x, topi, topw)
+    gen = torch.Generator(device=dev).manual_seed(4321)  # the same batch on every rank
+    x_all = torch.randn(T_all, H, generator=gen, device=dev).to(torch.bfloat16)
+    topi_all, topw_all = _route(T_all, E, 8, gen, dev, zipf=1.1)
+    sl = slice(rank * T, (rank + 1) * T)
+    x, topi, topw = x_all[sl].contiguous(), topi_all[sl].contiguous(), topw_all[sl].contiguous()
+    ep = ExpertParallelExperts(mods["gate"], mods["up"], mods["down"], E, torch.nn.functional.silu,
+                               max_tokens=T, top_k=8)
+    ep.check_errors = False
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    for _ in range(3):
+        y = ep(x, topi, topw)
     torch.cuda.synchronize()
-    ts = []
+    ts, phases = [], []
+    ep.record_phases = True
     for _ in range(iters):
+        flush.zero_()
+        torch.cuda.synchronize()
         barrier(world)
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
-        ep(x, topi, topw)
+        y = ep(x, topi, topw)
         b.record()
         torch.cuda.synchronize()
         ts.append(max_over_ranks(a.elapsed_time(b), world))
+        ev = ep.last_phases
+        phases.append([max_over_ranks(ev[i].elapsed_time(ev[i + 1]), world) for i in range(len(ev) - 1)])
+    ep.record_phases = False
     ms = statistics.median(ts)
-    del ep, mods
+    ph = [statistics.median(p[i] for p in phases) for i in range(len(phases[0]))]
+    # the single-GPU forward of the whole batch on the same modules
+    single = CodebookExperts(mods["gate"], mods["up"], mods["down"], E, torch.nn.functional.silu)
+    single.check_errors = False
+    y_one = single(x_all, topi_all, topw_all)
+    ms_one = _time_ms(lambda: single(x_all, topi_all, topw_all), 3, flush)
+    ref = y_one[sl].float()
+    cos = torch.nn.functional.cosine_similarity(y.float().flatten(), ref.flatten(), dim=0).item()
+    err = ((y.float() - ref).abs().max() / ref.abs().max()).item()
+    from skcq_b200 import _lib
+
+    _lib.poll_device_error()
+    owner = torch.bucketize(topi, torch.tensor([b[0] for b in ep.bounds[1:]], device=dev), right=True)
+    rows_sent = sum(int((owner == d).any(1).sum()) for d in range(world))
+    ep.close()
+    del ep, single, mods
     torch.cuda.empty_cache()
     return {"tokens": T_all, "tokens_per_rank": T, "experts_per_rank": E // world, "ms": ms,
-            "tokens_per_s": T_all / (ms / 1e3), "dispatch": "NCCL all_to_all_single (rows bf16, ids, counts)",
-            "codebooks": "random centroids, uniform indices, config-2 shapes"}
+            "tokens_per_s": T_all / (ms / 1e3), "single_gpu_ms": ms_one, "speedup_vs_single_gpu": ms_one / ms,
+            "phases_ms": {"dispatch_and_barrier": ph[0], "local_experts": ph[1], "return_and_barrier": ph[2],
+                          "gather": ph[3]},
+            "rows_sent_per_rank": rows_sent, "pairs_per_rank": T * 8,
+            "cos_vs_single_gpu": max_over_ranks(-cos, world) * -1.0,
+            "max_err_vs_single_gpu": max_over_ranks(err, world),
+            "transport": "peer-memory stores over NVLink (CUDA IPC), one row per (token, destination rank); "
+                         "one-element NCCL all-reduce as the phase barrier",
+            "codebooks": "the fitted layer (rank 0's), bf16"}
 
 
 # ---------------------------------------------------------------------------
@@ -759,14 +799,13 @@ def main() -> None:
 
     peaks, peak_kind = measured_peaks()
     fwd = None
+    fwd_ep = None
+    if not args.no_forward and world > 1 and fits and not rows_mode:
+        torch.cuda.empty_cache()
+        fwd_ep = ep_forward_bench(wl, fits, world, rank, dev)
     if not args.no_forward and not args.no_e2e and fits and not rows_mode:
         fwd = forward_bench(wl, fits, dev, peaks)
-        fits.clear()
-    fwd_ep = None
-    if not args.no_forward and world > 1:
-        fits.clear()
-        torch.cuda.empty_cache()
-        fwd_ep = ep_forward_bench(wl, world, rank, dev)
+    fits.clear()
     a = ksum.get("assign", {"ms": 0.0, "work": 0.0, "launches": 0, "padded": 0.0})
     achieved = a["work"] / (a["ms"] / 1e3) / 1e12 if a["ms"] > 0 else 0.0
     issued = a["padded"] / (a["ms"] / 1e3) / 1e12 if a["ms"] > 0 else 0.0

@@ -336,9 +336,13 @@ int skcq_pack_sign_masks(const int8_t* signs, int E, int out, int64_t sign_ld, i
  * seg[e+1] is expert e's run (seg has n_experts + 1 entries); row_of_pair[p]
  * is the inverse permutation; active[0] is the number of experts with rows and
  * active[1..] their ids ascending (n_experts + 1 entries). An expert id outside
- * [0, n_experts) sets the device error (the reference's one_hot raises). */
+ * [0, n_experts) sets the device error (the reference's one_hot raises),
+ * except that with skip_negative != 0 a negative id marks a slot that is not
+ * routed here (expert-parallel receive rows): such pairs sort after every
+ * expert's run and are never computed. */
 int skcq_route_sort(const int64_t* topk, int T, int k, int n_experts, int32_t* perm, int32_t* seg,
-                    int32_t* row_of_pair, int32_t* active, void* scratch, size_t scratch_bytes, void* stream);
+                    int32_t* row_of_pair, int32_t* active, void* scratch, size_t scratch_bytes, int skip_negative,
+                    void* stream);
 
 /* Scratch bytes with which skcq_route_sort spreads a large batch over many
  * CTAs (0: the one-CTA sort is used; it also runs when scratch is NULL or
@@ -371,7 +375,8 @@ int skcq_swiglu(const float* gate, const float* up, int n_split, int64_t n, floa
 
 /* out[t] = sum over the token's k slots, in ascending (expert, kpos) order, of
  * (sum_s part[s][row_of_pair[kpos * T + t]]) * weights[t][kpos]
- * (codebook_experts.py:476-480). part, weights and out f32 | bf16. */
+ * (codebook_experts.py:476-480); slots with a negative expert id are skipped.
+ * part, weights and out f32 | bf16. */
 int skcq_combine(const void* part, int part_dtype, int n_split, int64_t P, const int32_t* row_of_pair,
                  const int64_t* topk, const void* weights, int w_dtype, int T, int k, int H, void* out, int out_dtype,
                  void* stream);
@@ -422,6 +427,68 @@ int skcq_prefill_gemm(const void* A, const void* W, const int32_t* tiles, int ma
  * codebook_experts.py:427-433 fused into the epilogue). */
 int skcq_prefill_gemm_swiglu(const void* A, const void* W_gate_up, const int32_t* tiles, int max_tiles, int in_dim,
                              int inter_dim, void* A_out, void* stream);
+
+/* ---- expert-parallel exchange over peer memory -------------------------------
+ * CodebookExperts.forward (codebook_experts.py:454-481) with experts placed
+ * across the GPUs of one node, one process per GPU. Rank r owns experts
+ * [bounds[r], bounds[r + 1]) (bounds: world + 1 host ints, 0 .. n_experts).
+ * Every rank allocates one exchange buffer laid out by skcq_ep_layout for the
+ * same (world, capacity, top_k_cap, hidden) and maps the others' buffers
+ * (skcq_ep_alloc / skcq_ep_open); `peers` is the host array of the world
+ * buffers' addresses in this process (this rank's own at index rank).
+ * capacity bounds the tokens any rank passes to one forward. Stores into a
+ * peer's buffer are plain stores over NVLink; the caller orders the phases
+ * across ranks with a stream-ordered barrier (a one-element all-reduce) after
+ * skcq_ep_dispatch and after skcq_ep_return. */
+#define SKCQ_EP_MAX_RANKS 8
+
+/* Byte offsets in an exchange buffer: [0] token rows [world][capacity][hidden]
+ * (4-byte slots), [1] slot ids and [2] slot weights [world][capacity][top_k_cap],
+ * [3] row counts [8], [4] returned sums [world][capacity][hidden] (4-byte
+ * slots), [5] total bytes. */
+int skcq_ep_layout(int world, int capacity, int top_k_cap, int hidden, int64_t* offsets);
+
+/* cudaMalloc'd, zeroed exchange buffer and its CUDA IPC handle (64 bytes). */
+int skcq_ep_alloc(size_t bytes, void** ptr, void* ipc_handle);
+/* Map another process's buffer (peer access enabled on first use). */
+int skcq_ep_open(const void* ipc_handle, void** ptr);
+int skcq_ep_close(void* ptr);
+int skcq_ep_free(void* ptr);
+
+/* Send this rank's T tokens: x (T, hidden) f32 | bf16 with row stride x_ld,
+ * topk (T, k) int64 global expert ids, weights (T, k) f32 | bf16. Every row is
+ * stored once into each rank that owns one of its experts, with per slot the
+ * local expert id there (-1 when owned elsewhere) and the weight; pos (T x
+ * world ints) receives each token's row index at each rank (-1: not sent), and
+ * every rank's count of rows from this rank is published. chunk_counts:
+ * device scratch of 8 * max(1, ceil(T / 1024)) ints. An id outside
+ * [0, n_experts) sets the device error and is not routed. */
+int skcq_ep_dispatch(const void* x, int x_dtype, int64_t x_ld, const int64_t* topk, const void* weights, int w_dtype,
+                     int T, int k, int n_experts, const int32_t* bounds, void* const* peers, int world, int rank,
+                     int capacity, int top_k_cap, int hidden, int32_t* chunk_counts, int32_t* pos, void* stream);
+
+/* The rows received in this rank's buffer as a routing of its local experts:
+ * topk_out / weights_out (world * capacity, k) int64 / f32, id -1 (weight 0)
+ * for slots owned elsewhere and rows past a source's count (feed
+ * skcq_route_sort with skip_negative = 1). */
+int skcq_ep_unpack(const void* buffer, int world, int capacity, int k, int top_k_cap, int hidden, int64_t* topk_out,
+                   float* weights_out, void* stream);
+
+/* For every received row r = s * capacity + i (i below source s's count):
+ * sum over its local slots, in ascending (expert, slot) order, of
+ * (sum_split part[split][row_of_pair[kpos * world * capacity + r]]) * weight,
+ * stored in out_dtype into rank s's returned sums at [rank][i] (the combine of
+ * codebook_experts.py:476-480, restricted to this rank's experts, written
+ * straight into the source's memory). P = world * capacity * k. */
+int skcq_ep_return(const void* part, int part_dtype, int n_split, int64_t P, const int32_t* row_of_pair,
+                   const int64_t* topk_local, const float* weights_local, const void* buffer, void* const* peers,
+                   const int32_t* bounds, int n_experts, int world, int rank, int capacity, int k, int top_k_cap,
+                   int hidden, int out_dtype, void* stream);
+
+/* out[t] = sum over ranks d ascending with pos[t][d] >= 0 of the sum rank d
+ * returned for token t (ret_dtype), stored as out_dtype (T, hidden). */
+int skcq_ep_gather(const void* buffer, const int32_t* pos, int T, int world, int capacity, int top_k_cap, int hidden,
+                   int ret_dtype, void* out, int out_dtype, void* stream);
 
 #ifdef __cplusplus
 }

@@ -71,7 +71,7 @@ _SIGS: dict[str, list] = {
     "skcq_pack_sign_masks": [P, I, I, L, I, I, P, P],
     "skcq_lut_build": [P, P, I, L, I, P, P],
     "skcq_selftest_wait_timeout": [C.c_longlong, P],
-    "skcq_route_sort": [P, I, I, I, P, P, P, P, P, C.c_size_t, P],
+    "skcq_route_sort": [P, I, I, I, P, P, P, P, P, C.c_size_t, I, P],
     "skcq_route_sort_scratch_bytes": [I, I, I],
     "skcq_codebook_forward": [P, I, P, I, L, P, I, P, P, P, I, I, I, I, I, I, P, L, P],
     "skcq_sum_splits": [P, I, L, I, P, I, L, P],
@@ -82,6 +82,15 @@ _SIGS: dict[str, list] = {
     "skcq_prefill_dequant": [P, I, P, I, I, I, I, P, P],
     "skcq_prefill_gemm": [P, P, P, I, I, I, P, I, L, P],
     "skcq_prefill_gemm_swiglu": [P, P, P, I, I, I, P, P],
+    "skcq_ep_layout": [I, I, I, I, P],
+    "skcq_ep_alloc": [C.c_size_t, C.POINTER(P), P],
+    "skcq_ep_open": [P, C.POINTER(P)],
+    "skcq_ep_close": [P],
+    "skcq_ep_free": [P],
+    "skcq_ep_dispatch": [P, I, L, P, P, I, I, I, I, P, P, I, I, I, I, I, P, P, P],
+    "skcq_ep_unpack": [P, I, I, I, I, I, P, P, P],
+    "skcq_ep_return": [P, I, I, L, P, P, P, P, P, P, I, I, I, I, I, I, I, I, P],
+    "skcq_ep_gather": [P, P, I, I, I, I, I, I, P, I, P],
 }
 _RESTYPES = {"skcq_reseed_scratch_bytes": C.c_size_t, "skcq_route_sort_scratch_bytes": C.c_size_t}
 
@@ -128,7 +137,8 @@ _KERNELS_PER_CALL = {
     "skcq_lut_build": 1, "skcq_selftest_wait_timeout": 1,
     "skcq_route_sort": 1, "skcq_sum_splits": 1, "skcq_swiglu": 1, "skcq_combine": 1,
     "skcq_prefill_plan": 1, "skcq_prefill_pack": 1, "skcq_prefill_dequant": 1, "skcq_prefill_gemm": 1,
-    "skcq_prefill_gemm_swiglu": 1,
+    "skcq_prefill_gemm_swiglu": 1, "skcq_ep_dispatch": 3, "skcq_ep_unpack": 1, "skcq_ep_return": 1,
+    "skcq_ep_gather": 1,
 }
 
 

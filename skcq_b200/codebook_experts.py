@@ -502,13 +502,34 @@ class CodebookExperts(nn.Module):
         h = _as_rows(hidden_states.to(dev))
         T, H = h.shape
         k = top_k_index.shape[1]
-        E = self.num_experts
-        P = T * k
         topk = top_k_index.to(device=dev, dtype=torch.int64).contiguous()
         w = top_k_weights.to(dev)
         if w.dtype not in (torch.float32, torch.bfloat16):
             w = w.float()
         w = w.contiguous()
+        d, Sd, inv = self.pair_outputs(h, topk)
+        out = torch.empty(T, H, dtype=h.dtype, device=dev)
+        call("skcq_combine", ptr(d), _DTYPE[d.dtype], Sd, T * k, ptr(inv), ptr(topk), ptr(w), _DTYPE[w.dtype], T, k,
+             H, ptr(out), _DTYPE[out.dtype], stream())
+        if self.check_errors:
+            _lib.poll_device_error()
+        return out.to(device=hidden_states.device, dtype=hidden_states.dtype)
+
+    def pair_outputs(self, h: torch.Tensor, topk: torch.Tensor, skip_negative: bool = False,
+                     pairs_hint: int | None = None) -> tuple[torch.Tensor, int, torch.Tensor]:
+        """Expert outputs of every routed (token, slot) pair of ``h`` (T, H) and
+        ``topk`` (T, k) int64 on the modules' device: returns ``(d, n_split,
+        row_of_pair)`` with pair p = kpos * T + token's output the sum over
+        splits of ``d[s][row_of_pair[p]]`` (``d`` is (n_split, P, H) f32 on the
+        gather path, (P, H) bf16 with n_split 1 on the tensor-core path).
+        ``skip_negative``: slots with a negative id are not routed here.
+        ``pairs_hint``: the expected number of routed pairs (defaults to T * k),
+        which picks the path."""
+        dev = h.device
+        T = h.shape[0]
+        k = topk.shape[1]
+        E = self.num_experts
+        P = T * k
         route = torch.empty(2 * max(P, 1) + 2 * (E + 1), dtype=torch.int32, device=dev)
         perm = route[:max(P, 1)]
         inv = route[max(P, 1):2 * max(P, 1)]
@@ -517,14 +538,11 @@ class CodebookExperts(nn.Module):
         scratch_bytes = int(_lib.load().skcq_route_sort_scratch_bytes(T, k, E))
         scratch = torch.empty(scratch_bytes, dtype=torch.uint8, device=dev) if scratch_bytes else None
         call("skcq_route_sort", ptr(topk), T, k, E, ptr(perm), ptr(seg), ptr(inv), ptr(active), ptr(scratch),
-             scratch_bytes, stream())
+             scratch_bytes, int(skip_negative), stream())
         max_active = min(E, P)
         I = self.gate.out_dim
-        if self._use_prefill(h, P, max_active):
-            out = self._forward_prefill(h, topk, w, perm, seg, inv, active, T, k, E, P, max_active)
-            if self.check_errors:
-                _lib.poll_device_error()
-            return out.to(device=hidden_states.device, dtype=hidden_states.dtype)
+        if self._use_prefill(h, P if pairs_hint is None else pairs_hint, max_active):
+            return self._prefill_pairs(h, perm, seg, active, T, P, max_active), 1, inv
         S = _choose_splits(max_active, I, min(self.gate.min_blocks, self.up.min_blocks), P)
         # rows per expert: at most T when a token's k experts are distinct
         seg_kw = {"active": active, "max_active": max_active, "n_rows": P, "rows_hint": min(T, 8)}
@@ -539,12 +557,7 @@ class CodebookExperts(nn.Module):
             gs, us = g.sum(0), u.sum(0)
             inter.copy_(self.intermediate(gs, us))
         d, Sd = self.down.run_segments(inter, seg, None, E, lut_layers=self._lut_layers(self.down, P, P), **seg_kw)
-        out = torch.empty(T, H, dtype=h.dtype, device=dev)
-        call("skcq_combine", ptr(d), _DTYPE[d.dtype], Sd, P, ptr(inv), ptr(topk), ptr(w), _DTYPE[w.dtype], T, k, H,
-             ptr(out), _DTYPE[out.dtype], stream())
-        if self.check_errors:
-            _lib.poll_device_error()
-        return out.to(device=hidden_states.device, dtype=hidden_states.dtype)
+        return d, Sd, inv
 
     def _lut_layers(self, mod: CodebookModule, n_tok: int, P: int) -> list[bool] | None:
         """Which layers of ``mod`` read a lookup table: x has ``n_tok`` rows and
@@ -565,17 +578,17 @@ class CodebookExperts(nn.Module):
         return (h.dtype == torch.bfloat16 and P >= self.prefill_min_rows * max(1, max_active)
                 and all(la.codebook.dtype == torch.bfloat16 for m in mods for la in m.layers))
 
-    def _forward_prefill(self, h, topk, w, perm, seg, inv, active, T, k, E, P, max_active) -> torch.Tensor:
+    def _prefill_pairs(self, h, perm, seg, active, T, P, max_active) -> torch.Tensor:
         """Tensor-core path: plan 128-row tiles per expert, pack the routed
         rows once for gate and up, decode each projection's active experts and
         run the grouped tcgen05 GEMM; SwiGLU is fused into packing the down
-        projection's rows."""
+        projection's rows. Returns the (P, H) bf16 pair outputs."""
         dev = h.device
         H = h.shape[1]
         I = self.gate.out_dim
         max_tiles = -(-P // 128) + max_active
         tiles = torch.empty(1 + 3 * max_tiles, dtype=torch.int32, device=dev)
-        call("skcq_prefill_plan", ptr(seg), E, max_tiles, ptr(tiles), stream())
+        call("skcq_prefill_plan", ptr(seg), self.num_experts, max_tiles, ptr(tiles), stream())
         A = torch.empty(max_tiles * (-(-H // 64)) * 8192, dtype=torch.bfloat16, device=dev)
         call("skcq_prefill_pack", 0, ptr(h), _DTYPE[h.dtype], h.stride(0), ptr(perm), T, None, 0, H, ptr(tiles),
              max_tiles, ptr(A), stream())
@@ -597,11 +610,7 @@ class CodebookExperts(nn.Module):
                  ptr(tiles), max_tiles, ptr(A2), stream())
         del A
         # bf16 down outputs, as the reference's bf16 module produces them
-        d = self.down.prefill(A2, tiles, max_tiles, active, max_active, P, I, out_dtype=torch.bfloat16)
-        out = torch.empty(T, H, dtype=h.dtype, device=dev)
-        call("skcq_combine", ptr(d), _DTYPE[d.dtype], 1, P, ptr(inv), ptr(topk), ptr(w), _DTYPE[w.dtype], T, k, H,
-             ptr(out), _DTYPE[out.dtype], stream())
-        return out
+        return self.down.prefill(A2, tiles, max_tiles, active, max_active, P, I, out_dtype=torch.bfloat16)
 
 
 class GraphedExperts:

@@ -93,12 +93,14 @@ __global__ void pack_signs_kernel(const int8_t* __restrict__ signs, int E, int o
 constexpr int RT_THREADS = 1024;
 constexpr int RT_SMALL_E = 256;  // chunked warp-ranking path up to this many experts
 
-__device__ __forceinline__ int pair_bucket(const int64_t* topk, int T, int k, int E, int p, int* err) {
+// skip != 0: a negative id marks a slot routed elsewhere (expert-parallel
+// receive buffers) and goes to the trailing bucket without an error.
+__device__ __forceinline__ int pair_bucket(const int64_t* topk, int T, int k, int E, int p, int* err, int skip) {
   const int kp = p / T, t = p - kp * T;
   const int64_t e = topk[(int64_t)t * k + kp];
   if (e < 0 || e >= E) {
-    atomicCAS(err, 0, 41);
-    return E;  // trailing bucket: never computed, flagged
+    if (!(skip && e < 0)) atomicCAS(err, 0, 41);
+    return E;  // trailing bucket: never computed
   }
   return (int)e;
 }
@@ -110,7 +112,7 @@ __device__ __forceinline__ int pair_bucket(const int64_t* topk, int T, int k, in
 __global__ void __launch_bounds__(RT_THREADS) route_sort_kernel(const int64_t* __restrict__ topk, int T, int k, int E,
                                                                 int32_t* __restrict__ perm, int32_t* __restrict__ seg,
                                                                 int32_t* __restrict__ inv, int32_t* __restrict__ active,
-                                                                int* err) {
+                                                                int* err, int skip) {
   extern __shared__ int sm[];
   const int NB = E + 1;  // buckets incl. the invalid one
   int* cnt = sm;         // [NB]
@@ -121,7 +123,7 @@ __global__ void __launch_bounds__(RT_THREADS) route_sort_kernel(const int64_t* _
   const int tid = threadIdx.x;
   for (int b = tid; b < NB; b += RT_THREADS) cnt[b] = 0;
   __syncthreads();
-  for (int p = tid; p < P; p += RT_THREADS) atomicAdd(&cnt[pair_bucket(topk, T, k, E, p, err)], 1);
+  for (int p = tid; p < P; p += RT_THREADS) atomicAdd(&cnt[pair_bucket(topk, T, k, E, p, err, skip)], 1);
   __syncthreads();
   if (tid == 0) {
     int run = 0, na = 0;
@@ -143,7 +145,7 @@ __global__ void __launch_bounds__(RT_THREADS) route_sort_kernel(const int64_t* _
       for (int i = tid; i < 32 * NB; i += RT_THREADS) wcnt[i] = 0;
       __syncthreads();
       const int p = c0 + tid;
-      const int bk = p < P ? pair_bucket(topk, T, k, E, p, err) : -1;
+      const int bk = p < P ? pair_bucket(topk, T, k, E, p, err, skip) : -1;
       const unsigned peers = __match_any_sync(0xffffffffu, bk);
       const int rank = __popc(peers & ((1u << lane) - 1u));
       if (bk >= 0 && lane == __ffs(peers) - 1) wcnt[w * NB + bk] = __popc(peers);
@@ -193,13 +195,13 @@ __global__ void __launch_bounds__(RT_THREADS) route_sort_kernel(const int64_t* _
 constexpr int RS_CHUNK = 4096;
 
 __global__ void __launch_bounds__(RT_THREADS) route_count_kernel(const int64_t* __restrict__ topk, int T, int k, int E,
-                                                                 int32_t* __restrict__ hist, int* err) {
+                                                                 int32_t* __restrict__ hist, int* err, int skip) {
   extern __shared__ int sm[];
   const int NB = E + 1, P = T * k;
   for (int b = threadIdx.x; b < NB; b += RT_THREADS) sm[b] = 0;
   __syncthreads();
   const int p0 = blockIdx.x * RS_CHUNK, p1 = min(P, p0 + RS_CHUNK);
-  for (int p = p0 + threadIdx.x; p < p1; p += RT_THREADS) atomicAdd(&sm[pair_bucket(topk, T, k, E, p, err)], 1);
+  for (int p = p0 + threadIdx.x; p < p1; p += RT_THREADS) atomicAdd(&sm[pair_bucket(topk, T, k, E, p, err, skip)], 1);
   __syncthreads();
   for (int b = threadIdx.x; b < NB; b += RT_THREADS) hist[(int64_t)blockIdx.x * NB + b] = sm[b];
 }
@@ -242,7 +244,7 @@ __global__ void __launch_bounds__(RT_THREADS) route_scan_kernel(int E, int n_chu
 __global__ void __launch_bounds__(RT_THREADS) route_scatter_kernel(const int64_t* __restrict__ topk, int T, int k,
                                                                    int E, const int32_t* __restrict__ hist,
                                                                    int32_t* __restrict__ perm,
-                                                                   int32_t* __restrict__ inv, int* err) {
+                                                                   int32_t* __restrict__ inv, int* err, int skip) {
   extern __shared__ int sm[];
   const int NB = E + 1, P = T * k;
   int* base = sm;            // [NB]
@@ -255,7 +257,7 @@ __global__ void __launch_bounds__(RT_THREADS) route_scatter_kernel(const int64_t
     for (int i = tid; i < 32 * NB; i += RT_THREADS) wcnt[i] = 0;
     __syncthreads();
     const int p = c0 + tid;
-    const int bk = p < p1 ? pair_bucket(topk, T, k, E, p, err) : -1;
+    const int bk = p < p1 ? pair_bucket(topk, T, k, E, p, err, skip) : -1;
     const unsigned peers = __match_any_sync(0xffffffffu, bk);
     const int rank = __popc(peers & ((1u << lane) - 1u));
     if (bk >= 0 && lane == __ffs(peers) - 1) wcnt[w * NB + bk] = __popc(peers);
@@ -723,35 +725,59 @@ __global__ void __launch_bounds__(CB_THREADS) combine_kernel(const void* __restr
                                                              const int32_t* __restrict__ row_of_pair,
                                                              const int64_t* __restrict__ topk, const void* __restrict__ w,
                                                              int w_dtype, int T, int k, int H, void* __restrict__ out,
-                                                             int out_dtype) {
+                                                             int out_dtype, int vec8) {
   __shared__ int s_row[32];
   __shared__ float s_w[32];
+  __shared__ int s_n;
   const int64_t stride = P * H;
   for (int t = blockIdx.x; t < T; t += gridDim.x) {
     if (threadIdx.x < 32) {
       // lane kp ranks its slot by (expert, kpos) among the token's k slots
+      // (a negative id: a slot routed elsewhere, skipped)
       const int lane = threadIdx.x;
-      const int64_t e = lane < k ? topk[(int64_t)t * k + lane] : INT64_MAX;
+      int64_t e = lane < k ? topk[(int64_t)t * k + lane] : INT64_MAX;
+      if (e < 0) e = INT64_MAX;
       int rank = 0;
       for (int j = 0; j < k; ++j) {
         const int64_t ej = __shfl_sync(0xffffffffu, e, j);
         rank += (ej < e || (ej == e && j < lane)) ? 1 : 0;
       }
+      const unsigned live = __ballot_sync(0xffffffffu, lane < k && e != INT64_MAX);
+      if (lane == 0) s_n = __popc(live);
       if (lane < k) {
         s_row[rank] = row_of_pair[(int64_t)lane * T + t];
         s_w[rank] = ld_any(w, (int64_t)t * k + lane, w_dtype);
       }
     }
     __syncthreads();
-    for (int h = blockIdx.y * CB_THREADS + threadIdx.x; h < H; h += gridDim.y * CB_THREADS) {
-      float acc = 0.f;
-      for (int step = 0; step < k; ++step) {
-        const int64_t i = (int64_t)s_row[step] * H + h;
-        float y = ld_any(part, i, part_dtype);
-        for (int sp = 1; sp < n_split; ++sp) y += ld_any(part, sp * stride + i, part_dtype);
-        acc = __fadd_rn(acc, __fmul_rn(y, s_w[step]));
+    const int n_live = s_n;
+    if (vec8) {
+      // bf16 pair outputs, one split, H % 8 == 0: 16-byte loads and stores of
+      // 8 consecutive features, the same arithmetic per feature
+      for (int h = (blockIdx.y * CB_THREADS + threadIdx.x) * 8; h < H; h += gridDim.y * CB_THREADS * 8) {
+        float acc[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+        for (int step = 0; step < n_live; ++step) {
+          float y[8];
+          ld_bf16x8(part, (int64_t)s_row[step] * H + h, y);
+          const float ws = s_w[step];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[j] = __fadd_rn(acc[j], __fmul_rn(y[j], ws));
+        }
+        st_x8(out, (int64_t)t * H + h, out_dtype, acc);
       }
-      st_any(out, (int64_t)t * H + h, out_dtype, acc);
+    } else {
+      for (int h = blockIdx.y * CB_THREADS + threadIdx.x; h < H; h += gridDim.y * CB_THREADS) {
+        float acc = 0.f;
+        for (int step = 0; step < n_live; ++step) {
+          const int64_t i = (int64_t)s_row[step] * H + h;
+          float y = ld_any(part, i, part_dtype);
+          for (int sp = 1; sp < n_split; ++sp) y += ld_any(part, sp * stride + i, part_dtype);
+          acc = __fadd_rn(acc, __fmul_rn(y, s_w[step]));
+        }
+        st_any(out, (int64_t)t * H + h, out_dtype, acc);
+      }
     }
     __syncthreads();
   }
@@ -812,7 +838,7 @@ extern "C" size_t skcq_route_sort_scratch_bytes(int T, int k, int n_experts) {
 
 extern "C" int skcq_route_sort(const int64_t* topk, int T, int k, int n_experts, int32_t* perm, int32_t* seg,
                                int32_t* row_of_pair, int32_t* active, void* scratch, size_t scratch_bytes,
-                               void* stream) {
+                               int skip_negative, void* stream) {
   SKCQ_REQUIRE(topk && perm && seg && row_of_pair && active, SKCQ_ERR_INVALID, "route_sort: null pointer");
   SKCQ_REQUIRE(T >= 0 && k > 0 && k <= 31 && n_experts > 0 && n_experts <= 8192, SKCQ_ERR_INVALID,
                "route_sort: bad sizes (T %d, k %d, experts %d)", T, k, n_experts);
@@ -826,16 +852,17 @@ extern "C" int skcq_route_sort(const int64_t* topk, int T, int k, int n_experts,
     const int P = T * k;
     const int chunks = (P + RS_CHUNK - 1) / RS_CHUNK;
     int32_t* hist = static_cast<int32_t*>(scratch);
-    route_count_kernel<<<chunks, RT_THREADS, (size_t)NB * sizeof(int), s>>>(topk, T, k, n_experts, hist, err);
+    route_count_kernel<<<chunks, RT_THREADS, (size_t)NB * sizeof(int), s>>>(topk, T, k, n_experts, hist, err,
+                                                                            skip_negative);
     route_scan_kernel<<<1, RT_THREADS, (size_t)NB * sizeof(int), s>>>(n_experts, chunks, hist, seg, active);
     route_scatter_kernel<<<chunks, RT_THREADS, (size_t)34 * NB * sizeof(int), s>>>(topk, T, k, n_experts, hist, perm,
-                                                                                   row_of_pair, err);
+                                                                                   row_of_pair, err, skip_negative);
     return check_launch("route_sort");
   }
   size_t smem = (size_t)3 * NB * sizeof(int);
   if (n_experts <= RT_SMALL_E) smem += (size_t)32 * NB * sizeof(int);
   route_sort_kernel<<<1, RT_THREADS, smem, (cudaStream_t)stream>>>(topk, T, k, n_experts, perm, seg, row_of_pair,
-                                                                  active, err);
+                                                                  active, err, skip_negative);
   return check_launch("route_sort");
 }
 
@@ -1001,12 +1028,14 @@ extern "C" int skcq_combine(const void* part, int part_dtype, int n_split, int64
   SKCQ_REQUIRE(out_dtype == SKCQ_DTYPE_F32 || out_dtype == SKCQ_DTYPE_BF16, SKCQ_ERR_INVALID,
                "combine: output dtype %d", out_dtype);
   if ((int64_t)T * H <= 0) return SKCQ_OK;
+  const int vec8 = part_dtype == SKCQ_DTYPE_BF16 && n_split == 1 && H % 8 == 0 && ((uintptr_t)part & 15) == 0 &&
+                   ((uintptr_t)out & 15) == 0;
   const int gx = T < 148 * 16 ? T : 148 * 16;
-  int gy = ceil_div(H, CB_THREADS);
+  int gy = ceil_div(vec8 ? H / 8 : H, CB_THREADS);
   const int want_y = ceil_div(148 * 4, gx);
   if (gy > want_y) gy = want_y;
   combine_kernel<<<dim3(gx, gy), CB_THREADS, 0, (cudaStream_t)stream>>>(part, part_dtype, n_split, P, row_of_pair,
                                                                         topk, weights, w_dtype, T, k, H, out,
-                                                                        out_dtype);
+                                                                        out_dtype, vec8);
   return check_launch("combine");
 }

@@ -31,6 +31,34 @@ __device__ __forceinline__ void st_any(void* p, int64_t i, int dtype, float v) {
   }
 }
 
+// Elements [i, i + 8) of a bf16 array (i * 2 bytes 16-byte aligned) -> f32.
+__device__ __forceinline__ void ld_bf16x8(const void* p, int64_t i, float (&v)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p) + i);
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    v[2 * j] = __uint_as_float(w[j] << 16);
+    v[2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
+  }
+}
+
+// Elements [i, i + 8) of an f32 | bf16 array (16-byte aligned), rounded as st_any.
+__device__ __forceinline__ void st_x8(void* p, int64_t i, int dtype, const float (&v)[8]) {
+  if (dtype == SKCQ_DTYPE_BF16) {
+    uint32_t w[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      __nv_bfloat16 lo = __float2bfloat16_rn(v[2 * j]), hi = __float2bfloat16_rn(v[2 * j + 1]);
+      w[j] = (uint32_t)*reinterpret_cast<uint16_t*>(&lo) | ((uint32_t)*reinterpret_cast<uint16_t*>(&hi) << 16);
+    }
+    *reinterpret_cast<uint4*>(static_cast<uint16_t*>(p) + i) = make_uint4(w[0], w[1], w[2], w[3]);
+  } else {
+    float4* q = reinterpret_cast<float4*>(static_cast<float*>(p) + i);
+    q[0] = make_float4(v[0], v[1], v[2], v[3]);
+    q[1] = make_float4(v[4], v[5], v[6], v[7]);
+  }
+}
+
 // Centroid vector of BS elements at p -> f32 registers, with the widest
 // aligned vector loads (p is aligned to BS * sizeof(T)).
 template <int BS, typename T>

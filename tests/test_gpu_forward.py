@@ -412,7 +412,7 @@ def test_prefill_gemm_exact_on_bf16_operands():
     route = torch.empty(2 * P + 2 * (E + 1), dtype=torch.int32, device="cuda")
     perm, inv, seg, active = route[:P], route[P:2 * P], route[2 * P:2 * P + E + 1], route[2 * P + E + 1:]
     call("skcq_route_sort", ptr(topi.contiguous()), T, k, E, ptr(perm), ptr(seg), ptr(inv), ptr(active), None, 0,
-         stream())
+         0, stream())
     max_tiles = -(-P // 128) + E
     tiles = torch.empty(1 + 3 * max_tiles, dtype=torch.int32, device="cuda")
     call("skcq_prefill_plan", ptr(seg), E, max_tiles, ptr(tiles), stream())
@@ -488,7 +488,7 @@ def test_route_sort_multi_cta_matches_one_cta():
             assert not use_scratch or nbytes > 0
             scratch = torch.empty(max(nbytes, 1), dtype=torch.uint8, device="cuda")
             call("skcq_route_sort", ptr(topi), T, k, E, ptr(perm), ptr(seg), ptr(inv), ptr(active),
-                 ptr(scratch) if use_scratch else None, nbytes, stream())
+                 ptr(scratch) if use_scratch else None, nbytes, 0, stream())
             outs.append((perm.cpu(), inv.cpu(), seg.cpu(), active.cpu()))
         for a, b in zip(outs[0], outs[1]):
             assert torch.equal(a, b)
