@@ -179,10 +179,57 @@ int skcq_reseed_candidates(int metric, const float* X, const float* C, const int
  * cosine C = normalize(sums); euclidean C = sums / counts (reseeded clusters
  * take the point). moved = ||C_new - C_old||_F; a problem whose moved < 1e-6
  * stops (active = 0, converged = 1). Records moved_hist[iter][b] and
- * nempty_hist[iter][b], sets iters_run[b] = iter + 1, and zeroes sums/counts. */
+ * nempty_hist[iter][b], sets iters_run[b] = iter + 1, and zeroes sums/counts.
+ * changed (optional, [nblk][k_pad] bytes from skcq_mark_changed): a non-empty
+ * cluster with changed == 0 has the same members as at the previous update,
+ * so its centroid is kept bit for bit (and adds 0 to moved); every centroid
+ * that is recomputed or reseeded gets changed = 1, which tells the next
+ * incremental assignment that it moved. */
 int skcq_finalize(int metric, float* sums, int32_t* counts, const int32_t* n_empty, int nblk, int k_pad, int bs,
                   const int32_t* k, int32_t* active, int32_t* converged, int32_t* iters_run, float* moved_hist,
-                  int32_t* nempty_hist, int iter, float* C, void* stream);
+                  int32_t* nempty_hist, int iter, float* C, uint8_t* changed, void* stream);
+
+/* ---- incremental assignment ---------------------------------------------------
+ * Exact: a centroid whose cluster kept its members keeps its value (see
+ * skcq_finalize), so its scores are unchanged, and a point assigned to such a
+ * centroid can only move to a centroid that moved. The host runs, per
+ * iteration after the first: skcq_moved_lists; skcq_assign of every point
+ * against the moved centroids only (gathered with skcq_gather_rows, labels
+ * indexing the moved list); skcq_assign of the points whose centroid moved
+ * (gathered) against all centroids; skcq_assign_merge. The labels equal a full
+ * skcq_assign's. No counterpart in the reference, which rescans every
+ * centroid each iteration (kmeans.py:136-149). */
+
+/* changed[b][c] = 1 for every cluster c that gained or lost a point between
+ * prev and labels (all = 1: every cluster, for the first assignment); rows of
+ * problems with mask[b] == 0 are left as they are. */
+int skcq_mark_changed(const int32_t* prev, const int32_t* labels, int nblk, int n_pad, int k_pad, const int32_t* n,
+                      const int32_t* mask, int all, uint8_t* changed, void* stream);
+
+/* For the problems with mask[b] != 0: mlist[b][0 .. mcount[b]) = the centroids
+ * c < k[b] with changed[b][c], ascending; plist[b][0 .. pcount[b]) = the
+ * points i < n[b] whose labels[b][i] has changed set, ascending. scratch:
+ * skcq_moved_lists_scratch_bytes(nblk, n_pad, k_pad) bytes. */
+size_t skcq_moved_lists_scratch_bytes(int nblk, int n_pad, int k_pad);
+int skcq_moved_lists(const uint8_t* changed, const int32_t* labels, int nblk, int n_pad, int k_pad, const int32_t* n,
+                     const int32_t* k, const int32_t* mask, int32_t* mlist, int32_t* mcount, int32_t* plist,
+                     int32_t* pcount, void* scratch, size_t scratch_bytes, void* stream);
+
+/* dst[b][j][:] = src[b][idx[b][j]][:] for j < count[b], 0 for count[b] <= j <
+ * out_rows (src [nblk][src_rows][bs], idx row stride idx_ld). */
+int skcq_gather_rows(const float* src, int src_rows, const int32_t* idx, int idx_ld, const int32_t* count, int nblk,
+                     int out_rows, int bs, float* dst, void* stream);
+
+/* In place on labels (the previous assignment) for the active problems: a
+ * point whose centroid a did not move (changed[b][a] == 0) takes
+ * c = mlist[b][labels_m[b][i]] (the best moved centroid; labels_m from
+ * skcq_assign against the gathered moved centroids) when c scores higher than
+ * a under the reference formula, or the same with c < a; the points of plist
+ * take labels_f[b][j] (skcq_assign of the gathered points, row stride p_pad). */
+int skcq_assign_merge(int metric, const float* X, const float* C, const float* cnorm, int nblk, int n_pad, int k_pad,
+                      int bs, const int32_t* n, const int32_t* active, const uint8_t* changed, const int32_t* mlist,
+                      const int32_t* mcount, const int32_t* labels_m, const int32_t* plist, const int32_t* pcount,
+                      int p_pad, const int32_t* labels_f, int32_t* labels, void* stream);
 
 /* ---- codec post-processing ------------------------------------------------- */
 

@@ -111,6 +111,109 @@ def packed_width(metric: int, bs: int) -> int:
 TC_MAX_KP = 64  # widest split operand the tensor-core kernel stages (bs <= 20)
 
 
+# Called after every incremental assignment with (pts, B, C, cnorm, k_pad,
+# k_dev, active, labels) when set; tests compare the labels with a full pass.
+INCREMENTAL_CHECK: Callable | None = None
+
+# The incremental assignment replaces a full pass when its two tensor-core
+# passes cover fewer than this share of the full pass's (256-point unit x
+# 128-centroid tile) products.
+INCREMENTAL_MAX_SHARE = 0.8
+
+
+class IncrementalAssign:
+    """State of the exact incremental assignment of one Lloyd run
+    (csrc/incremental.cu): a centroid whose cluster kept its members keeps its
+    value, so a point assigned to it can only move to a centroid that moved.
+    After each update the moved centroids and the points assigned to them are
+    listed; the next assignment scores every point against the moved centroids
+    only, re-assigns the listed points over all centroids, and merges. The
+    labels are those of a full assignment."""
+
+    def __init__(self, pts: PointSet, k_pad: int, k_host: list[int], labels: torch.Tensor) -> None:
+        dev = pts.X.device
+        self.pts, self.k_pad, self.labels = pts, k_pad, labels
+        self.changed = torch.ones(pts.nblk, k_pad, dtype=torch.uint8, device=dev)
+        self.prev = torch.empty_like(labels)
+        self.mlist = torch.zeros(pts.nblk, k_pad, dtype=torch.int32, device=dev)
+        self.plist = torch.zeros(pts.nblk, pts.n_pad, dtype=torch.int32, device=dev)
+        self.counts = torch.zeros(2, pts.nblk, dtype=torch.int32, device=dev)  # moved centroids, listed points
+        self.counts_host = torch.zeros(2, pts.nblk, dtype=torch.int32, pin_memory=True)
+        self.scratch_bytes = int(_lib.load().skcq_moved_lists_scratch_bytes(pts.nblk, pts.n_pad, k_pad))
+        self.scratch = torch.empty(max(self.scratch_bytes, 1), dtype=torch.uint8, device=dev)
+        self.units_n = np.ceil(np.array(pts.n_host, dtype=np.float64) / ROWS_PER_UNIT)
+        self.units_k = np.ceil(np.array(k_host, dtype=np.float64) / CENT_TILE)
+        self.k_host = np.array(k_host, dtype=np.float64)
+        self.n_host = np.array(pts.n_host, dtype=np.float64)
+        self.listed = False
+
+    def mark(self, first: bool, mask: torch.Tensor) -> None:
+        """Clusters whose members changed in this iteration's assignment."""
+        pts = self.pts
+        call("skcq_mark_changed", ptr(self.prev), ptr(self.labels), pts.nblk, pts.n_pad, self.k_pad, ptr(pts.n),
+             ptr(mask), int(first), ptr(self.changed), stream())
+
+    def lists(self, mask: torch.Tensor, k_dev: torch.Tensor) -> None:
+        """After the update: moved centroids and the points assigned to them
+        (rows of the problems in ``mask``), counts copied to the host."""
+        pts = self.pts
+        call("skcq_moved_lists", ptr(self.changed), ptr(self.labels), pts.nblk, pts.n_pad, self.k_pad, ptr(pts.n),
+             ptr(k_dev), ptr(mask), ptr(self.mlist), ptr(self.counts[0]), ptr(self.plist), ptr(self.counts[1]),
+             ptr(self.scratch), self.scratch_bytes, stream())
+        self.counts_host.copy_(self.counts, non_blocking=True)
+        self.listed = True
+
+    def plan(self, act: np.ndarray) -> tuple[int, int, float] | None:
+        """(m_pad, p_pad, algorithmic work) of an incremental assignment of the
+        problems in ``act`` (host bool mask), or None when a full pass is cheaper.
+        Reads the counts of the last ``lists`` (the caller synchronised)."""
+        if not self.listed or not act.any():
+            return None
+        m = self.counts_host[0].numpy().astype(np.float64)
+        p = self.counts_host[1].numpy().astype(np.float64)
+        full = float((self.units_n * self.units_k)[act].sum())
+        inc = float((self.units_n * np.ceil(m / CENT_TILE) + np.ceil(p / ROWS_PER_UNIT) * self.units_k)[act].sum())
+        if full <= 0 or inc >= INCREMENTAL_MAX_SHARE * full:
+            return None
+        m_pad = int(np.ceil(m[act].max() / CENT_TILE)) * CENT_TILE if m[act].max() > 0 else 0
+        p_pad = int(np.ceil(p[act].max() / ROWS_PER_UNIT)) * ROWS_PER_UNIT if p[act].max() > 0 else 0
+        work = 2.0 * self.pts.bs * float((self.n_host * m + p * self.k_host)[act].sum())
+        return m_pad, p_pad, work
+
+    def assign(self, B, C, cnorm, k_dev, active, m_pad: int, p_pad: int) -> None:
+        """Labels of the problems in ``active`` (None: all) from the previous
+        labels, in place."""
+        pts, dev, s = self.pts, self.pts.X.device, stream()
+        act = active if active is not None else torch.ones(pts.nblk, dtype=torch.int32, device=dev)
+        mcount, pcount = self.counts[0], self.counts[1]
+        labels_m = torch.zeros(1, dtype=torch.int32, device=dev)
+        if m_pad > 0:  # every point against the moved centroids
+            Cm = torch.empty(pts.nblk, m_pad, pts.bs, dtype=torch.float32, device=dev)
+            call("skcq_gather_rows", ptr(C), self.k_pad, ptr(self.mlist), self.k_pad, ptr(mcount), pts.nblk, m_pad,
+                 pts.bs, ptr(Cm), s)
+            act_m = (act.bool() & (mcount > 0)).to(torch.int32)
+            Bm = torch.empty(pts.nblk, m_pad * pts.kp, dtype=torch.float32, device=dev)
+            cnm = torch.empty(pts.nblk, m_pad, dtype=torch.float32, device=dev)
+            call("skcq_pack_centroids", pts.metric, ptr(Cm), pts.nblk, m_pad, pts.bs, ptr(mcount), ptr(act_m),
+                 ptr(Bm), ptr(cnm), s)
+            labels_m = torch.zeros(pts.nblk, pts.n_pad, dtype=torch.int32, device=dev)
+            assign_call(pts, Bm, Cm, cnm, m_pad, mcount, act_m, labels_m)
+        labels_f = None
+        if p_pad > 0:  # the points whose centroid moved, against all centroids
+            Xf = torch.empty(pts.nblk, p_pad, pts.bs, dtype=torch.float32, device=dev)
+            call("skcq_gather_rows", ptr(pts.X), pts.n_pad, ptr(self.plist), pts.n_pad, ptr(pcount), pts.nblk,
+                 p_pad, pts.bs, ptr(Xf), s)
+            sub = PointSet(pts.metric, pts.nblk, pts.bs, p_pad, pcount, [], self.plist, Xf, Xf)
+            act_f = (act.bool() & (pcount > 0)).to(torch.int32)
+            labels_f = torch.zeros(pts.nblk, p_pad, dtype=torch.int32, device=dev)
+            assign_call(sub, B, C, cnorm, self.k_pad, k_dev, act_f, labels_f)
+        call("skcq_assign_merge", pts.metric, ptr(pts.X), ptr(C), ptr(cnorm), pts.nblk, pts.n_pad, self.k_pad,
+             pts.bs, ptr(pts.n), ptr(active), ptr(self.changed), ptr(self.mlist), ptr(mcount), ptr(labels_m),
+             ptr(self.plist), ptr(pcount), p_pad, ptr(labels_f), ptr(self.labels), s)
+        if INCREMENTAL_CHECK is not None:
+            INCREMENTAL_CHECK(pts, B, C, cnorm, self.k_pad, k_dev, active, self.labels)
+
+
 def assign_call(pts: PointSet, B, C, cnorm, k_pad: int, k_dev, active, labels) -> None:
     """Tensor-core assignment (+ exact re-score); blocks wider than the
     tensor-core path stages go to the exact CUDA-core kernel."""
@@ -246,20 +349,33 @@ def lloyd(
     iters_run = torch.zeros(nblk, dtype=torch.int32, device=dev)
     moved = torch.zeros(max(max_iters, 1), nblk, dtype=torch.float32, device=dev)
     nempty_hist = torch.zeros(max(max_iters, 1), nblk, dtype=torch.int32, device=dev)
-    flag = torch.empty(1, dtype=torch.int32, pin_memory=True)
+    act_host = torch.empty(nblk, dtype=torch.int32, pin_memory=True)
     T = TIMER
     nk = np.array(pts.n_host, dtype=np.float64) * np.array(k_host, dtype=np.float64)
+    # exact incremental assignment after the first iteration (one process;
+    # row-sharded problems rescan every centroid)
+    inc = IncrementalAssign(pts, k_pad, k_host, labels) if shard is None else None
+    act = (np.array(n_all) > 0)
     for it in range(max_iters):
-        work = padded = nbytes = 0.0
-        if T.enabled:  # algorithmic work of this iteration: 2*n*k*bs flops over active problems
-            act = active.cpu().numpy().astype(bool)
-            work = 2.0 * bs * float(nk[act].sum())
-            padded = work * kp / bs
-            # the split operands each active problem's tensor-core pass reads once
-            nbytes = 4.0 * kp * float(act.sum()) * (n_pad + k_pad)
         T.run("pack_centroids", lambda: call("skcq_pack_centroids", metric, ptr(C), nblk, k_pad, bs, ptr(k_dev),
                                              ptr(active), ptr(B), ptr(cnorm), s))
-        T.run("assign", lambda: assign_call(pts, B, C, cnorm, k_pad, k_dev, active, labels), work, padded, nbytes)
+        plan = inc.plan(act) if inc is not None else None
+        if inc is not None:
+            inc.prev.copy_(labels)
+        if plan is None:
+            # algorithmic work: 2*n*k*bs flops over the active problems
+            work = 2.0 * bs * float(nk[act].sum())
+            # the split operands each active problem's tensor-core pass reads once
+            nbytes = 4.0 * kp * float(act.sum()) * (n_pad + k_pad)
+            T.run("assign", lambda: assign_call(pts, B, C, cnorm, k_pad, k_dev, active, labels), work,
+                  work * kp / bs, nbytes)
+        else:
+            m_pad, p_pad, work = plan
+            nbytes = 4.0 * kp * float(act.sum()) * (n_pad + m_pad + p_pad + k_pad)
+            T.run("assign", lambda: inc.assign(B, C, cnorm, k_dev, active, m_pad, p_pad), work, work * kp / bs,
+                  nbytes)
+        if inc is not None:
+            inc.mark(it == 0, active)
         T.run("update", lambda: call("skcq_update", ptr(pts.R), ptr(labels), nblk, n_pad, k_pad, bs, ptr(pts.n),
                                      ptr(k_dev), ptr(active), ptr(sums), ptr(counts), s))
         if shard is None:
@@ -268,19 +384,30 @@ def lloyd(
                                          ptr(n_empty), ptr(scratch), s))
         else:
             _sharded_reseed(shard, pts, C, labels, k_pad, k_dev, active, sums, counts, n_empty, scratch, gofs)
+        ran = active.clone() if inc is not None else None
         T.run("finalize", lambda: call("skcq_finalize", metric, ptr(sums), ptr(counts), ptr(n_empty), nblk, k_pad,
                                        bs, ptr(k_dev), ptr(active), ptr(converged), ptr(iters_run), ptr(moved),
-                                       ptr(nempty_hist), it, ptr(C), s))
-        flag.copy_(active.max().reshape(1), non_blocking=True)
+                                       ptr(nempty_hist), it, ptr(C), ptr(inc.changed) if inc else None, s))
+        if inc is not None:
+            T.run("moved_lists", lambda: inc.lists(ran, k_dev))
+        act_host.copy_(active, non_blocking=True)
         torch.cuda.current_stream().synchronize()
-        if int(flag.item()) == 0:
+        act = act_host.numpy().astype(bool)
+        if not act.any():
             break
     _lib.poll_device_error()
     # final assignment with the final centroids (kmeans.py:190 / 246)
     call("skcq_pack_centroids", metric, ptr(C), nblk, k_pad, bs, ptr(k_dev), None, ptr(B), ptr(cnorm), s)
-    work = 2.0 * bs * float(nk.sum())
-    T.run("assign", lambda: assign_call(pts, B, C, cnorm, k_pad, k_dev, None, labels), work, work * kp / bs,
-          4.0 * kp * nblk * (n_pad + k_pad))
+    every = np.array(n_all) > 0
+    plan = inc.plan(every) if inc is not None and max_iters > 0 else None
+    if plan is None:
+        work = 2.0 * bs * float(nk.sum())
+        T.run("assign", lambda: assign_call(pts, B, C, cnorm, k_pad, k_dev, None, labels), work, work * kp / bs,
+              4.0 * kp * nblk * (n_pad + k_pad))
+    else:
+        m_pad, p_pad, work = plan
+        T.run("assign", lambda: inc.assign(B, C, cnorm, k_dev, None, m_pad, p_pad), work, work * kp / bs,
+              4.0 * kp * nblk * (n_pad + m_pad + p_pad + k_pad))
     return KmeansRun(
         C=C, k_pad=k_pad, k_host=k_host, labels=labels,
         iters_run=[int(v) for v in iters_run.cpu().tolist()],

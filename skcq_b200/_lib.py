@@ -53,7 +53,12 @@ _SIGS: dict[str, list] = {
     "skcq_reseed": [I, P, P, P, I, I, I, I, P, P, P, P, P, P, P, P],
     "skcq_reseed_noalloc": [I, P, P, P, I, I, I, I, P, P, P, P, P, P, P],
     "skcq_reseed_candidates": [I, P, P, P, I, I, I, I, P, P, P, P, P, I, P, P, P, P, P],
-    "skcq_finalize": [I, P, P, P, I, I, I, P, P, P, P, P, P, I, P, P],
+    "skcq_finalize": [I, P, P, P, I, I, I, P, P, P, P, P, P, I, P, P, P],
+    "skcq_mark_changed": [P, P, I, I, I, P, P, I, P, P],
+    "skcq_moved_lists_scratch_bytes": [I, I, I],
+    "skcq_moved_lists": [P, P, I, I, I, P, P, P, P, P, P, P, P, C.c_size_t, P],
+    "skcq_gather_rows": [P, I, P, I, P, I, I, I, P, P],
+    "skcq_assign_merge": [I, P, P, P, I, I, I, I, P, P, P, P, P, P, P, P, I, P, P, P],
     "skcq_flip_check": [P, P, P, I, I, I, I, P, P, P],
     "skcq_apply_flip": [P, I, I, I, P, P],
     "skcq_scatter_labels": [P, P, P, I, I, I, I, I, P, P],
@@ -92,7 +97,8 @@ _SIGS: dict[str, list] = {
     "skcq_ep_return": [P, I, I, L, P, P, P, P, P, P, I, I, I, I, I, I, I, I, P],
     "skcq_ep_gather": [P, P, I, I, I, I, I, I, P, I, P],
 }
-_RESTYPES = {"skcq_reseed_scratch_bytes": C.c_size_t, "skcq_route_sort_scratch_bytes": C.c_size_t}
+_RESTYPES = {"skcq_reseed_scratch_bytes": C.c_size_t, "skcq_route_sort_scratch_bytes": C.c_size_t,
+             "skcq_moved_lists_scratch_bytes": C.c_size_t}
 
 _lib: C.CDLL | None = None
 
@@ -137,6 +143,7 @@ _KERNELS_PER_CALL = {
     "skcq_lut_build": 1, "skcq_selftest_wait_timeout": 1,
     "skcq_route_sort": 1, "skcq_sum_splits": 1, "skcq_swiglu": 1, "skcq_combine": 1,
     "skcq_prefill_plan": 1, "skcq_prefill_pack": 1, "skcq_prefill_dequant": 1, "skcq_prefill_gemm": 1,
+    "skcq_mark_changed": 2, "skcq_moved_lists": 4, "skcq_gather_rows": 1, "skcq_assign_merge": 2,
     "skcq_prefill_gemm_swiglu": 1, "skcq_ep_dispatch": 3, "skcq_ep_unpack": 1, "skcq_ep_return": 1,
     "skcq_ep_gather": 1,
 }

@@ -1,0 +1,298 @@
+// Incremental Lloyd assignment: after the first iterations most clusters keep
+// their members, so most centroids keep their exact value, and a point's
+// nearest centroid can only change if its own centroid moved or a moved
+// centroid now beats it.
+//
+// Exactness. The Lloyd update (kmeans.py:152-188, 210-244) computes each
+// centroid from its members only, so a cluster whose member set did not change
+// since the previous update gets the same value again; skcq_finalize with a
+// `changed` mask keeps such centroids bit for bit. With X and those centroids
+// unchanged, every score of an unmoved centroid is bit-identical to the
+// previous assignment's, so for a point whose assigned centroid a did not
+// move, the new arg-max over all K centroids (first maximum wins) is a, or the
+// best moved centroid if that one scores higher, or scores the same with a
+// lower index. Points whose own centroid moved are re-assigned over all K.
+//
+// Kernels here:
+//   mark_changed   changed[b][c] = 1 for every cluster that gained or lost a
+//                  point between two assignments (or all, on the first)
+//   moved_lists    ascending lists of the moved centroids and of the points
+//                  assigned to one, per problem
+//   gather_rows    dst[b][j] = src[b][idx[b][j]] (moved centroids, flagged points)
+//   assign_merge   per point: keep a, or take the best moved centroid, or the
+//                  full re-assignment of a flagged point
+// The two tensor-core passes in between (moved centroids for all points; all
+// centroids for the flagged points) are skcq_assign calls by the host.
+#include "common.cuh"
+
+namespace skcq {
+
+constexpr int MC_THREADS = 256;
+constexpr int CP_THREADS = 1024;
+constexpr int CP_ITEMS = 4;  // consecutive items per thread
+constexpr int CP_CHUNK = CP_THREADS * CP_ITEMS;
+
+__global__ void mark_reset_kernel(int nblk, int k_pad, const int32_t* __restrict__ mask, int all,
+                                  uint8_t* __restrict__ changed) {
+  const int b = blockIdx.y;
+  if (mask && !mask[b]) return;
+  uint8_t* row = changed + (int64_t)b * k_pad;
+  for (int c = blockIdx.x * MC_THREADS + threadIdx.x; c < k_pad; c += gridDim.x * MC_THREADS) row[c] = all ? 1 : 0;
+}
+
+__global__ void mark_diff_kernel(const int32_t* __restrict__ prev, const int32_t* __restrict__ labels, int n_pad,
+                                 int k_pad, const int32_t* __restrict__ n, const int32_t* __restrict__ mask,
+                                 uint8_t* __restrict__ changed, int* err) {
+  const int b = blockIdx.y;
+  if (mask && !mask[b]) return;
+  const int nb = n[b];
+  uint8_t* row = changed + (int64_t)b * k_pad;
+  const int32_t* P = prev + (int64_t)b * n_pad;
+  const int32_t* L = labels + (int64_t)b * n_pad;
+  for (int i = blockIdx.x * MC_THREADS + threadIdx.x; i < nb; i += gridDim.x * MC_THREADS) {
+    const int p = P[i], l = L[i];
+    if (p == l) continue;
+    if (p < 0 || p >= k_pad || l < 0 || l >= k_pad) {
+      atomicCAS(err, 0, 71);
+      continue;
+    }
+    row[p] = 1;  // plain stores of the same value: no ordering needed
+    row[l] = 1;
+  }
+}
+
+// flag of item i of problem b: centroid lists (which == 0) or point lists
+__device__ __forceinline__ bool cp_flag(int which, int b, int i, int n_pad, int k_pad, const int32_t* n,
+                                        const int32_t* k, const uint8_t* changed, const int32_t* labels) {
+  const uint8_t* row = changed + (int64_t)b * k_pad;
+  if (which == 0) return i < k[b] && row[i];
+  if (i >= n[b]) return false;
+  const int l = labels[(int64_t)b * n_pad + i];
+  return l >= 0 && l < k_pad && row[l];
+}
+
+// cnt[b][chunk] = flagged items of the chunk
+__global__ void __launch_bounds__(CP_THREADS) cp_count_kernel(int which, int items, int n_pad, int k_pad,
+                                                              const int32_t* __restrict__ n,
+                                                              const int32_t* __restrict__ k,
+                                                              const int32_t* __restrict__ mask,
+                                                              const uint8_t* __restrict__ changed,
+                                                              const int32_t* __restrict__ labels, int n_chunks,
+                                                              int32_t* __restrict__ cnt) {
+  const int b = blockIdx.y;
+  if (mask && !mask[b]) return;
+  const int i0 = blockIdx.x * CP_CHUNK + threadIdx.x * CP_ITEMS;
+  int c = 0;
+#pragma unroll
+  for (int j = 0; j < CP_ITEMS; ++j)
+    if (i0 + j < items && cp_flag(which, b, i0 + j, n_pad, k_pad, n, k, changed, labels)) ++c;
+  int tot;
+  block_exclusive_scan(c, &tot);
+  if (threadIdx.x == 0) cnt[(int64_t)b * n_chunks + blockIdx.x] = tot;
+}
+
+// list[b][pos] = i for the flagged items in ascending order; count[b] = total
+__global__ void __launch_bounds__(CP_THREADS) cp_place_kernel(int which, int items, int n_pad, int k_pad,
+                                                              const int32_t* __restrict__ n,
+                                                              const int32_t* __restrict__ k,
+                                                              const int32_t* __restrict__ mask,
+                                                              const uint8_t* __restrict__ changed,
+                                                              const int32_t* __restrict__ labels, int n_chunks,
+                                                              const int32_t* __restrict__ cnt, int list_ld,
+                                                              int32_t* __restrict__ list, int32_t* __restrict__ count) {
+  __shared__ int s_base;
+  const int b = blockIdx.y;
+  if (mask && !mask[b]) return;
+  if (threadIdx.x == 0) {
+    int s = 0;
+    for (int c = 0; c < (int)blockIdx.x; ++c) s += cnt[(int64_t)b * n_chunks + c];
+    s_base = s;
+  }
+  const int i0 = blockIdx.x * CP_CHUNK + threadIdx.x * CP_ITEMS;
+  bool f[CP_ITEMS];
+  int c = 0;
+#pragma unroll
+  for (int j = 0; j < CP_ITEMS; ++j) {
+    f[j] = i0 + j < items && cp_flag(which, b, i0 + j, n_pad, k_pad, n, k, changed, labels);
+    c += f[j] ? 1 : 0;
+  }
+  int tot;
+  const int off = block_exclusive_scan(c, &tot);  // synchronises, so s_base is visible
+  int pos = s_base + off;
+  int32_t* out = list + (int64_t)b * list_ld;
+#pragma unroll
+  for (int j = 0; j < CP_ITEMS; ++j)
+    if (f[j]) out[pos++] = i0 + j;
+  if (blockIdx.x == gridDim.x - 1 && threadIdx.x == 0) count[b] = s_base + tot;
+}
+
+__global__ void gather_rows_kernel(const float* __restrict__ src, int src_rows, const int32_t* __restrict__ idx,
+                                   int idx_ld, const int32_t* __restrict__ count, int out_rows, int bs,
+                                   float* __restrict__ dst, int* err) {
+  const int b = blockIdx.y;
+  const int cb = count[b];
+  const float* S = src + (int64_t)b * src_rows * bs;
+  float* D = dst + (int64_t)b * out_rows * bs;
+  const int64_t total = (int64_t)out_rows * bs;
+  for (int64_t e = blockIdx.x * (int64_t)MC_THREADS + threadIdx.x; e < total; e += (int64_t)gridDim.x * MC_THREADS) {
+    const int j = (int)(e / bs), d = (int)(e - (int64_t)j * bs);
+    float v = 0.f;
+    if (j < cb) {
+      const int r = idx[(int64_t)b * idx_ld + j];
+      if (r >= 0 && r < src_rows)
+        v = S[(int64_t)r * bs + d];
+      else
+        atomicCAS(err, 0, 72);
+    }
+    D[e] = v;
+  }
+}
+
+// The reference score of point x against centroid c, computed exactly as the
+// assignment's re-score does (sequential FMAs; euclidean -(||c||^2 - 2 x.c)),
+// NaN as -inf and -0 as +0.
+__device__ __forceinline__ uint32_t exact_key(int metric, const float* x, const float* c, float cn, int bs) {
+  float dot = 0.f;
+  for (int j = 0; j < bs; ++j) dot = __fmaf_rn(x[j], c[j], dot);
+  float sc = metric == SKCQ_METRIC_COSINE ? dot : -__fadd_rn(__fmul_rn(dot, -2.0f), cn);
+  if (sc != sc) sc = -INFINITY;
+  return float_key(sc + 0.0f);
+}
+
+__global__ void assign_merge_kernel(int metric, const float* __restrict__ X, const float* __restrict__ C,
+                                    const float* __restrict__ cnorm, int n_pad, int k_pad, int bs,
+                                    const int32_t* __restrict__ n, const int32_t* __restrict__ active,
+                                    const uint8_t* __restrict__ changed, const int32_t* __restrict__ mlist,
+                                    const int32_t* __restrict__ mcount, const int32_t* __restrict__ labels_m,
+                                    const int32_t* __restrict__ plist, const int32_t* __restrict__ pcount, int p_pad,
+                                    const int32_t* __restrict__ labels_f, int32_t* __restrict__ labels, int phase,
+                                    int* err) {
+  const int b = blockIdx.y;
+  if (active && !active[b]) return;
+  const int nb = n[b], mb = mcount[b], pb = pcount[b];
+  const uint8_t* row = changed + (int64_t)b * k_pad;
+  const float* Xb = X + (int64_t)b * n_pad * bs;
+  const float* Cb = C + (int64_t)b * k_pad * bs;
+  const float* Nb = cnorm + (int64_t)b * k_pad;
+  int32_t* Lb = labels + (int64_t)b * n_pad;
+  const int lim = nb > pb ? nb : pb;
+  for (int i = blockIdx.x * MC_THREADS + threadIdx.x; i < lim; i += gridDim.x * MC_THREADS) {
+    if (phase == 0 && i < nb) {
+      const int a = Lb[i];
+      if (a < 0 || a >= k_pad) {
+        atomicCAS(err, 0, 73);
+      } else if (!row[a] && mb > 0) {
+        const int w = labels_m[(int64_t)b * n_pad + i];
+        if (w < 0 || w >= mb) {
+          atomicCAS(err, 0, 74);
+        } else {
+          const int cand = mlist[(int64_t)b * k_pad + w];
+          if (cand < 0 || cand >= k_pad) {
+            atomicCAS(err, 0, 74);
+          } else {
+            const float* x = Xb + (int64_t)i * bs;
+            const uint32_t ka = exact_key(metric, x, Cb + (int64_t)a * bs, Nb[a], bs);
+            const uint32_t kc = exact_key(metric, x, Cb + (int64_t)cand * bs, Nb[cand], bs);
+            if (kc > ka || (kc == ka && cand < a)) Lb[i] = cand;
+          }
+        }
+      }
+    }
+    if (phase == 1 && i < pb) {  // a point whose centroid moved: its full re-assignment
+      const int r = plist[(int64_t)b * n_pad + i];
+      if (r < 0 || r >= nb)
+        atomicCAS(err, 0, 75);
+      else
+        Lb[r] = labels_f[(int64_t)b * p_pad + i];
+    }
+  }
+}
+
+static int row_grid(int64_t work, int threads) {
+  int64_t g = (work + threads - 1) / threads;
+  if (g > 64) g = 64;
+  return (int)(g < 1 ? 1 : g);
+}
+
+}  // namespace skcq
+
+using namespace skcq;
+
+extern "C" int skcq_mark_changed(const int32_t* prev, const int32_t* labels, int nblk, int n_pad, int k_pad,
+                                 const int32_t* n, const int32_t* mask, int all, uint8_t* changed, void* stream) {
+  SKCQ_REQUIRE(changed && n && (all || (prev && labels)), SKCQ_ERR_INVALID, "mark_changed: null pointer");
+  SKCQ_REQUIRE(nblk > 0 && nblk <= 65535 && n_pad > 0 && k_pad > 0, SKCQ_ERR_INVALID, "mark_changed: bad sizes");
+  int* err = device_error_word();
+  SKCQ_REQUIRE(err != nullptr, SKCQ_ERR_CUDA, "mark_changed: no device error word");
+  cudaStream_t s = (cudaStream_t)stream;
+  mark_reset_kernel<<<dim3(row_grid(k_pad, MC_THREADS), nblk), MC_THREADS, 0, s>>>(nblk, k_pad, mask, all, changed);
+  if (!all)
+    mark_diff_kernel<<<dim3(row_grid(n_pad, MC_THREADS), nblk), MC_THREADS, 0, s>>>(prev, labels, n_pad, k_pad, n,
+                                                                                  mask, changed, err);
+  return check_launch("mark_changed");
+}
+
+extern "C" size_t skcq_moved_lists_scratch_bytes(int nblk, int n_pad, int k_pad) {
+  if (nblk <= 0 || n_pad <= 0 || k_pad <= 0) return 0;
+  const int64_t chunks = ceil_div64(n_pad, CP_CHUNK) + ceil_div64(k_pad, CP_CHUNK);
+  return (size_t)nblk * (size_t)chunks * sizeof(int32_t);
+}
+
+extern "C" int skcq_moved_lists(const uint8_t* changed, const int32_t* labels, int nblk, int n_pad, int k_pad,
+                                const int32_t* n, const int32_t* k, const int32_t* mask, int32_t* mlist,
+                                int32_t* mcount, int32_t* plist, int32_t* pcount, void* scratch,
+                                size_t scratch_bytes, void* stream) {
+  SKCQ_REQUIRE(changed && labels && n && k && mlist && mcount && plist && pcount && scratch, SKCQ_ERR_INVALID,
+               "moved_lists: null pointer");
+  SKCQ_REQUIRE(nblk > 0 && nblk <= 65535 && n_pad > 0 && k_pad > 0, SKCQ_ERR_INVALID, "moved_lists: bad sizes");
+  SKCQ_REQUIRE(scratch_bytes >= skcq_moved_lists_scratch_bytes(nblk, n_pad, k_pad), SKCQ_ERR_INVALID,
+               "moved_lists: scratch of %zu bytes, %zu needed", scratch_bytes,
+               skcq_moved_lists_scratch_bytes(nblk, n_pad, k_pad));
+  cudaStream_t s = (cudaStream_t)stream;
+  const int kc = (int)ceil_div64(k_pad, CP_CHUNK), nc = (int)ceil_div64(n_pad, CP_CHUNK);
+  int32_t* cnt_k = static_cast<int32_t*>(scratch);
+  int32_t* cnt_n = cnt_k + (int64_t)nblk * kc;
+  cp_count_kernel<<<dim3(kc, nblk), CP_THREADS, 0, s>>>(0, k_pad, n_pad, k_pad, n, k, mask, changed, labels, kc,
+                                                         cnt_k);
+  cp_place_kernel<<<dim3(kc, nblk), CP_THREADS, 0, s>>>(0, k_pad, n_pad, k_pad, n, k, mask, changed, labels, kc,
+                                                         cnt_k, k_pad, mlist, mcount);
+  cp_count_kernel<<<dim3(nc, nblk), CP_THREADS, 0, s>>>(1, n_pad, n_pad, k_pad, n, k, mask, changed, labels, nc,
+                                                         cnt_n);
+  cp_place_kernel<<<dim3(nc, nblk), CP_THREADS, 0, s>>>(1, n_pad, n_pad, k_pad, n, k, mask, changed, labels, nc,
+                                                         cnt_n, n_pad, plist, pcount);
+  return check_launch("moved_lists");
+}
+
+extern "C" int skcq_gather_rows(const float* src, int src_rows, const int32_t* idx, int idx_ld, const int32_t* count,
+                                int nblk, int out_rows, int bs, float* dst, void* stream) {
+  SKCQ_REQUIRE(src && idx && count && dst, SKCQ_ERR_INVALID, "gather_rows: null pointer");
+  SKCQ_REQUIRE(nblk > 0 && nblk <= 65535 && src_rows > 0 && out_rows > 0 && bs > 0 && idx_ld >= out_rows,
+               SKCQ_ERR_INVALID, "gather_rows: bad sizes");
+  int* err = device_error_word();
+  SKCQ_REQUIRE(err != nullptr, SKCQ_ERR_CUDA, "gather_rows: no device error word");
+  gather_rows_kernel<<<dim3(row_grid((int64_t)out_rows * bs, MC_THREADS), nblk), MC_THREADS, 0,
+                       (cudaStream_t)stream>>>(src, src_rows, idx, idx_ld, count, out_rows, bs, dst, err);
+  return check_launch("gather_rows");
+}
+
+extern "C" int skcq_assign_merge(int metric, const float* X, const float* C, const float* cnorm, int nblk, int n_pad,
+                                 int k_pad, int bs, const int32_t* n, const int32_t* active, const uint8_t* changed,
+                                 const int32_t* mlist, const int32_t* mcount, const int32_t* labels_m,
+                                 const int32_t* plist, const int32_t* pcount, int p_pad, const int32_t* labels_f,
+                                 int32_t* labels, void* stream) {
+  SKCQ_REQUIRE(X && C && cnorm && n && changed && mlist && mcount && labels_m && plist && pcount && labels &&
+                   (p_pad == 0 || labels_f),
+               SKCQ_ERR_INVALID, "assign_merge: null pointer");
+  SKCQ_REQUIRE(metric == SKCQ_METRIC_COSINE || metric == SKCQ_METRIC_L2, SKCQ_ERR_INVALID, "assign_merge: metric");
+  SKCQ_REQUIRE(nblk > 0 && nblk <= 65535 && n_pad > 0 && k_pad > 0 && bs > 0 && p_pad >= 0 && p_pad <= n_pad,
+               SKCQ_ERR_INVALID, "assign_merge: bad sizes");
+  int* err = device_error_word();
+  SKCQ_REQUIRE(err != nullptr, SKCQ_ERR_CUDA, "assign_merge: no device error word");
+  // phase 0 reads every point's previous label before phase 1 overwrites the
+  // flagged ones
+  for (int phase = 0; phase < 2; ++phase)
+    assign_merge_kernel<<<dim3(row_grid(n_pad, MC_THREADS), nblk), MC_THREADS, 0, (cudaStream_t)stream>>>(
+        metric, X, C, cnorm, n_pad, k_pad, bs, n, active, changed, mlist, mcount, labels_m, plist, pcount, p_pad,
+        labels_f, labels, phase, err);
+  return check_launch("assign_merge");
+}

@@ -309,7 +309,7 @@ __global__ void finalize_kernel(int metric, float* __restrict__ sums, int32_t* _
                                 const int32_t* __restrict__ kvec, int32_t* __restrict__ active,
                                 int32_t* __restrict__ converged, int32_t* __restrict__ iters_run,
                                 float* __restrict__ moved_hist, int32_t* __restrict__ nempty_hist, int iter,
-                                float* __restrict__ C) {
+                                float* __restrict__ C, uint8_t* __restrict__ changed) {
   for (int b = blockIdx.x; b < nblk; b += gridDim.x) {
     if (!active[b]) continue;
     const int kb = kvec[b];
@@ -321,6 +321,16 @@ __global__ void finalize_kernel(int metric, float* __restrict__ sums, int32_t* _
       float* s = Sb + (int64_t)c * bs;
       float* cc = Cb + (int64_t)c * bs;
       const int cnt = Nb[c];
+      if (changed) {
+        uint8_t& ch = changed[(int64_t)b * k_pad + c];
+        if (cnt > 0 && !ch) {
+          // same members as at the previous update: the same centroid, kept bit for bit
+          for (int j = 0; j < bs; ++j) s[j] = 0.f;
+          Nb[c] = 0;
+          continue;
+        }
+        ch = 1;  // recomputed (or reseeded): moved for the next assignment
+      }
       float den;
       if (metric == SKCQ_METRIC_COSINE) {
         float q = 0.f;
@@ -460,12 +470,14 @@ extern "C" int skcq_reseed_candidates(int metric, const float* X, const float* C
 
 extern "C" int skcq_finalize(int metric, float* sums, int32_t* counts, const int32_t* n_empty, int nblk, int k_pad,
                              int bs, const int32_t* k, int32_t* active, int32_t* converged, int32_t* iters_run,
-                             float* moved_hist, int32_t* nempty_hist, int iter, float* C, void* stream) {
+                             float* moved_hist, int32_t* nempty_hist, int iter, float* C, uint8_t* changed,
+                             void* stream) {
   SKCQ_REQUIRE(sums && counts && n_empty && k && active && converged && iters_run && moved_hist && nempty_hist && C,
                SKCQ_ERR_INVALID, "finalize: null pointer");
   int grid = nblk < 1024 ? nblk : 1024;
   finalize_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(metric, sums, counts, n_empty, nblk, k_pad, bs, k, active,
-                                                          converged, iters_run, moved_hist, nempty_hist, iter, C);
+                                                          converged, iters_run, moved_hist, nempty_hist, iter, C,
+                                                          changed);
   return check_launch("finalize");
 }
 
