@@ -117,8 +117,10 @@ INCREMENTAL_CHECK: Callable | None = None
 
 # The incremental assignment replaces a full pass when its two tensor-core
 # passes cover fewer than this share of the full pass's (256-point unit x
-# 128-centroid tile) products.
-INCREMENTAL_MAX_SHARE = 0.8
+# 128-centroid tile) products. Measured on B200 (one projection of the
+# benchmark layer): an incremental assignment costs about 0.4 of a full pass
+# plus its share of it at K = 4096, so it pays below a share of about 0.55-0.65.
+INCREMENTAL_MAX_SHARE = 0.55
 
 
 class IncrementalAssign:
@@ -179,6 +181,48 @@ class IncrementalAssign:
         p_pad = int(np.ceil(p[act].max() / ROWS_PER_UNIT)) * ROWS_PER_UNIT if p[act].max() > 0 else 0
         work = 2.0 * self.pts.bs * float((self.n_host * m + p * self.k_host)[act].sum())
         return m_pad, p_pad, work
+
+    def first_from_seeds(self, C: torch.Tensor, perm: torch.Tensor, k_dev: torch.Tensor) -> tuple[int, float]:
+        """First assignment of a Forgy start (euclidean centroids are points
+        X[perm[c]]): a seed point's own centroid is at distance 0, so it is the
+        point's nearest centroid unless another centroid lies within rounding of
+        it (a tie below the reference's rounding) or has the identical value (an
+        exact tie, which the first index wins). Seeds whose value occurs once get
+        their own index; every other point (and every seed with a duplicate,
+        detected by hashing the centroid bits) is listed for a search over all
+        centroids. Returns (p_pad, algorithmic work) for ``assign`` with no
+        moved centroids."""
+        pts, dev = self.pts, self.pts.X.device
+        nblk, k_pad = pts.nblk, self.k_pad
+        c_idx = torch.arange(k_pad, device=dev)
+        # equal centroid values have equal keys; different values sharing a
+        # key only send more seeds to the full search
+        valid = c_idx[None, :] < k_dev[:, None].long()
+        bits = (C + 0.0).view(torch.int32).long() & 0xFFFFFFFF  # -0 and +0 alike
+        mult = torch.tensor([0x9E3779B97F4A7C15 - (1 << 64), 0xC2B2AE3D27D4EB4F - (1 << 64),
+                             0x165667B19E3779F9, 0x27D4EB2F165667C5] * ((pts.bs + 3) // 4),
+                            dtype=torch.int64, device=dev)[:pts.bs]
+        h = (bits * mult).sum(-1)  # wraps modulo 2^64
+        h = torch.where(valid, h, -(c_idx[None, :].long() + 1) * 0x100000001)  # padding: distinct keys
+        hs, order = torch.sort(h, dim=1)
+        eq = hs[:, 1:] == hs[:, :-1]
+        dup_sorted = torch.zeros_like(hs, dtype=torch.bool)
+        dup_sorted[:, 1:] |= eq
+        dup_sorted[:, :-1] |= eq
+        dup = torch.zeros_like(dup_sorted).scatter_(1, order, dup_sorted)
+        own = valid & ~dup  # seeds that take their own index
+        b_idx = torch.arange(nblk, device=dev)[:, None].expand(-1, k_pad)[own]
+        p_idx = perm[:, :k_pad][own]
+        self.labels[b_idx, p_idx] = c_idx[None, :].expand(nblk, -1)[own].to(torch.int32)
+        covered = torch.zeros(nblk, pts.n_pad, dtype=torch.bool, device=dev)
+        covered[b_idx, p_idx] = True
+        need = (torch.arange(pts.n_pad, device=dev)[None, :] < pts.n[:, None].long()) & ~covered
+        self.plist.copy_(torch.argsort((~need).to(torch.int8), dim=1, stable=True).to(torch.int32))
+        self.counts[0].zero_()
+        self.counts[1].copy_(need.sum(1).to(torch.int32))
+        p_host = self.counts[1].cpu().numpy().astype(np.float64)
+        p_pad = int(np.ceil(p_host.max() / ROWS_PER_UNIT)) * ROWS_PER_UNIT if p_host.max() > 0 else 0
+        return p_pad, 2.0 * pts.bs * float((p_host * self.k_host).sum())
 
     def assign(self, B, C, cnorm, k_dev, active, m_pad: int, p_pad: int) -> None:
         """Labels of the problems in ``active`` (None: all) from the previous
@@ -310,6 +354,7 @@ def lloyd(
     """
     dev = pts.X.device
     nblk, bs, n_pad, metric = pts.nblk, pts.bs, pts.n_pad, pts.metric
+    forgy = False
     n_all = [int(v) for v in n_global.tolist()] if shard is not None else pts.n_host
     k_host = [min(K, nb) for nb in n_all]
     k_pad = round_up(max(k_host + [1]), CENT_TILE)
@@ -327,6 +372,7 @@ def lloyd(
                 C[b, :kb] = cache[kb]
     else:
         perm = torch.zeros(nblk, k_pad, dtype=torch.int64, device=dev)
+        forgy = True
         for b, kb in enumerate(k_host):
             if kb > 0:
                 perm[b, :kb] = init_perms[b][:kb].to(dev)
@@ -362,7 +408,11 @@ def lloyd(
         plan = inc.plan(act) if inc is not None else None
         if inc is not None:
             inc.prev.copy_(labels)
-        if plan is None:
+        if it == 0 and inc is not None and forgy:
+            p_pad, work = inc.first_from_seeds(C, perm, k_dev)
+            nbytes = 4.0 * kp * float(act.sum()) * (p_pad + k_pad)
+            T.run("assign", lambda: inc.assign(B, C, cnorm, k_dev, active, 0, p_pad), work, work * kp / bs, nbytes)
+        elif plan is None:
             # algorithmic work: 2*n*k*bs flops over the active problems
             work = 2.0 * bs * float(nk[act].sum())
             # the split operands each active problem's tensor-core pass reads once
