@@ -220,6 +220,16 @@ int skcq_moved_lists(const uint8_t* changed, const int32_t* labels, int nblk, in
 int skcq_gather_rows(const float* src, int src_rows, const int32_t* idx, int idx_ld, const int32_t* count, int nblk,
                      int out_rows, int bs, float* dst, void* stream);
 
+/* In place on labels, for the active problems with a moved list: a point whose
+ * centroid a did not move takes the best of mlist[b][0 .. mcount[b]) under
+ * the reference formula (exact fp32 on CUDA cores, first maximum) when it
+ * scores higher than a, or the same with a lower index. For short moved lists
+ * (bs <= 32); replaces the tensor-core pass over the gathered moved centroids
+ * and the first half of skcq_assign_merge (call that with zero mcount). */
+int skcq_assign_moved_exact(int metric, const float* X, const float* C, const float* cnorm, int nblk, int n_pad,
+                            int k_pad, int bs, const int32_t* n, const int32_t* active, const uint8_t* changed,
+                            const int32_t* mlist, const int32_t* mcount, int32_t* labels, void* stream);
+
 /* In place on labels (the previous assignment) for the active problems: a
  * point whose centroid a did not move (changed[b][a] == 0) takes
  * c = mlist[b][labels_m[b][i]] (the best moved centroid; labels_m from

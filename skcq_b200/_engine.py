@@ -121,6 +121,9 @@ INCREMENTAL_CHECK: Callable | None = None
 # benchmark layer): an incremental assignment costs about 0.4 of a full pass
 # plus its share of it at K = 4096, so it pays below a share of about 0.55-0.65.
 INCREMENTAL_MAX_SHARE = 0.55
+# Moved lists of at most this many centroids (per problem) are scored with the
+# exact formula on CUDA cores instead of a tensor-core pass over them.
+EXACT_MOVED_MAX = 256
 
 
 class IncrementalAssign:
@@ -168,7 +171,9 @@ class IncrementalAssign:
     def plan(self, act: np.ndarray) -> tuple[int, int, float] | None:
         """(m_pad, p_pad, algorithmic work) of an incremental assignment of the
         problems in ``act`` (host bool mask), or None when a full pass is cheaper.
-        Reads the counts of the last ``lists`` (the caller synchronised)."""
+        Reads the counts of the last ``lists`` (the caller synchronised). m_pad
+        is 0 when no problem has a moved centroid, negative when every moved
+        list is short enough for the exact CUDA-core pass."""
         if not self.listed or not act.any():
             return None
         m = self.counts_host[0].numpy().astype(np.float64)
@@ -178,6 +183,8 @@ class IncrementalAssign:
         if full <= 0 or inc >= INCREMENTAL_MAX_SHARE * full:
             return None
         m_pad = int(np.ceil(m[act].max() / CENT_TILE)) * CENT_TILE if m[act].max() > 0 else 0
+        if 0 < m[act].max() <= EXACT_MOVED_MAX and self.pts.bs <= 32:
+            m_pad = -m_pad
         p_pad = int(np.ceil(p[act].max() / ROWS_PER_UNIT)) * ROWS_PER_UNIT if p[act].max() > 0 else 0
         work = 2.0 * self.pts.bs * float((self.n_host * m + p * self.k_host)[act].sum())
         return m_pad, p_pad, work
@@ -231,7 +238,13 @@ class IncrementalAssign:
         act = active if active is not None else torch.ones(pts.nblk, dtype=torch.int32, device=dev)
         mcount, pcount = self.counts[0], self.counts[1]
         labels_m = torch.zeros(1, dtype=torch.int32, device=dev)
-        if m_pad > 0:  # every point against the moved centroids
+        merge_m = mcount
+        if m_pad < 0:  # short moved lists: exact scores on CUDA cores, merged in place
+            call("skcq_assign_moved_exact", pts.metric, ptr(pts.X), ptr(C), ptr(cnorm), pts.nblk, pts.n_pad,
+                 self.k_pad, pts.bs, ptr(pts.n), ptr(active), ptr(self.changed), ptr(self.mlist), ptr(mcount),
+                 ptr(self.labels), s)
+            merge_m = torch.zeros_like(mcount)
+        elif m_pad > 0:  # every point against the moved centroids
             Cm = torch.empty(pts.nblk, m_pad, pts.bs, dtype=torch.float32, device=dev)
             call("skcq_gather_rows", ptr(C), self.k_pad, ptr(self.mlist), self.k_pad, ptr(mcount), pts.nblk, m_pad,
                  pts.bs, ptr(Cm), s)
@@ -252,7 +265,7 @@ class IncrementalAssign:
             labels_f = torch.zeros(pts.nblk, p_pad, dtype=torch.int32, device=dev)
             assign_call(sub, B, C, cnorm, self.k_pad, k_dev, act_f, labels_f)
         call("skcq_assign_merge", pts.metric, ptr(pts.X), ptr(C), ptr(cnorm), pts.nblk, pts.n_pad, self.k_pad,
-             pts.bs, ptr(pts.n), ptr(active), ptr(self.changed), ptr(self.mlist), ptr(mcount), ptr(labels_m),
+             pts.bs, ptr(pts.n), ptr(active), ptr(self.changed), ptr(self.mlist), ptr(merge_m), ptr(labels_m),
              ptr(self.plist), ptr(pcount), p_pad, ptr(labels_f), ptr(self.labels), s)
         if INCREMENTAL_CHECK is not None:
             INCREMENTAL_CHECK(pts, B, C, cnorm, self.k_pad, k_dev, active, self.labels)
@@ -421,7 +434,7 @@ def lloyd(
                   work * kp / bs, nbytes)
         else:
             m_pad, p_pad, work = plan
-            nbytes = 4.0 * kp * float(act.sum()) * (n_pad + m_pad + p_pad + k_pad)
+            nbytes = 4.0 * kp * float(act.sum()) * (n_pad + abs(m_pad) + p_pad + k_pad)
             T.run("assign", lambda: inc.assign(B, C, cnorm, k_dev, active, m_pad, p_pad), work, work * kp / bs,
                   nbytes)
         if inc is not None:
@@ -457,7 +470,7 @@ def lloyd(
     else:
         m_pad, p_pad, work = plan
         T.run("assign", lambda: inc.assign(B, C, cnorm, k_dev, None, m_pad, p_pad), work, work * kp / bs,
-              4.0 * kp * nblk * (n_pad + m_pad + p_pad + k_pad))
+              4.0 * kp * nblk * (n_pad + abs(m_pad) + p_pad + k_pad))
     return KmeansRun(
         C=C, k_pad=k_pad, k_host=k_host, labels=labels,
         iters_run=[int(v) for v in iters_run.cpu().tolist()],

@@ -208,6 +208,105 @@ __global__ void assign_merge_kernel(int metric, const float* __restrict__ X, con
   }
 }
 
+// Every unflagged point (its centroid a did not move) against the moved
+// centroids of its problem, with the exact reference formula on CUDA cores:
+// the list is staged in shared memory in slices of MX_SLICE centroids, each
+// thread keeps the best (first maximum in list order, i.e. lowest index) and
+// then compares it with a. For short moved lists this replaces the
+// tensor-core pass over the gathered moved centroids and phase 0 of the merge.
+constexpr int MX_SLICE = 256;
+constexpr int MX_THREADS = 256;
+
+template <int BS>
+__global__ void __launch_bounds__(MX_THREADS) assign_moved_exact_kernel(
+    int metric, const float* __restrict__ X, const float* __restrict__ C, const float* __restrict__ cnorm, int n_pad,
+    int k_pad, int bs_rt, const int32_t* __restrict__ n, const int32_t* __restrict__ active,
+    const uint8_t* __restrict__ changed, const int32_t* __restrict__ mlist, const int32_t* __restrict__ mcount,
+    int32_t* __restrict__ labels, int* err) {
+  constexpr int XN = BS > 0 ? BS : 32;
+  const int bs = BS > 0 ? BS : bs_rt;
+  extern __shared__ float sm[];
+  float* tab = sm;                        // [MX_SLICE][bs]
+  float* cn = sm + MX_SLICE * bs;         // [MX_SLICE]
+  int* idx = reinterpret_cast<int*>(cn + MX_SLICE);  // [MX_SLICE]
+  const int b = blockIdx.y;
+  if (active && !active[b]) return;
+  const int nb = n[b], mb = mcount[b];
+  if (mb <= 0) return;
+  const uint8_t* row = changed + (int64_t)b * k_pad;
+  const float* Cb = C + (int64_t)b * k_pad * bs;
+  const float* Nb = cnorm + (int64_t)b * k_pad;
+  const int32_t* Mb = mlist + (int64_t)b * k_pad;
+  int32_t* Lb = labels + (int64_t)b * n_pad;
+  for (int i0 = blockIdx.x * MX_THREADS; i0 < nb; i0 += gridDim.x * MX_THREADS) {
+    const int i = i0 + threadIdx.x;
+    int a = -1;
+    float x[XN];
+    if (i < nb) {
+      a = Lb[i];
+      if (a < 0 || a >= k_pad) {
+        atomicCAS(err, 0, 73);
+        a = -1;
+      } else if (row[a]) {
+        a = -1;  // its centroid moved: re-assigned over all centroids elsewhere
+      }
+    }
+    if (a >= 0) {
+#pragma unroll
+      for (int j = 0; j < XN; ++j)
+        if (BS > 0 || j < bs) x[j] = X[((int64_t)b * n_pad + i) * bs + j];
+    }
+    uint32_t best = 0;
+    int best_c = -1;
+    for (int s0 = 0; s0 < mb; s0 += MX_SLICE) {
+      const int cnt = min(MX_SLICE, mb - s0);
+      __syncthreads();
+      for (int t = threadIdx.x; t < cnt; t += MX_THREADS) {
+        int c = Mb[s0 + t];
+        if (c < 0 || c >= k_pad) {
+          atomicCAS(err, 0, 74);
+          c = 0;
+        }
+        idx[t] = c;
+        cn[t] = Nb[c];
+      }
+      __syncthreads();
+      for (int e = threadIdx.x; e < cnt * bs; e += MX_THREADS) {
+        const int t = e / bs, j = e - t * bs;
+        tab[e] = Cb[(int64_t)idx[t] * bs + j];
+      }
+      __syncthreads();
+      if (a >= 0) {
+        for (int t = 0; t < cnt; ++t) {
+          const float* c = tab + t * bs;
+          float dot = 0.f;
+#pragma unroll
+          for (int j = 0; j < XN; ++j)
+            if (BS > 0 || j < bs) dot = __fmaf_rn(x[j], c[j], dot);
+          float sc = metric == SKCQ_METRIC_COSINE ? dot : -__fadd_rn(__fmul_rn(dot, -2.0f), cn[t]);
+          if (sc != sc) sc = -INFINITY;
+          const uint32_t key = float_key(sc + 0.0f);
+          if (best_c < 0 || key > best) {
+            best = key;
+            best_c = idx[t];
+          }
+        }
+      }
+    }
+    if (a >= 0 && best_c >= 0) {
+      const float* ca = Cb + (int64_t)a * bs;
+      float dot = 0.f;
+#pragma unroll
+      for (int j = 0; j < XN; ++j)
+        if (BS > 0 || j < bs) dot = __fmaf_rn(x[j], ca[j], dot);
+      float sc = metric == SKCQ_METRIC_COSINE ? dot : -__fadd_rn(__fmul_rn(dot, -2.0f), Nb[a]);
+      if (sc != sc) sc = -INFINITY;
+      const uint32_t ka = float_key(sc + 0.0f);
+      if (best > ka || (best == ka && best_c < a)) Lb[i] = best_c;
+    }
+  }
+}
+
 static int row_grid(int64_t work, int threads) {
   int64_t g = (work + threads - 1) / threads;
   if (g > 64) g = 64;
@@ -273,6 +372,39 @@ extern "C" int skcq_gather_rows(const float* src, int src_rows, const int32_t* i
   gather_rows_kernel<<<dim3(row_grid((int64_t)out_rows * bs, MC_THREADS), nblk), MC_THREADS, 0,
                        (cudaStream_t)stream>>>(src, src_rows, idx, idx_ld, count, out_rows, bs, dst, err);
   return check_launch("gather_rows");
+}
+
+extern "C" int skcq_assign_moved_exact(int metric, const float* X, const float* C, const float* cnorm, int nblk,
+                                       int n_pad, int k_pad, int bs, const int32_t* n, const int32_t* active,
+                                       const uint8_t* changed, const int32_t* mlist, const int32_t* mcount,
+                                       int32_t* labels, void* stream) {
+  SKCQ_REQUIRE(X && C && cnorm && n && changed && mlist && mcount && labels, SKCQ_ERR_INVALID,
+               "assign_moved_exact: null pointer");
+  SKCQ_REQUIRE(metric == SKCQ_METRIC_COSINE || metric == SKCQ_METRIC_L2, SKCQ_ERR_INVALID,
+               "assign_moved_exact: metric");
+  SKCQ_REQUIRE(nblk > 0 && nblk <= 65535 && n_pad > 0 && k_pad > 0 && bs > 0 && bs <= 32, SKCQ_ERR_INVALID,
+               "assign_moved_exact: bad sizes (block size %d, at most 32)", bs);
+  int* err = device_error_word();
+  SKCQ_REQUIRE(err != nullptr, SKCQ_ERR_CUDA, "assign_moved_exact: no device error word");
+  const size_t smem = (size_t)MX_SLICE * (bs + 2) * sizeof(float);
+  int64_t gx = (n_pad + MX_THREADS - 1) / MX_THREADS;
+  const int64_t want = (148 * 8 + nblk - 1) / nblk;  // about 8 CTAs per SM over all problems
+  if (gx > want) gx = want;
+  dim3 grid((unsigned)(gx < 1 ? 1 : gx), (unsigned)nblk);
+  cudaStream_t s = (cudaStream_t)stream;
+#define SKCQ_MX(BSV)                                                                                           \
+  assign_moved_exact_kernel<BSV><<<grid, MX_THREADS, smem, s>>>(metric, X, C, cnorm, n_pad, k_pad, bs, n, active, \
+                                                                changed, mlist, mcount, labels, err)
+  switch (bs) {
+    case 4: SKCQ_MX(4); break;
+    case 6: SKCQ_MX(6); break;
+    case 8: SKCQ_MX(8); break;
+    case 12: SKCQ_MX(12); break;
+    case 16: SKCQ_MX(16); break;
+    default: SKCQ_MX(0); break;
+  }
+#undef SKCQ_MX
+  return check_launch("assign_moved_exact");
 }
 
 extern "C" int skcq_assign_merge(int metric, const float* X, const float* C, const float* cnorm, int nblk, int n_pad,
