@@ -183,8 +183,9 @@ int skcq_reseed_candidates(int metric, const float* X, const float* C, const int
  * changed (optional, [nblk][k_pad] bytes from skcq_mark_changed): a non-empty
  * cluster with changed == 0 has the same members as at the previous update,
  * so its centroid is kept bit for bit (and adds 0 to moved); every centroid
- * that is recomputed or reseeded gets changed = 1, which tells the next
- * incremental assignment that it moved. */
+ * that is recomputed or reseeded gets changed = 1 if its value differs in any
+ * bit, else 0, which tells the next incremental assignment which centroids
+ * moved. */
 int skcq_finalize(int metric, float* sums, int32_t* counts, const int32_t* n_empty, int nblk, int k_pad, int bs,
                   const int32_t* k, int32_t* active, int32_t* converged, int32_t* iters_run, float* moved_hist,
                   int32_t* nempty_hist, int iter, float* C, uint8_t* changed, void* stream);
@@ -228,7 +229,16 @@ int skcq_gather_rows(const float* src, int src_rows, const int32_t* idx, int idx
  * and the first half of skcq_assign_merge (call that with zero mcount). */
 int skcq_assign_moved_exact(int metric, const float* X, const float* C, const float* cnorm, int nblk, int n_pad,
                             int k_pad, int bs, const int32_t* n, const int32_t* active, const uint8_t* changed,
-                            const int32_t* mlist, const int32_t* mcount, int32_t* labels, void* stream);
+                            const int32_t* mlist, const int32_t* mcount, int32_t* labels, const float* C_old,
+                            const float* cnorm_old, uint8_t* unres, void* stream);
+
+/* Resolution of the points whose centroid moved (both entry points above and
+ * below, when unres is not NULL): such a point takes the best moved centroid
+ * when its score exceeds the point's score against a's value before the
+ * update (C_old, cnorm_old: the centroids and norms that assignment used),
+ * since that score bounds every unmoved centroid's unchanged score; otherwise
+ * unres[b][i] = 1 and the point needs a search over all centroids (listed by
+ * skcq_list_points). unres is written for every point. */
 
 /* In place on labels (the previous assignment) for the active problems: a
  * point whose centroid a did not move (changed[b][a] == 0) takes
@@ -239,7 +249,14 @@ int skcq_assign_moved_exact(int metric, const float* X, const float* C, const fl
 int skcq_assign_merge(int metric, const float* X, const float* C, const float* cnorm, int nblk, int n_pad, int k_pad,
                       int bs, const int32_t* n, const int32_t* active, const uint8_t* changed, const int32_t* mlist,
                       const int32_t* mcount, const int32_t* labels_m, const int32_t* plist, const int32_t* pcount,
-                      int p_pad, const int32_t* labels_f, int32_t* labels, void* stream);
+                      int p_pad, const int32_t* labels_f, int32_t* labels, const float* C_old,
+                      const float* cnorm_old, uint8_t* unres, void* stream);
+
+/* plist[b][0 .. pcount[b]) = the points i < n[b] with flags[b][i] != 0,
+ * ascending, for the problems with mask[b] != 0 (flags [nblk][n_pad]);
+ * scratch: nblk * ceil(n_pad / 4096) ints. */
+int skcq_list_points(const uint8_t* flags, int nblk, int n_pad, const int32_t* n, const int32_t* mask,
+                     int32_t* plist, int32_t* pcount, void* scratch, size_t scratch_bytes, void* stream);
 
 /* ---- codec post-processing ------------------------------------------------- */
 

@@ -115,15 +115,21 @@ TC_MAX_KP = 64  # widest split operand the tensor-core kernel stages (bs <= 20)
 # k_dev, active, labels) when set; tests compare the labels with a full pass.
 INCREMENTAL_CHECK: Callable | None = None
 
-# The incremental assignment replaces a full pass when its two tensor-core
-# passes cover fewer than this share of the full pass's (256-point unit x
-# 128-centroid tile) products. Measured on B200 (one projection of the
-# benchmark layer): an incremental assignment costs about 0.4 of a full pass
-# plus its share of it at K = 4096, so it pays below a share of about 0.55-0.65.
-INCREMENTAL_MAX_SHARE = 0.55
-# Moved lists of at most this many centroids (per problem) are scored with the
-# exact formula on CUDA cores instead of a tensor-core pass over them.
-EXACT_MOVED_MAX = 256
+# Cost model of an assignment, in ns per point, from B200 measurements of the
+# benchmark layer: a tensor-core pass costs about (0.004 + 0.000375 * kp) ns per
+# point and 128-centroid tile (kp the packed width); its re-score and the merge
+# over every point add about (0.06 + 0.008 * bs) ns per point; the exact
+# CUDA-core scan of a moved list costs about (4e-4 + 3.5e-5 * bs) ns per point
+# and centroid plus 0.02 ns per point. The model ranks the two incremental
+# forms; whether an incremental pass beats a full one is decided from the
+# measured times of the run's own passes (the model scaled by them).
+INCREMENTAL_MAX_SHARE = 0.95
+# Tests set this to take the incremental form whenever moved lists exist.
+INCREMENTAL_FORCE = False
+
+
+def _tile_ns(kp: int) -> float:
+    return 0.004 + 0.000375 * kp
 
 
 class IncrementalAssign:
@@ -151,6 +157,17 @@ class IncrementalAssign:
         self.k_host = np.array(k_host, dtype=np.float64)
         self.n_host = np.array(pts.n_host, dtype=np.float64)
         self.listed = False
+        self.C_old = torch.empty(pts.nblk, k_pad, pts.bs, dtype=torch.float32, device=dev)
+        self.cnorm_old = torch.empty(pts.nblk, k_pad, dtype=torch.float32, device=dev)
+        self.have_old = False
+        self.unres = torch.zeros(pts.nblk, pts.n_pad, dtype=torch.uint8, device=dev)
+        self.ulist = torch.zeros(pts.nblk, pts.n_pad, dtype=torch.int32, device=dev)
+        self.ucount = torch.zeros(pts.nblk, dtype=torch.int32, device=dev)
+        self.ucount_host = torch.zeros(pts.nblk, dtype=torch.int32, pin_memory=True)
+        self.unres_rate = 0.5  # share of the points whose centroid moved left for a full search
+        self.ms_per_ns: float | None = None  # device ms per model ns (from full passes)
+        self.inc_ratio = 1.0  # measured / predicted time of incremental passes
+        self.pending = None
 
     def mark(self, first: bool, mask: torch.Tensor) -> None:
         """Clusters whose members changed in this iteration's assignment."""
@@ -168,26 +185,68 @@ class IncrementalAssign:
         self.counts_host.copy_(self.counts, non_blocking=True)
         self.listed = True
 
-    def plan(self, act: np.ndarray) -> tuple[int, int, float] | None:
-        """(m_pad, p_pad, algorithmic work) of an incremental assignment of the
-        problems in ``act`` (host bool mask), or None when a full pass is cheaper.
+    def full_estimate(self, act: np.ndarray) -> float:
+        """Model cost (ns) of a full pass over the problems in ``act``."""
+        return float((self.n_host * self.units_k)[act].sum()) * _tile_ns(self.pts.kp)
+
+    def plan(self, act: np.ndarray, force: bool = False) -> tuple[int, int, float, float] | None:
+        """(m_pad, p_pad, algorithmic work, model cost in ns) of an incremental
+        assignment of the problems in ``act`` (host bool mask), or None when a
+        full pass is expected to be faster (``force``: whenever lists exist).
         Reads the counts of the last ``lists`` (the caller synchronised). m_pad
-        is 0 when no problem has a moved centroid, negative when every moved
-        list is short enough for the exact CUDA-core pass."""
+        is 0 when no problem has a moved centroid, negative when the moved
+        lists are scored by the exact CUDA-core scan."""
         if not self.listed or not act.any():
             return None
-        m = self.counts_host[0].numpy().astype(np.float64)
-        p = self.counts_host[1].numpy().astype(np.float64)
-        full = float((self.units_n * self.units_k)[act].sum())
-        inc = float((self.units_n * np.ceil(m / CENT_TILE) + np.ceil(p / ROWS_PER_UNIT) * self.units_k)[act].sum())
-        if full <= 0 or inc >= INCREMENTAL_MAX_SHARE * full:
+        m = self.counts_host[0].numpy().astype(np.float64)[act]
+        p = self.counts_host[1].numpy().astype(np.float64)[act]
+        n, uk = self.n_host[act], self.units_k[act]
+        bs, tile = self.pts.bs, _tile_ns(self.pts.kp)
+        full = float((n * uk).sum()) * tile
+        tc_m = float((n * (np.ceil(m / CENT_TILE) * tile + 0.06 + 0.008 * bs) * (m > 0)).sum())
+        ex_m = float((n * (m * (4e-4 + 3.5e-5 * bs) + 0.02) * (m > 0)).sum()) if bs <= 32 else np.inf
+        keep = self.unres_rate if self.have_old else 1.0
+        est = min(tc_m, ex_m) + keep * float((p * uk).sum()) * tile
+        if full <= 0:
             return None
-        m_pad = int(np.ceil(m[act].max() / CENT_TILE)) * CENT_TILE if m[act].max() > 0 else 0
-        if 0 < m[act].max() <= EXACT_MOVED_MAX and self.pts.bs <= 32:
+        if not force:
+            if self.ms_per_ns is None:  # no full pass timed yet: the model alone
+                if est >= 0.9 * full:
+                    return None
+            elif est * self.inc_ratio >= INCREMENTAL_MAX_SHARE * full:
+                return None
+        m_pad = int(np.ceil(m.max() / CENT_TILE)) * CENT_TILE if m.max() > 0 else 0
+        if ex_m < tc_m:
             m_pad = -m_pad
-        p_pad = int(np.ceil(p[act].max() / ROWS_PER_UNIT)) * ROWS_PER_UNIT if p[act].max() > 0 else 0
-        work = 2.0 * self.pts.bs * float((self.n_host * m + p * self.k_host)[act].sum())
-        return m_pad, p_pad, work
+        p_pad = int(np.ceil(p.max() / ROWS_PER_UNIT)) * ROWS_PER_UNIT if p.max() > 0 else 0
+        work = 2.0 * bs * float((n * m + p * self.k_host[act]).sum())
+        return m_pad, p_pad, work, est
+
+    def timed(self, kind: str, est: float, fn) -> None:
+        """Run one assignment between CUDA events; ``observe`` reads them after
+        the iteration's synchronisation."""
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        self.pending = (kind, est, a, b)
+
+    def observe(self) -> None:
+        """Update the run's calibration from the last timed assignment: device
+        ms per model ns from full passes, and the measured / predicted ratio
+        of incremental passes."""
+        if self.pending is None:
+            return
+        kind, est, a, b = self.pending
+        self.pending = None
+        ms = a.elapsed_time(b)
+        if est <= 0:
+            return
+        if kind == "full":
+            self.ms_per_ns = ms / est
+        elif kind == "inc" and self.ms_per_ns is not None:
+            r = ms / (est * self.ms_per_ns)
+            self.inc_ratio = 0.5 * self.inc_ratio + 0.5 * r
 
     def first_from_seeds(self, C: torch.Tensor, perm: torch.Tensor, k_dev: torch.Tensor) -> tuple[int, float]:
         """First assignment of a Forgy start (euclidean centroids are points
@@ -231,19 +290,47 @@ class IncrementalAssign:
         p_pad = int(np.ceil(p_host.max() / ROWS_PER_UNIT)) * ROWS_PER_UNIT if p_host.max() > 0 else 0
         return p_pad, 2.0 * pts.bs * float((p_host * self.k_host).sum())
 
+    def save_old(self, C: torch.Tensor, cnorm: torch.Tensor, active: torch.Tensor) -> None:
+        """Keep the centroids and norms the iteration's assignment used (before
+        the update) for the problems that ran it: a moved centroid's previous
+        score bounds the unmoved ones'. Converged problems keep the values of
+        their last assignment."""
+        m = active.bool()
+        self.C_old.copy_(torch.where(m[:, None, None], C, self.C_old))
+        self.cnorm_old.copy_(torch.where(m[:, None], cnorm, self.cnorm_old))
+        self.have_old = True
+
+    def _full_search(self, B, C, cnorm, k_dev, act, plist, pcount, p_pad: int) -> torch.Tensor:
+        """Labels of the listed points against all centroids ([nblk][p_pad])."""
+        pts, dev, s = self.pts, self.pts.X.device, stream()
+        Xf = torch.empty(pts.nblk, p_pad, pts.bs, dtype=torch.float32, device=dev)
+        call("skcq_gather_rows", ptr(pts.X), pts.n_pad, ptr(plist), pts.n_pad, ptr(pcount), pts.nblk, p_pad, pts.bs,
+             ptr(Xf), s)
+        sub = PointSet(pts.metric, pts.nblk, pts.bs, p_pad, pcount, [], plist, Xf, Xf)
+        act_f = (act.bool() & (pcount > 0)).to(torch.int32)
+        labels_f = torch.zeros(pts.nblk, p_pad, dtype=torch.int32, device=dev)
+        assign_call(sub, B, C, cnorm, self.k_pad, k_dev, act_f, labels_f)
+        return labels_f
+
     def assign(self, B, C, cnorm, k_dev, active, m_pad: int, p_pad: int) -> None:
         """Labels of the problems in ``active`` (None: all) from the previous
-        labels, in place."""
+        labels, in place. With the previous centroids saved, a point whose
+        centroid moved keeps to the moved centroids when the best of them beats
+        its previous score, and only the rest are searched over all centroids."""
         pts, dev, s = self.pts, self.pts.X.device, stream()
         act = active if active is not None else torch.ones(pts.nblk, dtype=torch.int32, device=dev)
         mcount, pcount = self.counts[0], self.counts[1]
+        zeros = torch.zeros_like(mcount)
+        resolve = self.have_old and m_pad != 0
+        unres = self.unres if resolve else None
+        old = (ptr(self.C_old), ptr(self.cnorm_old)) if resolve else (None, None)
         labels_m = torch.zeros(1, dtype=torch.int32, device=dev)
         merge_m = mcount
         if m_pad < 0:  # short moved lists: exact scores on CUDA cores, merged in place
             call("skcq_assign_moved_exact", pts.metric, ptr(pts.X), ptr(C), ptr(cnorm), pts.nblk, pts.n_pad,
                  self.k_pad, pts.bs, ptr(pts.n), ptr(active), ptr(self.changed), ptr(self.mlist), ptr(mcount),
-                 ptr(self.labels), s)
-            merge_m = torch.zeros_like(mcount)
+                 ptr(self.labels), old[0], old[1], ptr(unres), s)
+            merge_m = zeros
         elif m_pad > 0:  # every point against the moved centroids
             Cm = torch.empty(pts.nblk, m_pad, pts.bs, dtype=torch.float32, device=dev)
             call("skcq_gather_rows", ptr(C), self.k_pad, ptr(self.mlist), self.k_pad, ptr(mcount), pts.nblk, m_pad,
@@ -255,18 +342,34 @@ class IncrementalAssign:
                  ptr(Bm), ptr(cnm), s)
             labels_m = torch.zeros(pts.nblk, pts.n_pad, dtype=torch.int32, device=dev)
             assign_call(pts, Bm, Cm, cnm, m_pad, mcount, act_m, labels_m)
-        labels_f = None
-        if p_pad > 0:  # the points whose centroid moved, against all centroids
-            Xf = torch.empty(pts.nblk, p_pad, pts.bs, dtype=torch.float32, device=dev)
-            call("skcq_gather_rows", ptr(pts.X), pts.n_pad, ptr(self.plist), pts.n_pad, ptr(pcount), pts.nblk,
-                 p_pad, pts.bs, ptr(Xf), s)
-            sub = PointSet(pts.metric, pts.nblk, pts.bs, p_pad, pcount, [], self.plist, Xf, Xf)
-            act_f = (act.bool() & (pcount > 0)).to(torch.int32)
-            labels_f = torch.zeros(pts.nblk, p_pad, dtype=torch.int32, device=dev)
-            assign_call(sub, B, C, cnorm, self.k_pad, k_dev, act_f, labels_f)
-        call("skcq_assign_merge", pts.metric, ptr(pts.X), ptr(C), ptr(cnorm), pts.nblk, pts.n_pad, self.k_pad,
-             pts.bs, ptr(pts.n), ptr(active), ptr(self.changed), ptr(self.mlist), ptr(merge_m), ptr(labels_m),
-             ptr(self.plist), ptr(pcount), p_pad, ptr(labels_f), ptr(self.labels), s)
+        if resolve:
+            # phase 0 (the moved centroids) for every point, then a full search
+            # for the points it left unresolved
+            if m_pad > 0:
+                call("skcq_assign_merge", pts.metric, ptr(pts.X), ptr(C), ptr(cnorm), pts.nblk, pts.n_pad,
+                     self.k_pad, pts.bs, ptr(pts.n), ptr(active), ptr(self.changed), ptr(self.mlist), ptr(merge_m),
+                     ptr(labels_m), ptr(self.ulist), ptr(zeros), 0, None, ptr(self.labels), old[0], old[1],
+                     ptr(unres), s)
+            call("skcq_list_points", ptr(unres), pts.nblk, pts.n_pad, ptr(pts.n), ptr(act), ptr(self.ulist),
+                 ptr(self.ucount), ptr(self.scratch), self.scratch_bytes, s)
+            self.ucount_host.copy_(self.ucount, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+            u = self.ucount_host.numpy()[act.bool().cpu().numpy()]
+            flagged = float(self.counts_host[1].numpy()[act.bool().cpu().numpy()].sum())
+            if flagged > 0:
+                self.unres_rate = 0.5 * self.unres_rate + 0.5 * float(u.sum()) / flagged
+            u_pad = int(np.ceil(u.max() / ROWS_PER_UNIT)) * ROWS_PER_UNIT if u.size and u.max() > 0 else 0
+            if u_pad > 0:
+                labels_f = self._full_search(B, C, cnorm, k_dev, act, self.ulist, self.ucount, u_pad)
+                call("skcq_assign_merge", pts.metric, ptr(pts.X), ptr(C), ptr(cnorm), pts.nblk, pts.n_pad,
+                     self.k_pad, pts.bs, ptr(pts.n), ptr(active), ptr(self.changed), ptr(self.mlist), ptr(zeros),
+                     ptr(labels_m), ptr(self.ulist), ptr(self.ucount), u_pad, ptr(labels_f), ptr(self.labels),
+                     None, None, None, s)
+        else:
+            labels_f = self._full_search(B, C, cnorm, k_dev, act, self.plist, pcount, p_pad) if p_pad > 0 else None
+            call("skcq_assign_merge", pts.metric, ptr(pts.X), ptr(C), ptr(cnorm), pts.nblk, pts.n_pad, self.k_pad,
+                 pts.bs, ptr(pts.n), ptr(active), ptr(self.changed), ptr(self.mlist), ptr(merge_m), ptr(labels_m),
+                 ptr(self.plist), ptr(pcount), p_pad, ptr(labels_f), ptr(self.labels), None, None, None, s)
         if INCREMENTAL_CHECK is not None:
             INCREMENTAL_CHECK(pts, B, C, cnorm, self.k_pad, k_dev, active, self.labels)
 
@@ -418,7 +521,7 @@ def lloyd(
     for it in range(max_iters):
         T.run("pack_centroids", lambda: call("skcq_pack_centroids", metric, ptr(C), nblk, k_pad, bs, ptr(k_dev),
                                              ptr(active), ptr(B), ptr(cnorm), s))
-        plan = inc.plan(act) if inc is not None else None
+        plan = inc.plan(act, force=INCREMENTAL_FORCE) if inc is not None else None
         if inc is not None:
             inc.prev.copy_(labels)
         if it == 0 and inc is not None and forgy:
@@ -430,13 +533,17 @@ def lloyd(
             work = 2.0 * bs * float(nk[act].sum())
             # the split operands each active problem's tensor-core pass reads once
             nbytes = 4.0 * kp * float(act.sum()) * (n_pad + k_pad)
-            T.run("assign", lambda: assign_call(pts, B, C, cnorm, k_pad, k_dev, active, labels), work,
-                  work * kp / bs, nbytes)
+            full_pass = lambda: assign_call(pts, B, C, cnorm, k_pad, k_dev, active, labels)  # noqa: E731
+            if inc is not None:
+                est = inc.full_estimate(act)
+                T.run("assign", lambda: inc.timed("full", est, full_pass), work, work * kp / bs, nbytes)
+            else:
+                T.run("assign", full_pass, work, work * kp / bs, nbytes)
         else:
-            m_pad, p_pad, work = plan
+            m_pad, p_pad, work, est = plan
             nbytes = 4.0 * kp * float(act.sum()) * (n_pad + abs(m_pad) + p_pad + k_pad)
-            T.run("assign", lambda: inc.assign(B, C, cnorm, k_dev, active, m_pad, p_pad), work, work * kp / bs,
-                  nbytes)
+            T.run("assign", lambda: inc.timed("inc", est, lambda: inc.assign(B, C, cnorm, k_dev, active, m_pad,
+                                                                             p_pad)), work, work * kp / bs, nbytes)
         if inc is not None:
             inc.mark(it == 0, active)
         T.run("update", lambda: call("skcq_update", ptr(pts.R), ptr(labels), nblk, n_pad, k_pad, bs, ptr(pts.n),
@@ -448,6 +555,8 @@ def lloyd(
         else:
             _sharded_reseed(shard, pts, C, labels, k_pad, k_dev, active, sums, counts, n_empty, scratch, gofs)
         ran = active.clone() if inc is not None else None
+        if inc is not None:
+            inc.save_old(C, cnorm, active)
         T.run("finalize", lambda: call("skcq_finalize", metric, ptr(sums), ptr(counts), ptr(n_empty), nblk, k_pad,
                                        bs, ptr(k_dev), ptr(active), ptr(converged), ptr(iters_run), ptr(moved),
                                        ptr(nempty_hist), it, ptr(C), ptr(inc.changed) if inc else None, s))
@@ -455,6 +564,8 @@ def lloyd(
             T.run("moved_lists", lambda: inc.lists(ran, k_dev))
         act_host.copy_(active, non_blocking=True)
         torch.cuda.current_stream().synchronize()
+        if inc is not None:
+            inc.observe()
         act = act_host.numpy().astype(bool)
         if not act.any():
             break
@@ -462,13 +573,13 @@ def lloyd(
     # final assignment with the final centroids (kmeans.py:190 / 246)
     call("skcq_pack_centroids", metric, ptr(C), nblk, k_pad, bs, ptr(k_dev), None, ptr(B), ptr(cnorm), s)
     every = np.array(n_all) > 0
-    plan = inc.plan(every) if inc is not None and max_iters > 0 else None
+    plan = inc.plan(every, force=INCREMENTAL_FORCE) if inc is not None and max_iters > 0 else None
     if plan is None:
         work = 2.0 * bs * float(nk.sum())
         T.run("assign", lambda: assign_call(pts, B, C, cnorm, k_pad, k_dev, None, labels), work, work * kp / bs,
               4.0 * kp * nblk * (n_pad + k_pad))
     else:
-        m_pad, p_pad, work = plan
+        m_pad, p_pad, work, _ = plan
         T.run("assign", lambda: inc.assign(B, C, cnorm, k_dev, None, m_pad, p_pad), work, work * kp / bs,
               4.0 * kp * nblk * (n_pad + abs(m_pad) + p_pad + k_pad))
     return KmeansRun(

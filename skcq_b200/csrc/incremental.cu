@@ -61,9 +61,12 @@ __global__ void mark_diff_kernel(const int32_t* __restrict__ prev, const int32_t
   }
 }
 
-// flag of item i of problem b: centroid lists (which == 0) or point lists
+// flag of item i of problem b: centroid lists (which == 0), points whose
+// centroid moved (1), or points marked in a per-point array (2, `changed` then
+// being [nblk][n_pad])
 __device__ __forceinline__ bool cp_flag(int which, int b, int i, int n_pad, int k_pad, const int32_t* n,
                                         const int32_t* k, const uint8_t* changed, const int32_t* labels) {
+  if (which == 2) return i < n[b] && changed[(int64_t)b * n_pad + i];
   const uint8_t* row = changed + (int64_t)b * k_pad;
   if (which == 0) return i < k[b] && row[i];
   if (i >= n[b]) return false;
@@ -165,8 +168,9 @@ __global__ void assign_merge_kernel(int metric, const float* __restrict__ X, con
                                     const uint8_t* __restrict__ changed, const int32_t* __restrict__ mlist,
                                     const int32_t* __restrict__ mcount, const int32_t* __restrict__ labels_m,
                                     const int32_t* __restrict__ plist, const int32_t* __restrict__ pcount, int p_pad,
-                                    const int32_t* __restrict__ labels_f, int32_t* __restrict__ labels, int phase,
-                                    int* err) {
+                                    const int32_t* __restrict__ labels_f, int32_t* __restrict__ labels,
+                                    const float* __restrict__ C_old, const float* __restrict__ cnorm_old,
+                                    uint8_t* __restrict__ unres, int phase, int* err) {
   const int b = blockIdx.y;
   if (active && !active[b]) return;
   const int nb = n[b], mb = mcount[b], pb = pcount[b];
@@ -175,12 +179,37 @@ __global__ void assign_merge_kernel(int metric, const float* __restrict__ X, con
   const float* Cb = C + (int64_t)b * k_pad * bs;
   const float* Nb = cnorm + (int64_t)b * k_pad;
   int32_t* Lb = labels + (int64_t)b * n_pad;
+  uint8_t* Ub = unres ? unres + (int64_t)b * n_pad : nullptr;
+  if ((phase == 0 && mb <= 0) || (phase == 1 && pb <= 0)) {  // nothing to merge in this phase
+    if (phase == 0 && Ub)
+      for (int i = blockIdx.x * MC_THREADS + threadIdx.x; i < nb; i += gridDim.x * MC_THREADS) Ub[i] = 0;
+    return;
+  }
   const int lim = nb > pb ? nb : pb;
   for (int i = blockIdx.x * MC_THREADS + threadIdx.x; i < lim; i += gridDim.x * MC_THREADS) {
     if (phase == 0 && i < nb) {
       const int a = Lb[i];
+      if (Ub) Ub[i] = 0;
       if (a < 0 || a >= k_pad) {
         atomicCAS(err, 0, 73);
+      } else if (row[a] && Ub) {
+        // its centroid moved: the best moved centroid wins outright when it
+        // scores above a's previous score (which bounds every unmoved
+        // centroid's unchanged score); otherwise a full search
+        const int w = labels_m[(int64_t)b * n_pad + i];
+        const int cand = (w >= 0 && w < mb) ? mlist[(int64_t)b * k_pad + w] : -1;
+        bool done = false;
+        if (cand >= 0 && cand < k_pad) {
+          const float* x = Xb + (int64_t)i * bs;
+          const uint32_t ko = exact_key(metric, x, C_old + ((int64_t)b * k_pad + a) * bs,
+                                        cnorm_old[(int64_t)b * k_pad + a], bs);
+          const uint32_t kc = exact_key(metric, x, Cb + (int64_t)cand * bs, Nb[cand], bs);
+          if (kc > ko) {
+            Lb[i] = cand;
+            done = true;
+          }
+        }
+        if (!done) Ub[i] = 1;
       } else if (!row[a] && mb > 0) {
         const int w = labels_m[(int64_t)b * n_pad + i];
         if (w < 0 || w >= mb) {
@@ -222,7 +251,8 @@ __global__ void __launch_bounds__(MX_THREADS) assign_moved_exact_kernel(
     int metric, const float* __restrict__ X, const float* __restrict__ C, const float* __restrict__ cnorm, int n_pad,
     int k_pad, int bs_rt, const int32_t* __restrict__ n, const int32_t* __restrict__ active,
     const uint8_t* __restrict__ changed, const int32_t* __restrict__ mlist, const int32_t* __restrict__ mcount,
-    int32_t* __restrict__ labels, int* err) {
+    int32_t* __restrict__ labels, const float* __restrict__ C_old, const float* __restrict__ cnorm_old,
+    uint8_t* __restrict__ unres, int* err) {
   constexpr int XN = BS > 0 ? BS : 32;
   const int bs = BS > 0 ? BS : bs_rt;
   extern __shared__ float sm[];
@@ -232,7 +262,12 @@ __global__ void __launch_bounds__(MX_THREADS) assign_moved_exact_kernel(
   const int b = blockIdx.y;
   if (active && !active[b]) return;
   const int nb = n[b], mb = mcount[b];
-  if (mb <= 0) return;
+  uint8_t* Ub = unres ? unres + (int64_t)b * n_pad : nullptr;
+  if (mb <= 0) {
+    if (Ub)
+      for (int i = blockIdx.x * MX_THREADS + threadIdx.x; i < nb; i += gridDim.x * MX_THREADS) Ub[i] = 0;
+    return;
+  }
   const uint8_t* row = changed + (int64_t)b * k_pad;
   const float* Cb = C + (int64_t)b * k_pad * bs;
   const float* Nb = cnorm + (int64_t)b * k_pad;
@@ -241,14 +276,17 @@ __global__ void __launch_bounds__(MX_THREADS) assign_moved_exact_kernel(
   for (int i0 = blockIdx.x * MX_THREADS; i0 < nb; i0 += gridDim.x * MX_THREADS) {
     const int i = i0 + threadIdx.x;
     int a = -1;
+    bool moved_a = false;
     float x[XN];
     if (i < nb) {
       a = Lb[i];
+      if (Ub) Ub[i] = 0;
       if (a < 0 || a >= k_pad) {
         atomicCAS(err, 0, 73);
         a = -1;
       } else if (row[a]) {
-        a = -1;  // its centroid moved: re-assigned over all centroids elsewhere
+        moved_a = true;
+        if (!Ub) a = -1;  // without the old scores: re-assigned over all centroids elsewhere
       }
     }
     if (a >= 0) {
@@ -294,15 +332,27 @@ __global__ void __launch_bounds__(MX_THREADS) assign_moved_exact_kernel(
       }
     }
     if (a >= 0 && best_c >= 0) {
-      const float* ca = Cb + (int64_t)a * bs;
+      // unmoved a: its current score; moved a: its score before the update,
+      // which bounds every unmoved centroid's (unchanged) score
+      const float* ca = moved_a ? C_old + ((int64_t)b * k_pad + a) * bs : Cb + (int64_t)a * bs;
+      const float na = moved_a ? cnorm_old[(int64_t)b * k_pad + a] : Nb[a];
       float dot = 0.f;
 #pragma unroll
       for (int j = 0; j < XN; ++j)
         if (BS > 0 || j < bs) dot = __fmaf_rn(x[j], ca[j], dot);
-      float sc = metric == SKCQ_METRIC_COSINE ? dot : -__fadd_rn(__fmul_rn(dot, -2.0f), Nb[a]);
+      float sc = metric == SKCQ_METRIC_COSINE ? dot : -__fadd_rn(__fmul_rn(dot, -2.0f), na);
       if (sc != sc) sc = -INFINITY;
       const uint32_t ka = float_key(sc + 0.0f);
-      if (best > ka || (best == ka && best_c < a)) Lb[i] = best_c;
+      if (moved_a) {
+        if (best > ka)
+          Lb[i] = best_c;
+        else
+          Ub[i] = 1;
+      } else if (best > ka || (best == ka && best_c < a)) {
+        Lb[i] = best_c;
+      }
+    } else if (moved_a && Ub) {
+      Ub[i] = 1;
     }
   }
 }
@@ -377,13 +427,15 @@ extern "C" int skcq_gather_rows(const float* src, int src_rows, const int32_t* i
 extern "C" int skcq_assign_moved_exact(int metric, const float* X, const float* C, const float* cnorm, int nblk,
                                        int n_pad, int k_pad, int bs, const int32_t* n, const int32_t* active,
                                        const uint8_t* changed, const int32_t* mlist, const int32_t* mcount,
-                                       int32_t* labels, void* stream) {
+                                       int32_t* labels, const float* C_old, const float* cnorm_old, uint8_t* unres,
+                                       void* stream) {
   SKCQ_REQUIRE(X && C && cnorm && n && changed && mlist && mcount && labels, SKCQ_ERR_INVALID,
                "assign_moved_exact: null pointer");
   SKCQ_REQUIRE(metric == SKCQ_METRIC_COSINE || metric == SKCQ_METRIC_L2, SKCQ_ERR_INVALID,
                "assign_moved_exact: metric");
   SKCQ_REQUIRE(nblk > 0 && nblk <= 65535 && n_pad > 0 && k_pad > 0 && bs > 0 && bs <= 32, SKCQ_ERR_INVALID,
                "assign_moved_exact: bad sizes (block size %d, at most 32)", bs);
+  SKCQ_REQUIRE(!unres || (C_old && cnorm_old), SKCQ_ERR_INVALID, "assign_moved_exact: unres without old centroids");
   int* err = device_error_word();
   SKCQ_REQUIRE(err != nullptr, SKCQ_ERR_CUDA, "assign_moved_exact: no device error word");
   const size_t smem = (size_t)MX_SLICE * (bs + 2) * sizeof(float);
@@ -394,7 +446,8 @@ extern "C" int skcq_assign_moved_exact(int metric, const float* X, const float* 
   cudaStream_t s = (cudaStream_t)stream;
 #define SKCQ_MX(BSV)                                                                                           \
   assign_moved_exact_kernel<BSV><<<grid, MX_THREADS, smem, s>>>(metric, X, C, cnorm, n_pad, k_pad, bs, n, active, \
-                                                                changed, mlist, mcount, labels, err)
+                                                                changed, mlist, mcount, labels, C_old, cnorm_old, \
+                                                                unres, err)
   switch (bs) {
     case 4: SKCQ_MX(4); break;
     case 6: SKCQ_MX(6); break;
@@ -411,10 +464,12 @@ extern "C" int skcq_assign_merge(int metric, const float* X, const float* C, con
                                  int k_pad, int bs, const int32_t* n, const int32_t* active, const uint8_t* changed,
                                  const int32_t* mlist, const int32_t* mcount, const int32_t* labels_m,
                                  const int32_t* plist, const int32_t* pcount, int p_pad, const int32_t* labels_f,
-                                 int32_t* labels, void* stream) {
+                                 int32_t* labels, const float* C_old, const float* cnorm_old, uint8_t* unres,
+                                 void* stream) {
   SKCQ_REQUIRE(X && C && cnorm && n && changed && mlist && mcount && labels_m && plist && pcount && labels &&
                    (p_pad == 0 || labels_f),
                SKCQ_ERR_INVALID, "assign_merge: null pointer");
+  SKCQ_REQUIRE(!unres || (C_old && cnorm_old), SKCQ_ERR_INVALID, "assign_merge: unres without old centroids");
   SKCQ_REQUIRE(metric == SKCQ_METRIC_COSINE || metric == SKCQ_METRIC_L2, SKCQ_ERR_INVALID, "assign_merge: metric");
   SKCQ_REQUIRE(nblk > 0 && nblk <= 65535 && n_pad > 0 && k_pad > 0 && bs > 0 && p_pad >= 0 && p_pad <= n_pad,
                SKCQ_ERR_INVALID, "assign_merge: bad sizes");
@@ -425,6 +480,21 @@ extern "C" int skcq_assign_merge(int metric, const float* X, const float* C, con
   for (int phase = 0; phase < 2; ++phase)
     assign_merge_kernel<<<dim3(row_grid(n_pad, MC_THREADS), nblk), MC_THREADS, 0, (cudaStream_t)stream>>>(
         metric, X, C, cnorm, n_pad, k_pad, bs, n, active, changed, mlist, mcount, labels_m, plist, pcount, p_pad,
-        labels_f, labels, phase, err);
+        labels_f, labels, C_old, cnorm_old, unres, phase, err);
   return check_launch("assign_merge");
+}
+
+extern "C" int skcq_list_points(const uint8_t* flags, int nblk, int n_pad, const int32_t* n, const int32_t* mask,
+                                int32_t* plist, int32_t* pcount, void* scratch, size_t scratch_bytes, void* stream) {
+  SKCQ_REQUIRE(flags && n && plist && pcount && scratch, SKCQ_ERR_INVALID, "list_points: null pointer");
+  SKCQ_REQUIRE(nblk > 0 && nblk <= 65535 && n_pad > 0, SKCQ_ERR_INVALID, "list_points: bad sizes");
+  const int nc = (int)ceil_div64(n_pad, CP_CHUNK);
+  SKCQ_REQUIRE(scratch_bytes >= (size_t)nblk * nc * sizeof(int32_t), SKCQ_ERR_INVALID,
+               "list_points: scratch of %zu bytes", scratch_bytes);
+  cudaStream_t s = (cudaStream_t)stream;
+  int32_t* cnt = static_cast<int32_t*>(scratch);
+  cp_count_kernel<<<dim3(nc, nblk), CP_THREADS, 0, s>>>(2, n_pad, n_pad, 1, n, n, mask, flags, nullptr, nc, cnt);
+  cp_place_kernel<<<dim3(nc, nblk), CP_THREADS, 0, s>>>(2, n_pad, n_pad, 1, n, n, mask, flags, nullptr, nc, cnt,
+                                                         n_pad, plist, pcount);
+  return check_launch("list_points");
 }

@@ -329,7 +329,6 @@ __global__ void finalize_kernel(int metric, float* __restrict__ sums, int32_t* _
           Nb[c] = 0;
           continue;
         }
-        ch = 1;  // recomputed (or reseeded): moved for the next assignment
       }
       float den;
       if (metric == SKCQ_METRIC_COSINE) {
@@ -339,14 +338,19 @@ __global__ void finalize_kernel(int metric, float* __restrict__ sums, int32_t* _
       } else {
         den = cnt > 0 ? (float)cnt : 1.f;  // reseeded clusters keep the point
       }
+      bool differs = false;
       for (int j = 0; j < bs; ++j) {
         const float nv = (metric == SKCQ_METRIC_COSINE || cnt > 0) ? __fdiv_rn(s[j], den) : s[j];
         const float d = __fsub_rn(nv, cc[j]);
         part = __fmaf_rn(d, d, part);
+        differs |= __float_as_uint(nv) != __float_as_uint(cc[j]);
         cc[j] = nv;
         s[j] = 0.f;
       }
       Nb[c] = 0;
+      // recomputed (or reseeded): moved for the next assignment unless the
+      // value came out bit for bit the same (e.g. a Forgy seed alone in its cluster)
+      if (changed) changed[(int64_t)b * k_pad + c] = differs ? 1 : 0;
     }
     const float tot = block_sum(part);
     if (threadIdx.x == 0) {

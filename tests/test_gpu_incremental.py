@@ -40,13 +40,13 @@ def _points(metric, nblk, n, bs, seed):
     return _engine.gather_block_points(w.cuda(), bs, nblk, False, 0.0, False, metric)
 
 
-def _run(metric, nblk, n, bs, K, iters, share, seed=3):
+def _run(metric, nblk, n, bs, K, iters, force, seed=3):
     from skcq_b200 import _engine
     from skcq_b200.codebook.kmeans import sobol_first_orthant
 
     pts = _points(metric, nblk, n, bs, seed)
-    old = _engine.INCREMENTAL_MAX_SHARE
-    _engine.INCREMENTAL_MAX_SHARE = share
+    old = _engine.INCREMENTAL_FORCE
+    _engine.INCREMENTAL_FORCE = force
     try:
         if metric == 0:
             run = _engine.lloyd(pts, K, iters,
@@ -56,7 +56,7 @@ def _run(metric, nblk, n, bs, K, iters, share, seed=3):
             perms = [torch.randperm(nb, generator=g) for nb in pts.n_host]
             run = _engine.lloyd(pts, K, iters, init_perms=perms)
     finally:
-        _engine.INCREMENTAL_MAX_SHARE = old
+        _engine.INCREMENTAL_FORCE = old
     return pts, run
 
 
@@ -99,7 +99,7 @@ def test_incremental_assignment_equals_full(case):
 
     _engine.INCREMENTAL_CHECK = check
     try:
-        pts, run = _run(metric, nblk, n, bs, K, iters, share=1e9)  # incremental whenever lists exist
+        pts, run = _run(metric, nblk, n, bs, K, iters, force=True)  # incremental whenever lists exist
     finally:
         _engine.INCREMENTAL_CHECK = None
     assert seen["calls"] >= 2, seen
@@ -119,7 +119,7 @@ def test_incremental_pass_is_taken():
     _engine.TIMER.reset()
     _engine.TIMER.enabled = True
     try:
-        _run(1, 4, 6144, 4, 4096, 12, share=_engine.INCREMENTAL_MAX_SHARE)
+        _run(1, 4, 6144, 4, 4096, 12, force=False)
         summ = _engine.TIMER.summary()
     finally:
         _engine.TIMER.enabled = False
