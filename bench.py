@@ -756,6 +756,27 @@ def main() -> None:
     launches = _lib.LAUNCHES.kernels
     ksum = _engine.TIMER.summary()
 
+    # ---- the same step with every assignment a full pass -------------------
+    # (the reference's schedule; identical labels, more tensor-core work):
+    # one step, for comparison with the incremental schedule above
+    full_rescan = None
+    if not args.no_legs:
+        _engine.INCREMENTAL = False
+        try:
+            torch.cuda.synchronize()
+            barrier(world)
+            a_ev, b_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a_ev.record()
+            n_full, _ = step(weights)
+            b_ev.record()
+            torch.cuda.synchronize()
+            ms_full = max_over_ranks(a_ev.elapsed_time(b_ev), world)
+        finally:
+            _engine.INCREMENTAL = True
+        bi_full = n_full if rows_mode else sum_over_ranks(n_full, world)
+        full_rescan = {"value": bi_full / (ms_full / 1e3) / 1e6, "unit": UNIT, "ms_per_step": ms_full,
+                       "what": "one step with every k-means assignment a full pass over all centroids"}
+
     # ---- end to end through the public API with host buffers --------------
     # AQLMCodebook.fit on the pinned host weights: the fit copies them to the
     # device and returns the CWR payload (indices, scales, signs, remainders)
@@ -837,6 +858,7 @@ def main() -> None:
             "config": bench_config(args.workload, wl, world, rows_mode),
             "block_iters_per_step": total_block_iters / args.steps,
             "roofline": roofline, "clocks": clocks.summary(), "gpu_launches": launches, "e2e": e2e,
+            "full_rescan": full_rescan,
             "forward": fwd,
             "forward_expert_parallel": fwd_ep,
             "rows_sharded": rows,

@@ -126,6 +126,9 @@ INCREMENTAL_CHECK: Callable | None = None
 INCREMENTAL_MAX_SHARE = 0.95
 # Tests set this to take the incremental form whenever moved lists exist.
 INCREMENTAL_FORCE = False
+# False: every assignment is a full pass over all centroids (the reference's
+# schedule, kmeans.py:136-149); same labels, more work.
+INCREMENTAL = True
 
 
 def _tile_ns(kp: int) -> float:
@@ -514,9 +517,10 @@ def lloyd(
     act_host = torch.empty(nblk, dtype=torch.int32, pin_memory=True)
     T = TIMER
     nk = np.array(pts.n_host, dtype=np.float64) * np.array(k_host, dtype=np.float64)
-    # exact incremental assignment after the first iteration (one process;
-    # row-sharded problems rescan every centroid)
-    inc = IncrementalAssign(pts, k_pad, k_host, labels) if shard is None else None
+    # exact incremental assignment after the first iteration (row-sharded
+    # problems too: the change marks are OR-ed over the ranks, so every rank
+    # keeps the same centroids and lists the same moved ones)
+    inc = IncrementalAssign(pts, k_pad, k_host, labels) if INCREMENTAL else None
     act = (np.array(n_all) > 0)
     for it in range(max_iters):
         T.run("pack_centroids", lambda: call("skcq_pack_centroids", metric, ptr(C), nblk, k_pad, bs, ptr(k_dev),
@@ -524,7 +528,7 @@ def lloyd(
         plan = inc.plan(act, force=INCREMENTAL_FORCE) if inc is not None else None
         if inc is not None:
             inc.prev.copy_(labels)
-        if it == 0 and inc is not None and forgy:
+        if it == 0 and inc is not None and forgy and shard is None:
             p_pad, work = inc.first_from_seeds(C, perm, k_dev)
             nbytes = 4.0 * kp * float(act.sum()) * (p_pad + k_pad)
             T.run("assign", lambda: inc.assign(B, C, cnorm, k_dev, active, 0, p_pad), work, work * kp / bs, nbytes)
@@ -546,6 +550,8 @@ def lloyd(
                                                                              p_pad)), work, work * kp / bs, nbytes)
         if inc is not None:
             inc.mark(it == 0, active)
+            if shard is not None:
+                shard.all_reduce_max_(inc.changed)
         T.run("update", lambda: call("skcq_update", ptr(pts.R), ptr(labels), nblk, n_pad, k_pad, bs, ptr(pts.n),
                                      ptr(k_dev), ptr(active), ptr(sums), ptr(counts), s))
         if shard is None:

@@ -62,6 +62,13 @@ class RowShard:
             t.copy_(s)
         return t
 
+    def all_reduce_max_(self, t: torch.Tensor) -> torch.Tensor:
+        s = self._stage(t)
+        dist.all_reduce(s, op=dist.ReduceOp.MAX, group=self.group)
+        if s is not t:
+            t.copy_(s)
+        return t
+
     def all_gather(self, t: torch.Tensor) -> torch.Tensor:
         """(world, *t.shape) on t's device."""
         s = self._stage(t.contiguous())
