@@ -522,12 +522,20 @@ def lloyd(
     # keeps the same centroids and lists the same moved ones)
     inc = IncrementalAssign(pts, k_pad, k_host, labels) if INCREMENTAL else None
     act = (np.array(n_all) > 0)
-    for it in range(max_iters):
+    def prepare() -> None:
+        """The next assignment's device work that needs no host decision:
+        packing the centroids and keeping the labels it starts from. Queued
+        before the iteration's synchronisation, so the GPU has it to run while
+        the host plans."""
         T.run("pack_centroids", lambda: call("skcq_pack_centroids", metric, ptr(C), nblk, k_pad, bs, ptr(k_dev),
                                              ptr(active), ptr(B), ptr(cnorm), s))
-        plan = inc.plan(act, force=INCREMENTAL_FORCE) if inc is not None else None
         if inc is not None:
             inc.prev.copy_(labels)
+
+    if max_iters > 0:
+        prepare()
+    for it in range(max_iters):
+        plan = inc.plan(act, force=INCREMENTAL_FORCE) if inc is not None else None
         if it == 0 and inc is not None and forgy and shard is None:
             p_pad, work = inc.first_from_seeds(C, perm, k_dev)
             nbytes = 4.0 * kp * float(act.sum()) * (p_pad + k_pad)
@@ -569,7 +577,11 @@ def lloyd(
         if inc is not None:
             T.run("moved_lists", lambda: inc.lists(ran, k_dev))
         act_host.copy_(active, non_blocking=True)
-        torch.cuda.current_stream().synchronize()
+        done = torch.cuda.Event()
+        done.record()
+        if it + 1 < max_iters:
+            prepare()
+        done.synchronize()  # the iteration's results, not the queued preparation
         if inc is not None:
             inc.observe()
         act = act_host.numpy().astype(bool)
