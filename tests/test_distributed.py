@@ -80,6 +80,16 @@ def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
             assert torch.equal(sums, ref)
             flags = torch.tensor([1 << rank, 0, -(1 << 63) if rank == 1 else 0], dtype=torch.int64)
             assert D.or_over_ranks(sh, flags).tolist() == [3, 0, -(1 << 63)]
+            # the incremental assignment's change marks: a cluster changed if it
+            # changed on any rank
+            changed = torch.zeros(nblk, k_pad, dtype=torch.uint8)
+            changed[0, rank] = 1
+            changed[2, 5] = 1
+            sh.all_reduce_max_(changed)
+            ref = torch.zeros(nblk, k_pad, dtype=torch.uint8)
+            ref[0, :2] = 1
+            ref[2, 5] = 1
+            assert torch.equal(changed, ref)
         assert D.current() is None
         torch.save({"ok": True}, os.path.join(out_dir, f"r{rank}.pt"))
     finally:
