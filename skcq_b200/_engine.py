@@ -168,6 +168,8 @@ class IncrementalAssign:
         self.ucount = torch.zeros(pts.nblk, dtype=torch.int32, device=dev)
         self.ucount_host = torch.zeros(pts.nblk, dtype=torch.int32, pin_memory=True)
         self.unres_rate = 0.5  # share of the points whose centroid moved left for a full search
+        self.resolved_pending: torch.Tensor | None = None
+        self.counts_prev = np.zeros(pts.nblk)
         self.ms_per_ns: float | None = None  # device ms per model ns (from full passes)
         self.inc_ratio = 1.0  # measured / predicted time of incremental passes
         self.pending = None
@@ -236,8 +238,15 @@ class IncrementalAssign:
 
     def observe(self) -> None:
         """Update the run's calibration from the last timed assignment: device
-        ms per model ns from full passes, and the measured / predicted ratio
-        of incremental passes."""
+        ms per model ns from full passes, the measured / predicted ratio of
+        incremental passes, and the share of moved-centroid points that needed
+        a full search."""
+        if self.resolved_pending is not None:
+            act = self.resolved_pending.bool().cpu().numpy()
+            self.resolved_pending = None
+            flagged = float(self.counts_prev[act].sum())
+            if flagged > 0:
+                self.unres_rate = 0.5 * self.unres_rate + 0.5 * float(self.ucount_host.numpy()[act].sum()) / flagged
         if self.pending is None:
             return
         kind, est, a, b = self.pending
@@ -323,6 +332,7 @@ class IncrementalAssign:
         pts, dev, s = self.pts, self.pts.X.device, stream()
         act = active if active is not None else torch.ones(pts.nblk, dtype=torch.int32, device=dev)
         mcount, pcount = self.counts[0], self.counts[1]
+        self.counts_prev = self.counts_host[1].numpy().astype(np.float64).copy()
         zeros = torch.zeros_like(mcount)
         resolve = self.have_old and m_pad != 0
         unres = self.unres if resolve else None
@@ -355,19 +365,17 @@ class IncrementalAssign:
                      ptr(unres), s)
             call("skcq_list_points", ptr(unres), pts.nblk, pts.n_pad, ptr(pts.n), ptr(act), ptr(self.ulist),
                  ptr(self.ucount), ptr(self.scratch), self.scratch_bytes, s)
-            self.ucount_host.copy_(self.ucount, non_blocking=True)
-            torch.cuda.current_stream().synchronize()
-            u = self.ucount_host.numpy()[act.bool().cpu().numpy()]
-            flagged = float(self.counts_host[1].numpy()[act.bool().cpu().numpy()].sum())
-            if flagged > 0:
-                self.unres_rate = 0.5 * self.unres_rate + 0.5 * float(u.sum()) / flagged
-            u_pad = int(np.ceil(u.max() / ROWS_PER_UNIT)) * ROWS_PER_UNIT if u.size and u.max() > 0 else 0
-            if u_pad > 0:
-                labels_f = self._full_search(B, C, cnorm, k_dev, act, self.ulist, self.ucount, u_pad)
+            # the unresolved points are a subset of the listed ones, so the
+            # listed count pads their search without a host round trip (the
+            # tensor-core pass skips units past each problem's count)
+            if p_pad > 0:
+                labels_f = self._full_search(B, C, cnorm, k_dev, act, self.ulist, self.ucount, p_pad)
                 call("skcq_assign_merge", pts.metric, ptr(pts.X), ptr(C), ptr(cnorm), pts.nblk, pts.n_pad,
                      self.k_pad, pts.bs, ptr(pts.n), ptr(active), ptr(self.changed), ptr(self.mlist), ptr(zeros),
-                     ptr(labels_m), ptr(self.ulist), ptr(self.ucount), u_pad, ptr(labels_f), ptr(self.labels),
+                     ptr(labels_m), ptr(self.ulist), ptr(self.ucount), p_pad, ptr(labels_f), ptr(self.labels),
                      None, None, None, s)
+            self.ucount_host.copy_(self.ucount, non_blocking=True)
+            self.resolved_pending = act
         else:
             labels_f = self._full_search(B, C, cnorm, k_dev, act, self.plist, pcount, p_pad) if p_pad > 0 else None
             call("skcq_assign_merge", pts.metric, ptr(pts.X), ptr(C), ptr(cnorm), pts.nblk, pts.n_pad, self.k_pad,
