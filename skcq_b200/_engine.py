@@ -260,7 +260,8 @@ class IncrementalAssign:
             r = ms / (est * self.ms_per_ns)
             self.inc_ratio = 0.5 * self.inc_ratio + 0.5 * r
 
-    def first_from_seeds(self, C: torch.Tensor, perm: torch.Tensor, k_dev: torch.Tensor) -> tuple[int, float]:
+    def first_from_seeds(self, C: torch.Tensor, perm: torch.Tensor, k_dev: torch.Tensor,
+                         gofs: torch.Tensor | None = None) -> tuple[int, float]:
         """First assignment of a Forgy start (euclidean centroids are points
         X[perm[c]]): a seed point's own centroid is at distance 0, so it is the
         point's nearest centroid unless another centroid lies within rounding of
@@ -268,8 +269,10 @@ class IncrementalAssign:
         exact tie, which the first index wins). Seeds whose value occurs once get
         their own index; every other point (and every seed with a duplicate,
         detected by hashing the centroid bits) is listed for a search over all
-        centroids. Returns (p_pad, algorithmic work) for ``assign`` with no
-        moved centroids."""
+        centroids. Row-sharded: ``perm`` holds global point indices and this
+        rank's points start at global index ``gofs[b]``; a rank takes the seeds
+        it owns. Returns (p_pad, algorithmic work) for ``assign`` with no moved
+        centroids."""
         pts, dev = self.pts, self.pts.X.device
         nblk, k_pad = pts.nblk, self.k_pad
         c_idx = torch.arange(k_pad, device=dev)
@@ -289,8 +292,12 @@ class IncrementalAssign:
         dup_sorted[:, :-1] |= eq
         dup = torch.zeros_like(dup_sorted).scatter_(1, order, dup_sorted)
         own = valid & ~dup  # seeds that take their own index
+        local = perm[:, :k_pad]
+        if gofs is not None:  # this rank's own points among the seeds
+            local = local - gofs.to(dev)[:, None].long()
+            own &= (local >= 0) & (local < pts.n[:, None].long())
         b_idx = torch.arange(nblk, device=dev)[:, None].expand(-1, k_pad)[own]
-        p_idx = perm[:, :k_pad][own]
+        p_idx = local[own]
         self.labels[b_idx, p_idx] = c_idx[None, :].expand(nblk, -1)[own].to(torch.int32)
         covered = torch.zeros(nblk, pts.n_pad, dtype=torch.bool, device=dev)
         covered[b_idx, p_idx] = True
@@ -544,8 +551,8 @@ def lloyd(
         prepare()
     for it in range(max_iters):
         plan = inc.plan(act, force=INCREMENTAL_FORCE) if inc is not None else None
-        if it == 0 and inc is not None and forgy and shard is None:
-            p_pad, work = inc.first_from_seeds(C, perm, k_dev)
+        if it == 0 and inc is not None and forgy:
+            p_pad, work = inc.first_from_seeds(C, perm, k_dev, gofs if shard is not None else None)
             nbytes = 4.0 * kp * float(act.sum()) * (p_pad + k_pad)
             T.run("assign", lambda: inc.assign(B, C, cnorm, k_dev, active, 0, p_pad), work, work * kp / bs, nbytes)
         elif plan is None:
