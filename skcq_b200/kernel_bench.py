@@ -253,9 +253,56 @@ def forward_case(kind: str, E: int, T: int, reps: int, warmup: int) -> dict:
             "stages_ms": {k: [round(x.elapsed_time(y), 4) for x, y in v] for k, v in stages.items()}}
 
 
+def lloyd_case(metric: int, bs: int, K: int, blocks: int, rows: int, iters: int) -> dict:
+    """One batched Lloyd run (Student-t(5) block rows at std 0.02, Sobol start
+    for cosine, Forgy for euclidean) with every assignment timed: the
+    incremental schedule against the all-full-pass schedule on the same
+    points."""
+    from skcq_b200.codebook.kmeans import sobol_first_orthant
+
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(0)
+    z = torch.randn(rows, blocks * bs, generator=g, device=dev)
+    chi2 = torch.randn(5, rows, blocks * bs, generator=g, device=dev).square_().sum(0)
+    w = z / torch.sqrt(chi2 / 5.0) * (0.02 / (5.0 / 3.0) ** 0.5)
+    del z, chi2
+    pts = _engine.gather_block_points(w, bs, blocks, False, 0.0, False, metric)
+    del w
+    gp = torch.Generator().manual_seed(1)
+    perms = [torch.randperm(nb, generator=gp) for nb in pts.n_host]
+    out = {"case": "lloyd", "metric": "cosine" if metric == 0 else "l2", "bs": bs, "K": K, "blocks": blocks,
+           "rows": rows, "iters": iters}
+    for label, inc in (("incremental", True), ("full", False)):
+        _engine.INCREMENTAL = inc
+        try:
+            for timed in (False, True):  # one untimed run first (kernel set-up)
+                _engine.TIMER.reset()
+                _engine.TIMER.enabled = timed
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                if metric == _engine.COSINE:
+                    run = _engine.lloyd(pts, K, iters, init_cosine=lambda kk, dd: sobol_first_orthant(kk, dd, dev))
+                else:
+                    run = _engine.lloyd(pts, K, iters, init_perms=perms)
+                b.record()
+                torch.cuda.synchronize()
+        finally:
+            _engine.INCREMENTAL = True
+            _engine.TIMER.enabled = False
+        full_work = 2.0 * bs * float(sum(pts.n_host)) * K
+        assigns = [(round(s.elapsed_time(e), 3), round(work / full_work, 4))
+                   for name, s, e, work, _, _ in _engine.TIMER.records if name == "assign"]
+        out[label] = {"ms": a.elapsed_time(b), "iters_run": max(run.iters_run),
+                      "assign_ms": round(sum(x for x, _ in assigns), 2),
+                      "assignments": [{"ms": x, "work_share": y} for x, y in assigns]}
+    _lib.poll_device_error()
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["assign", "prefill", "dequant", "decode", "update", "reconstruct"])
+    ap.add_argument("kernel", choices=["assign", "prefill", "dequant", "decode", "update", "reconstruct", "lloyd"])
+    ap.add_argument("--iters", type=int, default=25)
     ap.add_argument("--experts", type=int, default=128)
     ap.add_argument("--tokens", type=int, default=16384)
     ap.add_argument("--metric", default="l2", choices=["cosine", "l2"])
@@ -272,6 +319,8 @@ def main() -> None:
         res = assign_case(metric, a.bs, a.K, a.blocks, a.rows, a.reps, a.warmup)
     elif a.kernel == "update":
         res = update_case(metric, a.bs, a.K, a.blocks, a.rows, a.reps, a.warmup)
+    elif a.kernel == "lloyd":
+        res = lloyd_case(metric, a.bs, a.K, a.blocks, a.rows, a.iters)
     elif a.kernel == "reconstruct":
         res = reconstruct_case(a.rows, a.reps, a.warmup)
     else:
