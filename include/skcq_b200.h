@@ -123,9 +123,13 @@ int skcq_assign_exact(int metric, const float* X, const float* C, const float* c
 
 /* Segmented sums and counts of the update (kmeans.py:152-159 / 210-217):
  * sums[b][labels[b][i]] += R[b][i], counts[b][labels[b][i]] += 1.
- * sums/counts must be zero on entry (skcq_finalize leaves them zeroed). */
+ * sums/counts must be zero on entry (skcq_finalize leaves them zeroed).
+ * changed (optional, from skcq_mark_changed): points of clusters with
+ * changed == 0 are counted but not summed (skcq_finalize keeps those
+ * centroids and ignores their sums). */
 int skcq_update(const float* R, const int32_t* labels, int nblk, int n_pad, int k_pad, int bs, const int32_t* n,
-                const int32_t* k, const int32_t* active, float* sums, int32_t* counts, void* stream);
+                const int32_t* k, const int32_t* active, float* sums, int32_t* counts, const uint8_t* changed,
+                void* stream);
 
 /* Empty-cluster reseed (kmeans.py:161-172, 219-230): for each active problem
  * with empty clusters, the n_empty worst-fit points (cosine: lowest

@@ -576,7 +576,8 @@ def lloyd(
             if shard is not None:
                 shard.all_reduce_max_(inc.changed)
         T.run("update", lambda: call("skcq_update", ptr(pts.R), ptr(labels), nblk, n_pad, k_pad, bs, ptr(pts.n),
-                                     ptr(k_dev), ptr(active), ptr(sums), ptr(counts), s))
+                                     ptr(k_dev), ptr(active), ptr(sums), ptr(counts),
+                                     ptr(inc.changed) if inc is not None else None, s))
         if shard is None:
             T.run("reseed", lambda: call("skcq_reseed", metric, ptr(pts.X), ptr(C), ptr(labels), nblk, n_pad, k_pad,
                                          bs, ptr(pts.n), ptr(k_dev), ptr(active), ptr(sums), ptr(counts),

@@ -48,7 +48,7 @@ _SIGS: dict[str, list] = {
     "skcq_pack_centroids": [I, P, I, I, I, P, P, P, P, P],
     "skcq_assign": [I, P, P, P, P, P, I, I, I, I, P, P, P, P, P],
     "skcq_assign_exact": [I, P, P, P, I, I, I, I, P, P, P, P, P],
-    "skcq_update": [P, P, I, I, I, I, P, P, P, P, P, P],
+    "skcq_update": [P, P, I, I, I, I, P, P, P, P, P, P, P],
     "skcq_reseed_scratch_bytes": [I, I],
     "skcq_reseed": [I, P, P, P, I, I, I, I, P, P, P, P, P, P, P, P],
     "skcq_reseed_noalloc": [I, P, P, P, I, I, I, I, P, P, P, P, P, P, P],

@@ -32,7 +32,8 @@ __global__ void __launch_bounds__(512) update_smem_kernel(const float* __restric
                                                           int bs, int cols_per_pass, const int32_t* __restrict__ n,
                                                           const int32_t* __restrict__ active,
                                                           const int32_t* __restrict__ kvec, int rows_per_cta,
-                                                          float* __restrict__ sums, int32_t* __restrict__ counts) {
+                                                          float* __restrict__ sums, int32_t* __restrict__ counts,
+                                                          const uint8_t* __restrict__ changed) {
   extern __shared__ float acc[];  // [kb][sp]: jn sums, then the count (as int)
   const int b = blockIdx.y;
   if (active && !active[b]) return;
@@ -50,19 +51,22 @@ __global__ void __launch_bounds__(512) update_smem_kernel(const float* __restric
   const int32_t* Lb = labels + (int64_t)b * n_pad;
   // rows are 16-byte aligned: R is [nblk][n_pad][bs] from an aligned base
   const bool vec4 = (bs & 3) == 0 && (j0 & 3) == 0 && (jn & 3) == 0;
+  const uint8_t* Chb = changed ? changed + (int64_t)b * k_pad : nullptr;
   for (int base = i0 + threadIdx.x; base < i1; base += UP * blockDim.x) {
     int l[UP];
+    bool sum_it[UP];  // false: the cluster kept its members, its centroid is kept (count only)
 #pragma unroll
     for (int u = 0; u < UP; ++u) {
       const int i = base + u * blockDim.x;
       const int v = i < i1 ? Lb[i] : -1;
       l[u] = v < kb ? v : -1;  // a label outside [0, k) never indexes the accumulator
+      sum_it[u] = l[u] >= 0 && (!Chb || Chb[l[u]]);
     }
     if (jn <= 16) {
       float x[UP][16];
 #pragma unroll
       for (int u = 0; u < UP; ++u) {
-        if (l[u] < 0) continue;
+        if (!sum_it[u]) continue;
         const float* xr = Rb + (int64_t)(base + u * blockDim.x) * bs;
         if (vec4) {
 #pragma unroll
@@ -82,9 +86,11 @@ __global__ void __launch_bounds__(512) update_smem_kernel(const float* __restric
       for (int u = 0; u < UP; ++u) {
         if (l[u] < 0) continue;
         float* row = acc + (size_t)l[u] * sp;
+        if (sum_it[u]) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j)
-          if (j < jn) atomicAdd(row + j, x[u][j]);
+          for (int j = 0; j < 16; ++j)
+            if (j < jn) atomicAdd(row + j, x[u][j]);
+        }
         if (counting) atomicAdd(reinterpret_cast<int*>(row + jn), 1);
       }
     } else {
@@ -93,7 +99,8 @@ __global__ void __launch_bounds__(512) update_smem_kernel(const float* __restric
         if (l[u] < 0) continue;
         const float* xr = Rb + (int64_t)(base + u * blockDim.x) * bs;
         float* row = acc + (size_t)l[u] * sp;
-        for (int j = 0; j < jn; ++j) atomicAdd(row + j, xr[j]);
+        if (sum_it[u])
+          for (int j = 0; j < jn; ++j) atomicAdd(row + j, xr[j]);
         if (counting) atomicAdd(reinterpret_cast<int*>(row + jn), 1);
       }
     }
@@ -118,15 +125,17 @@ __global__ void __launch_bounds__(512) update_smem_kernel(const float* __restric
 __global__ void update_global_kernel(const float* __restrict__ R, const int32_t* __restrict__ labels, int nblk,
                                      int n_pad, int k_pad, int bs, const int32_t* __restrict__ n,
                                      const int32_t* __restrict__ active, float* __restrict__ sums,
-                                     int32_t* __restrict__ counts) {
+                                     int32_t* __restrict__ counts, const uint8_t* __restrict__ changed) {
   const int64_t total = (int64_t)nblk * n_pad;
   for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
     const int64_t b = t / n_pad, i = t % n_pad;
     if (i >= n[b] || (active && !active[b])) continue;
     const int l = labels[t];
-    const float* x = R + t * bs;
-    float* s = sums + (b * k_pad + l) * bs;
-    for (int j = 0; j < bs; ++j) atomicAdd(&s[j], x[j]);
+    if (!changed || changed[b * k_pad + l]) {  // else the cluster kept its members: count only
+      const float* x = R + t * bs;
+      float* s = sums + (b * k_pad + l) * bs;
+      for (int j = 0; j < bs; ++j) atomicAdd(&s[j], x[j]);
+    }
     atomicAdd(&counts[b * k_pad + l], 1);
   }
 }
@@ -373,7 +382,7 @@ using namespace skcq;
 
 extern "C" int skcq_update(const float* R, const int32_t* labels, int nblk, int n_pad, int k_pad, int bs,
                              const int32_t* n, const int32_t* k, const int32_t* active, float* sums,
-                             int32_t* counts, void* stream) {
+                             int32_t* counts, const uint8_t* changed, void* stream) {
   SKCQ_REQUIRE(R && labels && n && k && sums && counts, SKCQ_ERR_INVALID, "update: null pointer");
   SKCQ_REQUIRE(bs > 0 && bs <= 64, SKCQ_ERR_INVALID, "update: bad block size %d", bs);
   cudaStream_t s = (cudaStream_t)stream;
@@ -400,13 +409,13 @@ extern "C" int skcq_update(const float* R, const int32_t* labels, int nblk, int 
     if (rpc > n_pad) rpc = n_pad;
     dim3 grid((unsigned)((n_pad + rpc - 1) / rpc), nblk, passes);
     update_smem_kernel<<<grid, 512, smem, s>>>(R, labels, n_pad, k_pad, bs, cpp, n, active, k, (int)rpc, sums,
-                                               counts);
+                                               counts, changed);
     return check_launch("update (shared)");
   }
   int64_t work = (int64_t)nblk * n_pad;
   int grid = (int)((work + 255) / 256);
   if (grid > 148 * 32) grid = 148 * 32;
-  update_global_kernel<<<grid, 256, 0, s>>>(R, labels, nblk, n_pad, k_pad, bs, n, active, sums, counts);
+  update_global_kernel<<<grid, 256, 0, s>>>(R, labels, nblk, n_pad, k_pad, bs, n, active, sums, counts, changed);
   return check_launch("update (global)");
 }
 

@@ -130,7 +130,7 @@ def update_case(metric: int, bs: int, K: int, blocks: int, rows: int, reps: int,
         counts.zero_()
 
     ms = _time(lambda: call("skcq_update", ptr(pts.R), ptr(labels), blocks, pts.n_pad, k_pad, bs, ptr(pts.n),
-                            ptr(k_dev), None, ptr(sums), ptr(counts), s), prepare, reps, warmup)
+                            ptr(k_dev), None, ptr(sums), ptr(counts), None, s), prepare, reps, warmup)
     n_pts = float(sum(pts.n_host))
     algo = n_pts * (bs * 4 + 4) + blocks * K * (bs + 1) * 4.0
     gbs = algo / (ms / 1e3) / 1e9

@@ -77,12 +77,13 @@ def _worker(rank: int, world: int, port: int, out_dir: str, backend: str = "gloo
             if name == "f32_small":
                 ep.close()
         # a rank with no tokens still takes part in the collectives
-        x0 = torch.empty(0 if rank == 1 else 3, 64).cuda()
+        x0 = torch.randn(0 if rank == 1 else 3, 64, generator=torch.Generator().manual_seed(7)).cuda()
         t0 = torch.zeros(x0.shape[0], 2, dtype=torch.int64).cuda()
         t0[:, 1] = 5
         x0 = x0.to(torch.bfloat16)
         y0 = ep(x0, t0, torch.ones(x0.shape[0], 2).cuda())
         res["empty_ok"] = y0.shape == x0.shape and bool(torch.isfinite(y0).all())
+        res["empty_detail"] = (tuple(y0.shape), tuple(x0.shape), y0.float().abs().max().item() if y0.numel() else 0.0)
         # an expert id outside [0, E) raises on the rank that passed it (after
         # the barriers, which every rank still takes)
         bad = torch.zeros(2, 2, dtype=torch.int64).cuda()
@@ -114,7 +115,8 @@ def _check(tmp_path) -> None:
         assert res["f32_small_counts"] and res["bf16_large_counts"], (res["f32_small_count_values"],
                                                                       res["bf16_large_count_values"])
         assert res["bf16_large_dedup"], res
-        assert res["empty_ok"] and res["capacity_checked"], res
+        assert res["empty_ok"] and res["capacity_checked"], (r, res["empty_ok"], res["empty_detail"],
+                                                             res["capacity_checked"])
     # the id 9 of rank 0 is flagged by rank 0, which routed its other slot;
     # rank 1's inputs were valid
     assert torch.load(tmp_path / "ep0.pt")["raised"]

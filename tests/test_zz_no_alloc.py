@@ -46,7 +46,7 @@ def _problem(metric: int, nblk: int, n: int, bs: int, K: int, seed: int):
     sums = torch.zeros(nblk, k_pad, bs, device="cuda")
     counts = torch.zeros(nblk, k_pad, dtype=torch.int32, device="cuda")
     call("skcq_update", ptr(pts.R), ptr(labels), nblk, pts.n_pad, k_pad, bs, ptr(pts.n), ptr(k), None, ptr(sums),
-         ptr(counts), stream())
+         ptr(counts), None, stream())
     return pts, C, labels, k, k_pad, sums, counts
 
 
