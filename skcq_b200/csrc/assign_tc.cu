@@ -556,6 +556,114 @@ refine_kernel(int metric, const float* __restrict__ X, const float* __restrict__
   }
 }
 
+// Re-score for short centroid lists (at most RSO_MAX_GROUPS groups of 32): a
+// CTA takes RSO_CHUNK points of one problem, sorts them by winning group in
+// shared memory (counting sort), and a warp then holds one group's 32
+// centroids in registers (lane = centroid) while it scores every point of
+// that group, each point's coordinates read as a broadcast from the warp's
+// staging slot. The table is read once per group and chunk instead of once
+// per point, which is what bounds refine_kernel (shared-memory reads of the
+// group table for every point). Same arithmetic and tie rule as refine_kernel.
+constexpr int RSO_CHUNK = 4096;
+constexpr int RSO_THREADS = 256;
+constexpr int RSO_WARPS = RSO_THREADS / 32;
+constexpr int RSO_MAX_GROUPS = 256;
+
+template <int BS>
+__global__ void __launch_bounds__(RSO_THREADS) refine_sorted_kernel(
+    int metric, const float* __restrict__ X, const float* __restrict__ C, const float* __restrict__ cnorm, int n_pad,
+    int k_pad, const int32_t* __restrict__ n, const int32_t* __restrict__ kvec, const int32_t* __restrict__ active,
+    int32_t* __restrict__ labels) {
+  __shared__ int idx[RSO_CHUNK];
+  __shared__ int off[RSO_MAX_GROUPS + 1];
+  __shared__ int pos[RSO_MAX_GROUPS];
+  __shared__ __align__(16) float xs[RSO_WARPS][32][BS];
+  const int b = blockIdx.y;
+  if (active && !active[b]) return;
+  const int nb = n[b], kb = kvec[b];
+  const int i0 = blockIdx.x * RSO_CHUNK;
+  if (i0 >= nb) return;
+  const int i1 = min(nb, i0 + RSO_CHUNK);
+  const int G = k_pad / GROUP;  // <= RSO_MAX_GROUPS (host check)
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  int32_t* Lb = labels + (int64_t)b * n_pad;
+  for (int g = tid; g < RSO_MAX_GROUPS; g += RSO_THREADS) pos[g] = 0;
+  __syncthreads();
+  for (int i = i0 + tid; i < i1; i += RSO_THREADS) {
+    const int v = Lb[i];
+    if (v < 0 && -v - 1 < G) atomicAdd(&pos[-v - 1], 1);
+  }
+  __syncthreads();
+  int tot;
+  const int c0 = tid < G ? pos[tid] : 0;
+  const int ex = block_exclusive_scan(c0, &tot);  // RSO_THREADS >= RSO_MAX_GROUPS
+  if (tid < G) {
+    off[tid] = ex;
+    pos[tid] = ex;
+  }
+  if (tid == 0) off[G] = tot;
+  __syncthreads();
+  for (int i = i0 + tid; i < i1; i += RSO_THREADS) {
+    const int v = Lb[i];
+    if (v < 0 && -v - 1 < G) idx[atomicAdd(&pos[-v - 1], 1)] = i;
+  }
+  __syncthreads();
+  const float* Cb = C + (int64_t)b * k_pad * BS;
+  const float* Nb = cnorm + (int64_t)b * k_pad;
+  const float* Xb = X + (int64_t)b * n_pad * BS;
+  for (int g = warp; g < G; g += RSO_WARPS) {
+    const int p0 = off[g], cnt = off[g + 1] - p0;
+    if (cnt == 0) continue;
+    const int c = g * GROUP + lane;
+    const bool ok = c < kb;
+    float cr[BS];
+    rf_load_point<BS>(Cb + (int64_t)c * BS, BS, cr);  // c < k_pad: in bounds; values past k unused
+    const float cn = ok ? __ldg(Nb + c) : 0.f;
+    for (int base = 0; base < cnt; base += 32) {
+      const int m = min(32, cnt - base);
+      __syncwarp();
+      if (lane < m) {
+        float xo[BS];
+        rf_load_point<BS>(Xb + (int64_t)idx[p0 + base + lane] * BS, BS, xo);
+#pragma unroll
+        for (int j = 0; j < BS; ++j) xs[warp][lane][j] = xo[j];
+      }
+      __syncwarp();
+      for (int k = 0; k < m; ++k) {
+        float x[BS];
+        if constexpr (BS % 4 == 0) {
+#pragma unroll
+          for (int j = 0; j < BS; j += 4) {
+            const float4 q = *reinterpret_cast<const float4*>(&xs[warp][k][j]);
+            x[j] = q.x; x[j + 1] = q.y; x[j + 2] = q.z; x[j + 3] = q.w;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < BS; ++j) x[j] = xs[warp][k][j];
+        }
+        float dot = 0.f;
+#pragma unroll
+        for (int j = 0; j < BS; ++j) dot = __fmaf_rn(x[j], cr[j], dot);
+        float sc = metric == SKCQ_METRIC_COSINE ? dot : -__fadd_rn(__fmul_rn(dot, -2.0f), cn);
+        if (!ok || sc != sc) sc = -INFINITY;
+        const uint32_t key = float_key(sc + 0.0f);
+        const uint32_t top = __reduce_max_sync(0xffffffffu, key);
+        const uint32_t win = __ballot_sync(0xffffffffu, key == top);
+        if (lane == 0) Lb[idx[p0 + base + k]] = g * GROUP + (__ffs(win) - 1);
+      }
+    }
+  }
+}
+
+template <int BS>
+static cudaError_t launch_refine_sorted(int metric, const float* X, const float* C, const float* cnorm, int nblk,
+                                        int n_pad, int k_pad, const int32_t* n, const int32_t* k,
+                                        const int32_t* active, int32_t* labels, cudaStream_t s) {
+  dim3 grid((unsigned)((n_pad + RSO_CHUNK - 1) / RSO_CHUNK), (unsigned)nblk);
+  refine_sorted_kernel<BS><<<grid, RSO_THREADS, 0, s>>>(metric, X, C, cnorm, n_pad, k_pad, n, k, active, labels);
+  return cudaGetLastError();
+}
+
 static int num_sms() {
   static int cached[64] = {0};
   int dev = 0;
@@ -661,6 +769,18 @@ extern "C" int skcq_assign(int metric, const float* A, const float* B, const flo
   }
   if (e != cudaSuccess) return set_error(SKCQ_ERR_CUDA, "assign: %s", cudaGetErrorString(e));
   SKCQ_REQUIRE(nblk <= 65535, SKCQ_ERR_INVALID, "assign: %d problems exceed 65535", nblk);
+  const bool sorted = k_pad / GROUP <= RSO_MAX_GROUPS && (bs == 4 || bs == 6 || bs == 8 || bs == 12 || bs == 16);
+  if (sorted) {
+    switch (bs) {
+      case 4: e = launch_refine_sorted<4>(metric, X, C, cnorm, nblk, n_pad, k_pad, n, k, active, labels, s); break;
+      case 6: e = launch_refine_sorted<6>(metric, X, C, cnorm, nblk, n_pad, k_pad, n, k, active, labels, s); break;
+      case 8: e = launch_refine_sorted<8>(metric, X, C, cnorm, nblk, n_pad, k_pad, n, k, active, labels, s); break;
+      case 12: e = launch_refine_sorted<12>(metric, X, C, cnorm, nblk, n_pad, k_pad, n, k, active, labels, s); break;
+      default: e = launch_refine_sorted<16>(metric, X, C, cnorm, nblk, n_pad, k_pad, n, k, active, labels, s); break;
+    }
+    if (e != cudaSuccess) return set_error(SKCQ_ERR_CUDA, "assign (refine): %s", cudaGetErrorString(e));
+    return SKCQ_OK;
+  }
   switch (bs) {
     case 4: e = launch_refine<4>(metric, X, C, cnorm, nblk, n_pad, k_pad, bs, n, k, active, labels, s); break;
     case 6: e = launch_refine<6>(metric, X, C, cnorm, nblk, n_pad, k_pad, bs, n, k, active, labels, s); break;
