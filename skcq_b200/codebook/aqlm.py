@@ -64,7 +64,7 @@ class AQLMCodebook(WeightsCodebookBase[AQLMCWR]):
         out_dev = torch.device(cfg.device) if cfg.device is not None else w.device
         dev = _engine.cuda_device(cfg.device, w)
         n_rows, in_dim = w.shape
-        raw = w.to(device=dev, dtype=torch.float32).contiguous()
+        raw = _engine.to_device_f32(w, dev)
         zero_mask = _engine.row_zero_mask(raw, cfg.norm_threshold)
         if logger.isEnabledFor(logging.INFO):
             logger.info("AQLM: %d/%d rows below norm threshold %s", int(zero_mask.sum()), n_rows, cfg.norm_threshold)

@@ -59,7 +59,13 @@ def cwr_to(cwr: CompressedWeightsRepresentation, device: torch.device) -> Compre
     """Move every tensor of a (possibly nested) payload to ``device``."""
 
     def mv(t):
-        return t.to(device) if isinstance(t, torch.Tensor) else t
+        if not isinstance(t, torch.Tensor):
+            return t
+        if device.type == "cpu" and t.is_cuda:
+            from skcq_b200._engine import to_host
+
+            return to_host(t)
+        return t.to(device)
 
     if isinstance(cwr, AQLMCWR):
         return AQLMCWR(cwr_to(cwr.primary, device), [cwr_to(r, device) for r in cwr.residuals])

@@ -53,7 +53,7 @@ class EuclideanCodebook(WeightsCodebookBase[EuclideanCWR], Experiment):
         dev = _engine.cuda_device(cfg.device, w)
         bs = cfg.block_size
         n_blocks = w.shape[1] // bs
-        raw = w.to(device=dev, dtype=torch.float32).contiguous()
+        raw = _engine.to_device_f32(w, dev)
         fit = fit_blocks(
             self, raw, metric=_engine.L2, bs=bs, K=cfg.K, shared=cfg.shared, max_iters=cfg.max_iters,
             norm_threshold=cfg.norm_threshold, skip_zeros=cfg.skip_zeros,

@@ -25,11 +25,11 @@ _METRIC = {"cosine": _engine.COSINE, "euclidean": _engine.L2}
 
 def _single_problem(data: torch.Tensor, raw: torch.Tensor | None, metric: int, dev: torch.device) -> _engine.PointSet:
     """Wrap an (n, d) matrix as a one-problem point set (no zero skipping)."""
-    x = data.to(device=dev, dtype=torch.float32).contiguous()
+    x = _engine.to_device_f32(data, dev)
     n, d = x.shape
     pts = _engine.gather_block_points(x, d, 1, False, 0.0, False, metric)
     if metric == _engine.COSINE and raw is not None:
-        r = raw.to(device=dev, dtype=torch.float32).contiguous()
+        r = _engine.to_device_f32(raw, dev)
         rp = _engine.gather_block_points(r, d, 1, False, 0.0, False, _engine.L2)
         pts.R = rp.X
     return pts

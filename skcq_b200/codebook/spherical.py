@@ -122,7 +122,7 @@ class SphericalCodebook(WeightsCodebookBase[SphericalCWR], Experiment):
         bs = cfg.block_size
         n_blocks = in_dim // bs
         cov = n_blocks * bs
-        raw = w.to(device=dev, dtype=torch.float32).contiguous()
+        raw = _engine.to_device_f32(w, dev)
         row_zero = _engine.row_zero_mask(raw, cfg.norm_threshold)
         fit = fit_blocks(
             self, raw, metric=_engine.COSINE, bs=bs, K=cfg.K, shared=cfg.shared, max_iters=cfg.max_iters,
