@@ -177,6 +177,42 @@ def _tile_ns(kp: int) -> float:
     return 0.004 + 0.000375 * kp
 
 
+def plan_incremental(m: np.ndarray, p: np.ndarray, n: np.ndarray, k: np.ndarray, bs: int, kp: int, keep: float,
+                     calibrated: bool, inc_ratio: float, force: bool = False
+                     ) -> tuple[int, int, float, float] | None:
+    """The incremental assignment of problems with m moved centroids, p points
+    on moved centroids, n points and k centroids each (host arrays): (m_pad,
+    p_pad, algorithmic work, model cost in ns), or None when the cost model puts
+    a full pass below it. ``keep``: expected share of the p points left for a
+    search over all centroids; ``calibrated``: a full pass of the run has been
+    timed, so ``inc_ratio`` (measured / modelled time of the run's incremental
+    passes) applies. m_pad is 0 when no problem has a moved centroid, negative
+    when the moved lists are scored by the exact CUDA-core scan."""
+    m, p, n, k = (np.asarray(v, dtype=np.float64) for v in (m, p, n, k))
+    if m.size == 0:
+        return None
+    uk = np.ceil(k / CENT_TILE)
+    tile = _tile_ns(kp)
+    full = float((n * uk).sum()) * tile
+    if full <= 0:
+        return None
+    tc_m = float((n * (np.ceil(m / CENT_TILE) * tile + 0.06 + 0.008 * bs) * (m > 0)).sum())
+    ex_m = float((n * (m * (4e-4 + 3.5e-5 * bs) + 0.02) * (m > 0)).sum()) if bs <= 32 else np.inf
+    est = min(tc_m, ex_m) + keep * float((p * uk).sum()) * tile
+    if not force:
+        if not calibrated:  # no full pass timed yet: the model alone
+            if est >= 0.9 * full:
+                return None
+        elif est * inc_ratio >= INCREMENTAL_MAX_SHARE * full:
+            return None
+    m_pad = int(np.ceil(m.max() / CENT_TILE)) * CENT_TILE if m.max() > 0 else 0
+    if ex_m < tc_m:
+        m_pad = -m_pad
+    p_pad = int(np.ceil(p.max() / ROWS_PER_UNIT)) * ROWS_PER_UNIT if p.max() > 0 else 0
+    work = 2.0 * bs * float((n * m + p * k).sum())
+    return m_pad, p_pad, work, est
+
+
 class IncrementalAssign:
     """State of the exact incremental assignment of one Lloyd run
     (csrc/incremental.cu): a centroid whose cluster kept its members keeps its
@@ -240,34 +276,13 @@ class IncrementalAssign:
         """(m_pad, p_pad, algorithmic work, model cost in ns) of an incremental
         assignment of the problems in ``act`` (host bool mask), or None when a
         full pass is expected to be faster (``force``: whenever lists exist).
-        Reads the counts of the last ``lists`` (the caller synchronised). m_pad
-        is 0 when no problem has a moved centroid, negative when the moved
-        lists are scored by the exact CUDA-core scan."""
+        Reads the counts of the last ``lists`` (the caller synchronised)."""
         if not self.listed or not act.any():
             return None
-        m = self.counts_host[0].numpy().astype(np.float64)[act]
-        p = self.counts_host[1].numpy().astype(np.float64)[act]
-        n, uk = self.n_host[act], self.units_k[act]
-        bs, tile = self.pts.bs, _tile_ns(self.pts.kp)
-        full = float((n * uk).sum()) * tile
-        tc_m = float((n * (np.ceil(m / CENT_TILE) * tile + 0.06 + 0.008 * bs) * (m > 0)).sum())
-        ex_m = float((n * (m * (4e-4 + 3.5e-5 * bs) + 0.02) * (m > 0)).sum()) if bs <= 32 else np.inf
-        keep = self.unres_rate if self.have_old else 1.0
-        est = min(tc_m, ex_m) + keep * float((p * uk).sum()) * tile
-        if full <= 0:
-            return None
-        if not force:
-            if self.ms_per_ns is None:  # no full pass timed yet: the model alone
-                if est >= 0.9 * full:
-                    return None
-            elif est * self.inc_ratio >= INCREMENTAL_MAX_SHARE * full:
-                return None
-        m_pad = int(np.ceil(m.max() / CENT_TILE)) * CENT_TILE if m.max() > 0 else 0
-        if ex_m < tc_m:
-            m_pad = -m_pad
-        p_pad = int(np.ceil(p.max() / ROWS_PER_UNIT)) * ROWS_PER_UNIT if p.max() > 0 else 0
-        work = 2.0 * bs * float((n * m + p * self.k_host[act]).sum())
-        return m_pad, p_pad, work, est
+        return plan_incremental(
+            self.counts_host[0].numpy()[act], self.counts_host[1].numpy()[act], self.n_host[act],
+            self.k_host[act], self.pts.bs, self.pts.kp, self.unres_rate if self.have_old else 1.0,
+            self.ms_per_ns is not None, self.inc_ratio, force)
 
     def timed(self, kind: str, est: float, fn) -> None:
         """Run one assignment between CUDA events; ``observe`` reads them after
