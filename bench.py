@@ -49,8 +49,9 @@ WORKLOADS = {
 MODEL = dict(experts=128, hidden=2048, inter=768, prim=(12, 65536), res=[(6, 16384)], iters=25, bits=16,
              layers_total=48)
 METRIC = "kmeans_mblock_iters_per_s"
-# DRAM bytes per split-operand byte of one assignment launch (ncu,
-# profiles/assign_tc_*.md): every operand byte is read from DRAM once.
+# DRAM bytes per split-operand byte of one assignment launch, from ncu's
+# dram__bytes_read + write of the tensor-core pass at the layer's three
+# codebook shapes: every operand byte is read from DRAM once.
 ASSIGN_DRAM_PER_OPERAND_BYTE = 1.0
 UNIT = "Mblock-iters/s"
 
@@ -834,8 +835,8 @@ def main() -> None:
     # (power-capped) bf16 figure is its denominator; the burst figure is kept
     # beside it. traffic: DRAM bytes per launch, the operand bytes the launch
     # reads scaled by the DRAM-to-operand ratio ncu measured for this kernel
-    # (profiles/assign_tc_*.md: dram__bytes_read + write equal the split
-    # operands, ratio 1.00 on all three codebook shapes).
+    # (dram__bytes_read + write equal the split operands, ratio 1.00 on all
+    # three codebook shapes).
     sustained = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
     roofline = {
         "bound": "tensor", "kernel": "skcq_assign (tensor-core pass + exact re-score)", "achieved": achieved,
