@@ -846,6 +846,9 @@ def main() -> None:
         "traffic": ASSIGN_DRAM_PER_OPERAND_BYTE * a["bytes"] / a["launches"] if a.get("launches") else None,
         "traffic_unit": "bytes per launch",
         "issued_tf32_tflops": issued,
+        # the pass issues split-tf32 MMAs: tf32 runs at half the bf16 rate, so
+        # the issued work's own ceiling is half the measured bf16 figure
+        "issued_frac_of_tf32": issued / (sustained / 2.0) if sustained else None,
         "assign_share_of_step": a["ms"] / ms if ms else None,
         "kernel_ms": {k: round(v["ms"], 2) for k, v in ksum.items()},
         "kernel_launches": {k: int(v["launches"]) for k, v in ksum.items()},
