@@ -249,12 +249,28 @@ int skcq_assign_moved_exact(int metric, const float* X, const float* C, const fl
  * c = mlist[b][labels_m[b][i]] (the best moved centroid; labels_m from
  * skcq_assign against the gathered moved centroids) when c scores higher than
  * a under the reference formula, or the same with c < a; the points of plist
- * take labels_f[b][j] (skcq_assign of the gathered points, row stride p_pad). */
+ * take labels_f[b][j] (skcq_assign of the gathered points, row stride p_pad).
+ * labels_m[b][i] < 0 means point i was not scored against the moved
+ * centroids (see skcq_mpass_points) and keeps its label. */
 int skcq_assign_merge(int metric, const float* X, const float* C, const float* cnorm, int nblk, int n_pad, int k_pad,
                       int bs, const int32_t* n, const int32_t* active, const uint8_t* changed, const int32_t* mlist,
                       const int32_t* mcount, const int32_t* labels_m, const int32_t* plist, const int32_t* pcount,
                       int p_pad, const int32_t* labels_f, int32_t* labels, const float* C_old,
                       const float* cnorm_old, uint8_t* unres, void* stream);
+
+/* Euclidean problems: flags[b][i] = 1 for the points the moved-centroid pass
+ * must score -- those whose centroid moved and those not bit for bit equal to
+ * their centroid (a point on its unmoved centroid has the largest score any
+ * centroid can reach, so only an exact tie could move it). */
+int skcq_mpass_points(const float* X, const float* C, const int32_t* labels, const uint8_t* changed,
+                      const int32_t* n, const int32_t* active, int nblk, int n_pad, int k_pad, int bs,
+                      uint8_t* flags, void* stream);
+
+/* labels_m[b][list[b][j]] = sub[b][j] for j < count[b] (sub row stride s_pad,
+ * list and labels_m row stride n_pad): results of a pass over a listed subset
+ * back to point order. */
+int skcq_scatter_sub(const int32_t* list, const int32_t* count, const int32_t* sub, int nblk, int s_pad, int n_pad,
+                     int32_t* labels_m, void* stream);
 
 /* plist[b][0 .. pcount[b]) = the points i < n[b] with flags[b][i] != 0,
  * ascending, for the problems with mask[b] != 0 (flags [nblk][n_pad]);

@@ -417,8 +417,31 @@ class IncrementalAssign:
             cnm = torch.empty(pts.nblk, m_pad, dtype=torch.float32, device=dev)
             call("skcq_pack_centroids", pts.metric, ptr(Cm), pts.nblk, m_pad, pts.bs, ptr(mcount), ptr(act_m),
                  ptr(Bm), ptr(cnm), s)
-            labels_m = torch.zeros(pts.nblk, pts.n_pad, dtype=torch.int32, device=dev)
-            assign_call(pts, Bm, Cm, cnm, m_pad, mcount, act_m, labels_m)
+            if pts.metric == L2 and resolve:
+                # only the points that can move: a point exactly on its unmoved
+                # centroid cannot be beaten (label -1 below: not scored)
+                labels_m = torch.full((pts.nblk, pts.n_pad), -1, dtype=torch.int32, device=dev)
+                call("skcq_mpass_points", ptr(pts.X), ptr(C), ptr(self.labels), ptr(self.changed), ptr(pts.n),
+                     ptr(act_m), pts.nblk, pts.n_pad, self.k_pad, pts.bs, ptr(self.unres), s)
+                call("skcq_list_points", ptr(self.unres), pts.nblk, pts.n_pad, ptr(pts.n), ptr(act_m),
+                     ptr(self.ulist), ptr(self.ucount), ptr(self.scratch), self.scratch_bytes, s)
+                self.ucount_host.copy_(self.ucount, non_blocking=True)
+                torch.cuda.current_stream().synchronize()
+                c_max = int(self.ucount_host.numpy()[act_m.bool().cpu().numpy()].max(initial=0))
+                s_pad = int(np.ceil(c_max / ROWS_PER_UNIT)) * ROWS_PER_UNIT
+                if s_pad > 0:
+                    Xs = torch.empty(pts.nblk, s_pad, pts.bs, dtype=torch.float32, device=dev)
+                    call("skcq_gather_rows", ptr(pts.X), pts.n_pad, ptr(self.ulist), pts.n_pad, ptr(self.ucount),
+                         pts.nblk, s_pad, pts.bs, ptr(Xs), s)
+                    sub = PointSet(pts.metric, pts.nblk, pts.bs, s_pad, self.ucount, [], self.ulist, Xs, Xs)
+                    labels_s = torch.zeros(pts.nblk, s_pad, dtype=torch.int32, device=dev)
+                    assign_call(sub, Bm, Cm, cnm, m_pad, mcount, (act_m.bool() & (self.ucount > 0)).to(torch.int32),
+                                labels_s)
+                    call("skcq_scatter_sub", ptr(self.ulist), ptr(self.ucount), ptr(labels_s), pts.nblk, s_pad,
+                         pts.n_pad, ptr(labels_m), s)
+            else:
+                labels_m = torch.zeros(pts.nblk, pts.n_pad, dtype=torch.int32, device=dev)
+                assign_call(pts, Bm, Cm, cnm, m_pad, mcount, act_m, labels_m)
         if resolve:
             # phase 0 (the moved centroids) for every point, then a full search
             # for the points it left unresolved

@@ -61,6 +61,8 @@ _SIGS: dict[str, list] = {
     "skcq_assign_merge": [I, P, P, P, I, I, I, I, P, P, P, P, P, P, P, P, I, P, P, P, P, P, P],
     "skcq_assign_moved_exact": [I, P, P, P, I, I, I, I, P, P, P, P, P, P, P, P, P, P],
     "skcq_list_points": [P, I, I, P, P, P, P, P, C.c_size_t, P],
+    "skcq_mpass_points": [P, P, P, P, P, P, I, I, I, I, P, P],
+    "skcq_scatter_sub": [P, P, P, I, I, I, P, P],
     "skcq_flip_check": [P, P, P, I, I, I, I, P, P, P],
     "skcq_apply_flip": [P, I, I, I, P, P],
     "skcq_scatter_labels": [P, P, P, I, I, I, I, I, P, P],
@@ -147,6 +149,7 @@ _KERNELS_PER_CALL = {
     "skcq_prefill_plan": 1, "skcq_prefill_pack": 1, "skcq_prefill_dequant": 1, "skcq_prefill_gemm": 1,
     "skcq_mark_changed": 2, "skcq_moved_lists": 4, "skcq_gather_rows": 1, "skcq_assign_merge": 2,
     "skcq_assign_moved_exact": 1, "skcq_list_points": 2,
+    "skcq_mpass_points": 1, "skcq_scatter_sub": 1,
     "skcq_prefill_gemm_swiglu": 1, "skcq_ep_dispatch": 3, "skcq_ep_unpack": 1, "skcq_ep_return": 1,
     "skcq_ep_gather": 1,
 }

@@ -212,7 +212,9 @@ __global__ void assign_merge_kernel(int metric, const float* __restrict__ X, con
         if (!done) Ub[i] = 1;
       } else if (!row[a] && mb > 0) {
         const int w = labels_m[(int64_t)b * n_pad + i];
-        if (w < 0 || w >= mb) {
+        if (w < 0) {
+          // not scored against the moved centroids (exactly on its centroid): keeps a
+        } else if (w >= mb) {
           atomicCAS(err, 0, 74);
         } else {
           const int cand = mlist[(int64_t)b * k_pad + w];
@@ -357,6 +359,48 @@ __global__ void __launch_bounds__(MX_THREADS) assign_moved_exact_kernel(
   }
 }
 
+// Points the moved-centroid pass must score (euclidean): those whose centroid
+// moved, and those not exactly on their centroid. A point equal to its
+// unmoved centroid already has the largest score any centroid can reach
+// (||c||^2 - 2 x.c = -||x||^2 + ||x - c||^2), so no moved centroid can beat it
+// apart from one of identical value (an exact tie).
+__global__ void mpass_points_kernel(const float* __restrict__ X, const float* __restrict__ C,
+                                    const int32_t* __restrict__ labels, const uint8_t* __restrict__ changed,
+                                    const int32_t* __restrict__ n, const int32_t* __restrict__ active, int n_pad,
+                                    int k_pad, int bs, uint8_t* __restrict__ flags) {
+  const int b = blockIdx.y;
+  if (active && !active[b]) return;
+  const int nb = n[b];
+  const float* Xb = X + (int64_t)b * n_pad * bs;
+  const float* Cb = C + (int64_t)b * k_pad * bs;
+  for (int i = blockIdx.x * MC_THREADS + threadIdx.x; i < nb; i += gridDim.x * MC_THREADS) {
+    const int a = labels[(int64_t)b * n_pad + i];
+    bool need = true;
+    if (a >= 0 && a < k_pad && !changed[(int64_t)b * k_pad + a]) {
+      need = false;
+      for (int j = 0; j < bs; ++j)
+        need |= __float_as_uint(Xb[(int64_t)i * bs + j]) != __float_as_uint(Cb[(int64_t)a * bs + j]);
+    }
+    flags[(int64_t)b * n_pad + i] = need ? 1 : 0;
+  }
+}
+
+// labels_m[b][list[b][j]] = sub[b][j] for j < count[b]
+__global__ void scatter_sub_kernel(const int32_t* __restrict__ list, const int32_t* __restrict__ count,
+                                   const int32_t* __restrict__ sub, int s_pad, int n_pad,
+                                   int32_t* __restrict__ labels_m, int* err) {
+  const int b = blockIdx.y;
+  const int cb = count[b];
+  for (int j = blockIdx.x * MC_THREADS + threadIdx.x; j < cb && j < s_pad; j += gridDim.x * MC_THREADS) {
+    const int i = list[(int64_t)b * n_pad + j];
+    if (i < 0 || i >= n_pad) {
+      atomicCAS(err, 0, 76);
+      continue;
+    }
+    labels_m[(int64_t)b * n_pad + i] = sub[(int64_t)b * s_pad + j];
+  }
+}
+
 static int row_grid(int64_t work, int threads) {
   int64_t g = (work + threads - 1) / threads;
   if (g > 64) g = 64;
@@ -497,4 +541,26 @@ extern "C" int skcq_list_points(const uint8_t* flags, int nblk, int n_pad, const
   cp_place_kernel<<<dim3(nc, nblk), CP_THREADS, 0, s>>>(2, n_pad, n_pad, 1, n, n, mask, flags, nullptr, nc, cnt,
                                                          n_pad, plist, pcount);
   return check_launch("list_points");
+}
+
+extern "C" int skcq_mpass_points(const float* X, const float* C, const int32_t* labels, const uint8_t* changed,
+                                 const int32_t* n, const int32_t* active, int nblk, int n_pad, int k_pad, int bs,
+                                 uint8_t* flags, void* stream) {
+  SKCQ_REQUIRE(X && C && labels && changed && n && flags, SKCQ_ERR_INVALID, "mpass_points: null pointer");
+  SKCQ_REQUIRE(nblk > 0 && nblk <= 65535 && n_pad > 0 && k_pad > 0 && bs > 0, SKCQ_ERR_INVALID,
+               "mpass_points: bad sizes");
+  mpass_points_kernel<<<dim3(row_grid(n_pad, MC_THREADS), nblk), MC_THREADS, 0, (cudaStream_t)stream>>>(
+      X, C, labels, changed, n, active, n_pad, k_pad, bs, flags);
+  return check_launch("mpass_points");
+}
+
+extern "C" int skcq_scatter_sub(const int32_t* list, const int32_t* count, const int32_t* sub, int nblk, int s_pad,
+                                int n_pad, int32_t* labels_m, void* stream) {
+  SKCQ_REQUIRE(list && count && sub && labels_m, SKCQ_ERR_INVALID, "scatter_sub: null pointer");
+  SKCQ_REQUIRE(nblk > 0 && nblk <= 65535 && s_pad > 0 && n_pad >= s_pad, SKCQ_ERR_INVALID, "scatter_sub: bad sizes");
+  int* err = device_error_word();
+  SKCQ_REQUIRE(err != nullptr, SKCQ_ERR_CUDA, "scatter_sub: no device error word");
+  scatter_sub_kernel<<<dim3(row_grid(s_pad, MC_THREADS), nblk), MC_THREADS, 0, (cudaStream_t)stream>>>(
+      list, count, sub, s_pad, n_pad, labels_m, err);
+  return check_launch("scatter_sub");
 }
