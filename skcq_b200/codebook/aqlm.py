@@ -162,5 +162,5 @@ class AQLMCodebook(WeightsCodebookBase[AQLMCWR]):
                 max_iters=e.max_iters, moved=e.moved, n_empty=e.n_empty, metric=metric,
             ))
 
-        child.on(KmeansIterEvent, wrap_iter)
+        child.on(KmeansIterEvent, wrap_iter, when=lambda: self.listens(CodebookIterEvent))
         self._forward_from(child, KmeansIterEvent)

@@ -86,20 +86,29 @@ class CodebookDoneEvent:
 
 class Experiment:
     """Listener registry: ``on(EventType, callback)``; ``_emit`` calls the
-    callbacks registered for the event's exact type, in registration order."""
+    callbacks registered for the event's exact type, in registration order.
+    A callback may come with ``when``, a predicate checked at emit time (the
+    forwarding and wrapping callbacks between nested experiments use it, so
+    that events nobody listens to further up cost nothing); ``listens(type)``
+    tells an emitter whether building an event is worth it."""
 
     def __init__(self) -> None:
-        self._listeners: dict[type, list[Callable[..., None]]] = defaultdict(list)
+        self._listeners: dict[type, list[tuple[Callable[..., None], Callable[[], bool] | None]]] = defaultdict(list)
 
-    def on(self, event_type: type[T], callback: Callable[[T], None]) -> None:
-        self._listeners[event_type].append(callback)
+    def on(self, event_type: type[T], callback: Callable[[T], None],
+           when: Callable[[], bool] | None = None) -> None:
+        self._listeners[event_type].append((callback, when))
+
+    def listens(self, event_type: type) -> bool:
+        return any(when is None or when() for _, when in self._listeners.get(event_type, ()))
 
     def _emit(self, event: object) -> None:
-        for cb in list(self._listeners.get(type(event), ())):
-            cb(event)
+        for cb, when in list(self._listeners.get(type(event), ())):
+            if when is None or when():
+                cb(event)
 
     def _forward_from(self, child: Experiment, event_type: type[T]) -> None:
-        child.on(event_type, self._emit)
+        child.on(event_type, self._emit, when=lambda: self.listens(event_type))
 
 
 class TqdmListener:

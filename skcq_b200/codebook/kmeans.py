@@ -93,9 +93,10 @@ def emit_run_events(exp: Experiment, run: _engine.KmeansRun, b: int, name: str, 
     """The Start / Iter* / Done sequence of problem ``b`` (kmeans.py:115-192)."""
     exp._emit(KmeansStartEvent(name=name, metric=metric, k=run.k_host[b], max_iters=max_iters, n_points=n_points,
                                block_idx=block_idx, n_blocks=n_blocks))
-    for it in range(run.iters_run[b]):
-        exp._emit(KmeansIterEvent(iter=it, max_iters=max_iters, moved=float(run.moved[it, b]),
-                                  n_empty=int(run.n_empty[it, b])))
+    if exp.listens(KmeansIterEvent):  # one event per iteration: built only for a listener
+        for it in range(run.iters_run[b]):
+            exp._emit(KmeansIterEvent(iter=it, max_iters=max_iters, moved=float(run.moved[it, b]),
+                                      n_empty=int(run.n_empty[it, b])))
     exp._emit(KmeansDoneEvent(iters_run=run.iters_run[b], final_moved=run.final_moved(b),
                               converged=run.converged[b]))
 
