@@ -88,6 +88,12 @@ def to_host(src: torch.Tensor) -> torch.Tensor:
     n = src.numel() * src.element_size()
     if n == 0:
         return dst
+    with torch.cuda.device(src.device):  # the copies and their events on the source's stream
+        _stage_to_host(src, dst, n)
+    return dst
+
+
+def _stage_to_host(src: torch.Tensor, dst: torch.Tensor, n: int) -> None:
     s = src.contiguous().reshape(-1).view(torch.uint8)
     d = dst.reshape(-1).view(torch.uint8)
     stage = [torch.empty(min(n, _STAGE_BYTES), dtype=torch.uint8, pin_memory=True) for _ in range(2)]
@@ -106,7 +112,6 @@ def to_host(src: torch.Tensor) -> torch.Tensor:
     po, pe, pbuf, pev = prev
     pev.synchronize()
     d[po:pe].copy_(pbuf)
-    return dst
 
 
 def cuda_device(requested: torch.device | str | None, like: torch.Tensor) -> torch.device:
