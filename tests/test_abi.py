@@ -54,3 +54,32 @@ def test_null_pointers_are_rejected_without_touching_the_device():
         _lib.call("skcq_assign", 0, None, None, None, None, None, 1, 256, 128, 4, None, None, None, None, None)
     with pytest.raises(RuntimeError, match="null pointer"):
         _lib.call("skcq_reconstruct", None, 1, 1, 1, None, 0, None, 0, None)
+
+
+def test_exchange_layout_and_argument_checks_without_gpu():
+    """Host-side checks of the expert-parallel and incremental-assignment
+    entry points: sizes and null pointers are rejected before any device
+    work."""
+    import ctypes as C
+
+    from skcq_b200 import _lib
+
+    offs = (C.c_int64 * 6)()
+    assert _lib.call("skcq_ep_layout", 2, 16, 8, 64, offs) == 0
+    rows, ids, wts, cnt, ret, total = list(offs)
+    assert rows == 0 and ids >= 2 * 16 * 64 * 4 and wts >= ids + 2 * 16 * 8 * 4 and cnt > wts
+    assert ret > cnt and total >= ret + 2 * 16 * 64 * 4
+    assert all(v % 256 == 0 for v in offs)
+    with pytest.raises(RuntimeError, match="bad sizes"):
+        _lib.call("skcq_ep_layout", 9, 16, 8, 64, offs)  # more ranks than one node has
+    with pytest.raises(RuntimeError, match="bad sizes"):
+        _lib.call("skcq_ep_layout", 2, 16, 32, 64, offs)  # top-k above 31
+    with pytest.raises(RuntimeError, match="null pointer"):
+        _lib.call("skcq_moved_lists", None, None, 1, 256, 128, None, None, None, None, None, None, None, None, 0,
+                  None)
+    with pytest.raises(RuntimeError, match="null pointer"):
+        _lib.call("skcq_assign_merge", 1, None, None, None, 1, 256, 128, 4, None, None, None, None, None, None, None,
+                  None, 0, None, None, None, None, None, None)
+    with pytest.raises(RuntimeError, match="null pointer"):
+        _lib.call("skcq_list_points", None, 1, 256, None, None, None, None, None, 0, None)
+    assert _lib.load().skcq_moved_lists_scratch_bytes(3, 8192, 4096) == 3 * (2 + 1) * 4
