@@ -376,6 +376,137 @@ __global__ void finalize_kernel(int metric, float* __restrict__ sums, int32_t* _
   }
 }
 
+// Rows of BS floats (16-, 8- or 4-byte vectors; a row starts at a multiple of
+// BS * 4 bytes of a 16-byte aligned problem slice).
+template <int BS>
+__device__ __forceinline__ void fin_load(const float* p, float (&v)[BS]) {
+  if constexpr (BS % 4 == 0) {
+#pragma unroll
+    for (int i = 0; i < BS / 4; ++i) {
+      const float4 t = reinterpret_cast<const float4*>(p)[i];
+      v[4 * i] = t.x, v[4 * i + 1] = t.y, v[4 * i + 2] = t.z, v[4 * i + 3] = t.w;
+    }
+  } else if constexpr (BS % 2 == 0) {
+#pragma unroll
+    for (int i = 0; i < BS / 2; ++i) {
+      const float2 t = reinterpret_cast<const float2*>(p)[i];
+      v[2 * i] = t.x, v[2 * i + 1] = t.y;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < BS; ++i) v[i] = p[i];
+  }
+}
+
+template <int BS>
+__device__ __forceinline__ void fin_store(float* p, const float (&v)[BS]) {
+  if constexpr (BS % 4 == 0) {
+#pragma unroll
+    for (int i = 0; i < BS / 4; ++i)
+      reinterpret_cast<float4*>(p)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+  } else if constexpr (BS % 2 == 0) {
+#pragma unroll
+    for (int i = 0; i < BS / 2; ++i) reinterpret_cast<float2*>(p)[i] = make_float2(v[2 * i], v[2 * i + 1]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < BS; ++i) p[i] = v[i];
+  }
+}
+
+// finalize_kernel for a compile-time block size: the same arithmetic, and the
+// same centroids per thread in the same order (so `moved` has the same bits),
+// with each row moved as vectors and fin_unroll<BS>() centroids in flight per
+// thread. A cluster that kept its members (cnt > 0, not changed) has its sum
+// row zeroed without being read, and its centroid row is not touched.
+constexpr int FIN_THREADS = 256;
+template <int BS>
+__host__ __device__ constexpr int fin_unroll() {
+  return BS >= 12 ? 2 : 4;
+}
+
+template <int BS>
+__global__ void __launch_bounds__(FIN_THREADS) finalize_vec_kernel(
+    int metric, float* __restrict__ sums, int32_t* __restrict__ counts, const int32_t* __restrict__ n_empty, int nblk,
+    int k_pad, const int32_t* __restrict__ kvec, int32_t* __restrict__ active, int32_t* __restrict__ converged,
+    int32_t* __restrict__ iters_run, float* __restrict__ moved_hist, int32_t* __restrict__ nempty_hist, int iter,
+    float* __restrict__ C, uint8_t* __restrict__ changed) {
+  for (int b = blockIdx.x; b < nblk; b += gridDim.x) {
+    if (!active[b]) continue;
+    const int kb = kvec[b];
+    float* Sb = sums + (int64_t)b * k_pad * BS;
+    int32_t* Nb = counts + (int64_t)b * k_pad;
+    float* Cb = C + (int64_t)b * k_pad * BS;
+    uint8_t* chb = changed ? changed + (int64_t)b * k_pad : nullptr;
+    float part = 0.f;
+    constexpr int FIN_UNROLL = fin_unroll<BS>();
+    for (int c0 = threadIdx.x; c0 < kb; c0 += FIN_UNROLL * FIN_THREADS) {
+      int cnt[FIN_UNROLL];
+      bool redo[FIN_UNROLL];
+#pragma unroll
+      for (int u = 0; u < FIN_UNROLL; ++u) {
+        const int c = c0 + u * FIN_THREADS;
+        cnt[u] = c < kb ? Nb[c] : 0;
+        redo[u] = c < kb && !(chb && cnt[u] > 0 && !chb[c]);
+      }
+      float s[FIN_UNROLL][BS], cv[FIN_UNROLL][BS];
+#pragma unroll
+      for (int u = 0; u < FIN_UNROLL; ++u) {
+        const int c = c0 + u * FIN_THREADS;
+        if (redo[u]) {
+          fin_load<BS>(Sb + (int64_t)c * BS, s[u]);
+          fin_load<BS>(Cb + (int64_t)c * BS, cv[u]);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < FIN_UNROLL; ++u) {
+        const int c = c0 + u * FIN_THREADS;
+        if (c >= kb) continue;
+        float z[BS];
+#pragma unroll
+        for (int j = 0; j < BS; ++j) z[j] = 0.f;
+        fin_store<BS>(Sb + (int64_t)c * BS, z);
+        Nb[c] = 0;
+        // same members as at the previous update: the same centroid, kept bit for bit
+        if (!redo[u]) continue;
+        float den;
+        if (metric == SKCQ_METRIC_COSINE) {
+          float q = 0.f;
+#pragma unroll
+          for (int j = 0; j < BS; ++j) q = __fmaf_rn(s[u][j], s[u][j], q);
+          den = fmaxf(sqrtf(q), 1e-12f);  // F.normalize
+        } else {
+          den = cnt[u] > 0 ? (float)cnt[u] : 1.f;  // reseeded clusters keep the point
+        }
+        bool differs = false;
+#pragma unroll
+        for (int j = 0; j < BS; ++j) {
+          const float nv = (metric == SKCQ_METRIC_COSINE || cnt[u] > 0) ? __fdiv_rn(s[u][j], den) : s[u][j];
+          const float d = __fsub_rn(nv, cv[u][j]);
+          part = __fmaf_rn(d, d, part);
+          differs |= __float_as_uint(nv) != __float_as_uint(cv[u][j]);
+          cv[u][j] = nv;
+        }
+        fin_store<BS>(Cb + (int64_t)c * BS, cv[u]);
+        // recomputed (or reseeded): moved for the next assignment unless the
+        // value came out bit for bit the same (e.g. a Forgy seed alone in its cluster)
+        if (chb) chb[c] = differs ? 1 : 0;
+      }
+    }
+    const float tot = block_sum(part);
+    if (threadIdx.x == 0) {
+      const float moved = sqrtf(tot);
+      moved_hist[(int64_t)iter * nblk + b] = moved;
+      nempty_hist[(int64_t)iter * nblk + b] = n_empty[b];
+      iters_run[b] = iter + 1;
+      if (moved < 1e-6f) {
+        active[b] = 0;
+        converged[b] = 1;
+      }
+    }
+    __syncthreads();
+  }
+}
+
 }  // namespace skcq
 
 using namespace skcq;
@@ -488,6 +619,25 @@ extern "C" int skcq_finalize(int metric, float* sums, int32_t* counts, const int
   SKCQ_REQUIRE(sums && counts && n_empty && k && active && converged && iters_run && moved_hist && nempty_hist && C,
                SKCQ_ERR_INVALID, "finalize: null pointer");
   int grid = nblk < 1024 ? nblk : 1024;
+  if (grid == 0) return SKCQ_OK;
+  using VecFn = void (*)(int, float*, int32_t*, const int32_t*, int, int, const int32_t*, int32_t*, int32_t*,
+                         int32_t*, float*, int32_t*, int, float*, uint8_t*);
+  VecFn vec = nullptr;
+  switch (bs) {
+    case 4: vec = finalize_vec_kernel<4>; break;
+    case 6: vec = finalize_vec_kernel<6>; break;
+    case 8: vec = finalize_vec_kernel<8>; break;
+    case 12: vec = finalize_vec_kernel<12>; break;
+    case 16: vec = finalize_vec_kernel<16>; break;
+    default: break;
+  }
+  const bool aligned = (((uintptr_t)sums | (uintptr_t)C) & 15) == 0 && k_pad % 4 == 0;
+  if (vec && aligned) {
+    vec<<<grid, FIN_THREADS, 0, (cudaStream_t)stream>>>(metric, sums, counts, n_empty, nblk, k_pad, k, active,
+                                                        converged, iters_run, moved_hist, nempty_hist, iter, C,
+                                                        changed);
+    return check_launch("finalize");
+  }
   finalize_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(metric, sums, counts, n_empty, nblk, k_pad, bs, k, active,
                                                           converged, iters_run, moved_hist, nempty_hist, iter, C,
                                                           changed);
