@@ -515,6 +515,59 @@ def test_prefill_persistent_gemm_many_tiles():
     assert (y_tc - y_ref).abs().max().item() <= 1e-2 * y_ref.abs().max().item()
 
 
+def _upcast_module(mod):
+    """The same codebook module with its codebooks, scales and remainder
+    upcast to f32 (exact), sign buffers and indices shared."""
+    from skcq_b200.codebook_experts import CodebookModule, _CodebookLayer
+
+    layers = []
+    for lay in mod.layers:
+        layers.append(_CodebookLayer(
+            lay.codebook.detach().float(), lay.assignments, lay.n_blocks, lay.block_size, lay.out_dim, lay.k,
+            remainder=lay.remainder.float() if lay.rem else None,
+            signs=lay.signs,
+            scales=lay.scales.detach().float() if lay.scales is not None else None,
+        ))
+    return CodebookModule(torch.nn.ModuleList(layers), len(layers), mod.out_dim).cuda()
+
+
+@pytest.mark.parametrize("case", ["base", "ragged", "signs", "bench_shapes"])
+def test_prefill_dequant_fast_path_is_bit_identical(case):
+    """The register fast path of skcq_prefill_dequant (bf16 tables, block
+    sizes 4 / 8 / 16) writes the same operand-image bits as the
+    shared-memory decoder does for the same module in f32 (taken for f32
+    tables): same scale * sign * centroid products and the same per-column
+    order of layers, for whole 256-output images, for the gate/up interleaved
+    halves and for an active-expert list."""
+    E, out, inp, specs = {
+        "base": (4, 512, 256, [(8, 64, True), (16, 64, False), (4, 256, False)]),
+        # out not a multiple of 256, in not a multiple of 64, remainder columns
+        "ragged": (3, 300, 200, [(8, 32, True), (16, 64, False), (4, 128, False)]),
+        "signs": (3, 256, 128, [(8, 32, True), (16, 32, False)]),
+        # the benchmark layer's codebooks (16-bit indices above 32767)
+        "bench_shapes": (2, 768, 2048, [(8, 4096, True), (16, 4096, False), (4, 65536, False)]),
+    }[case]
+    mod = _random_module(E, out, inp, specs, seed=808, dtype=torch.bfloat16)
+    if case == "signs":
+        lay = mod.layers[0]
+        g = torch.Generator().manual_seed(809)
+        lay.signs = torch.where(torch.rand(E, out, lay.n_blocks * lay.block_size, generator=g) < 0.5, -1,
+                                1).to(torch.int8).cuda()
+        lay.sign_cov = lay.signs.shape[-1]
+    ref = _upcast_module(mod)
+    KC = -(-inp // 64)
+    active = torch.tensor([E - 1, *range(E - 1, 0, -1)], dtype=torch.int32, device="cuda")  # all but expert 0
+    for half, slots, act in ((-1, E, None), (0, E - 1, active), (1, E - 1, active)):
+        NT = -(-out // (256 if half < 0 else 128))
+        imgs = []
+        for m in (mod, ref):
+            W = torch.full((slots * NT * KC * 16384,), -7.0, dtype=torch.bfloat16, device="cuda")
+            m.dequant_into(W, act, slots, inp, half)
+            imgs.append(W.view(torch.int16))
+        torch.cuda.synchronize()
+        assert torch.equal(imgs[0], imgs[1]), (half, (imgs[0] != imgs[1]).sum().item())
+
+
 @pytest.mark.parametrize("T", [1, 3, 8, 24])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_decode_lookup_table_is_bit_identical(T, dtype):
