@@ -167,6 +167,11 @@ def model_leg(world: int, rank: int, dev: str) -> dict:
     wl = MODEL
     weights = make_weights(wl, seed=5000 + rank, device=dev)
     outs = {"gate": wl["inter"], "up": wl["inter"], "down": wl["hidden"]}
+    # untimed warm-up: one fit of the down projection at these shapes (first
+    # launches, workspace allocation), as the main step has its warm-up steps
+    for name, _, in_dim in projections(wl):
+        if name == "down":
+            model_aqlm(wl, name, in_dim, outs[name]).fit(weights[name])
     torch.cuda.synchronize()
     barrier(world)
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
