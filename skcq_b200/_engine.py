@@ -477,7 +477,92 @@ class IncrementalAssign:
             INCREMENTAL_CHECK(pts, B, C, cnorm, self.k_pad, k_dev, active, self.labels)
 
 
+# Euclidean problems of block size 2-4 with at least this many centroids are
+# searched through the centroid grid (csrc/assign_grid.cu); the points it
+# cannot certify go to the tensor-core pass. False: always the tensor-core pass.
+GRID = True
+GRID_MIN_K = 8192
+
+
+def grid_cells(bs: int, k: int) -> int:
+    """Grid cells per coordinate for k centroids in bs dimensions: about one
+    centroid per cell, within the kernel's limits."""
+    g = int(round(k ** (1.0 / bs)))
+    cap = {2: 256, 3: 100, 4: 31}[bs]
+    return max(2, min(g, cap))
+
+
+def _grid_assign(pts: PointSet, B, C, cnorm, k_pad: int, k_dev, active, labels) -> None:
+    """Labels through the centroid grid; uncertified points (rare: a point whose
+    nearest centroid lies beyond its cell neighbourhood) are gathered and
+    searched over all centroids on the tensor cores, then scattered back.
+    With the timer on, the call is recorded as "assign_grid" (inside the
+    caller's "assign" record) with the work of the full pass it replaces, so
+    the tensor-core figures can leave it out."""
+    T = TIMER
+    if not T.enabled:
+        _grid_assign_run(pts, B, C, cnorm, k_pad, k_dev, active, labels)
+        return
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    _grid_assign_run(pts, B, C, cnorm, k_pad, k_dev, active, labels)
+    b.record()
+    act = (active.bool() if active is not None else torch.ones(pts.nblk, dtype=torch.bool, device=pts.X.device))
+    act_h = act.cpu().numpy()
+    pairs = float((pts.n.cpu().numpy().astype(np.float64) * k_dev.cpu().numpy())[act_h].sum())
+    work = 2.0 * pts.bs * pairs
+    T.records.append(("assign_grid", a, b, work, work * pts.kp / pts.bs,
+                      4.0 * pts.kp * float(act_h.sum()) * (pts.n_pad + k_pad)))
+
+
+def _grid_assign_run(pts: PointSet, B, C, cnorm, k_pad: int, k_dev, active, labels) -> None:
+    dev, s = pts.X.device, stream()
+    lib = _lib.load()
+    G = grid_cells(pts.bs, k_pad)
+    nbytes = int(lib.skcq_assign_grid_scratch_bytes(pts.nblk, pts.n_pad, k_pad, pts.bs, G))
+    scratch = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    unres = torch.zeros(pts.nblk, pts.n_pad, dtype=torch.uint8, device=dev)
+    act = active if active is not None else torch.ones(pts.nblk, dtype=torch.int32, device=dev)
+    call("skcq_assign_grid", ptr(pts.X), ptr(C), ptr(cnorm), pts.nblk, pts.n_pad, k_pad, pts.bs, ptr(pts.n),
+         ptr(k_dev), ptr(act), G, ptr(labels), ptr(unres), ptr(scratch), nbytes, s)
+    ulist = torch.empty(pts.nblk, pts.n_pad, dtype=torch.int32, device=dev)
+    ucount = torch.zeros(pts.nblk, dtype=torch.int32, device=dev)
+    lbytes = 4 * pts.nblk * -(-pts.n_pad // 4096)
+    lscr = torch.empty(max(lbytes, 1), dtype=torch.uint8, device=dev)
+    call("skcq_list_points", ptr(unres), pts.nblk, pts.n_pad, ptr(pts.n), ptr(act), ptr(ulist), ptr(ucount),
+         ptr(lscr), lbytes, s)
+    GRID_STATS["points"] += float(pts.n[act.bool()].sum()) if GRID_STATS["enabled"] else 0.0
+    c_max = int(ucount.max())
+    if GRID_STATS["enabled"]:
+        GRID_STATS["fallback"] += float(ucount.sum())
+    if c_max == 0:
+        return
+    s_pad = round_up(c_max, ROWS_PER_UNIT)
+    Xs = torch.empty(pts.nblk, s_pad, pts.bs, dtype=torch.float32, device=dev)
+    call("skcq_gather_rows", ptr(pts.X), pts.n_pad, ptr(ulist), pts.n_pad, ptr(ucount), pts.nblk, s_pad, pts.bs,
+         ptr(Xs), s)
+    sub = PointSet(pts.metric, pts.nblk, pts.bs, s_pad, ucount, [], ulist, Xs, Xs)
+    labels_s = torch.zeros(pts.nblk, s_pad, dtype=torch.int32, device=dev)
+    _scan_call(sub, B, C, cnorm, k_pad, k_dev, (act.bool() & (ucount > 0)).to(torch.int32), labels_s)
+    call("skcq_scatter_sub", ptr(ulist), ptr(ucount), ptr(labels_s), pts.nblk, s_pad, pts.n_pad, ptr(labels), s)
+
+
+# Counts of grid-searched points and of those sent to the full search (tests
+# and the kernel bench enable it).
+GRID_STATS = {"enabled": False, "points": 0.0, "fallback": 0.0}
+
+
 def assign_call(pts: PointSet, B, C, cnorm, k_pad: int, k_dev, active, labels) -> None:
+    """Labels against all k_dev[b] centroids: the centroid grid for
+    low-dimensional euclidean problems with many centroids, else the
+    tensor-core pass (+ exact re-score)."""
+    if GRID and pts.metric == L2 and 2 <= pts.bs <= 4 and k_pad >= GRID_MIN_K:
+        _grid_assign(pts, B, C, cnorm, k_pad, k_dev, active, labels)
+    else:
+        _scan_call(pts, B, C, cnorm, k_pad, k_dev, active, labels)
+
+
+def _scan_call(pts: PointSet, B, C, cnorm, k_pad: int, k_dev, active, labels) -> None:
     """Tensor-core assignment (+ exact re-score); blocks wider than the
     tensor-core path stages go to the exact CUDA-core kernel."""
     if pts.kp <= TC_MAX_KP:

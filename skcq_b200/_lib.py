@@ -48,6 +48,8 @@ _SIGS: dict[str, list] = {
     "skcq_pack_centroids": [I, P, I, I, I, P, P, P, P, P],
     "skcq_assign": [I, P, P, P, P, P, I, I, I, I, P, P, P, P, P],
     "skcq_assign_exact": [I, P, P, P, I, I, I, I, P, P, P, P, P],
+    "skcq_assign_grid_scratch_bytes": [I, I, I, I, I],
+    "skcq_assign_grid": [P, P, P, I, I, I, I, P, P, P, I, P, P, P, C.c_size_t, P],
     "skcq_update": [P, P, I, I, I, I, P, P, P, P, P, P, P],
     "skcq_reseed_scratch_bytes": [I, I],
     "skcq_reseed": [I, P, P, P, I, I, I, I, P, P, P, P, P, P, P, P],
@@ -101,7 +103,7 @@ _SIGS: dict[str, list] = {
     "skcq_ep_return": [P, I, I, L, P, P, P, P, P, P, I, I, I, I, I, I, I, I, P],
     "skcq_ep_gather": [P, P, I, I, I, I, I, I, P, I, P],
 }
-_RESTYPES = {"skcq_reseed_scratch_bytes": C.c_size_t, "skcq_route_sort_scratch_bytes": C.c_size_t,
+_RESTYPES = {"skcq_reseed_scratch_bytes": C.c_size_t, "skcq_assign_grid_scratch_bytes": C.c_size_t, "skcq_route_sort_scratch_bytes": C.c_size_t,
              "skcq_moved_lists_scratch_bytes": C.c_size_t}
 
 _lib: C.CDLL | None = None
@@ -139,7 +141,7 @@ def last_error() -> str:
 # Kernels each entry point launches (for launch accounting by the benchmark).
 _KERNELS_PER_CALL = {
     "skcq_compact_points": 1, "skcq_gather_points": 1, "skcq_pack_points": 1, "skcq_init_from_points": 1,
-    "skcq_pack_centroids": 1, "skcq_assign": 2, "skcq_assign_exact": 1, "skcq_update": 1, "skcq_reseed": 1, "skcq_reseed_noalloc": 1, "skcq_reseed_candidates": 1,
+    "skcq_pack_centroids": 1, "skcq_assign": 2, "skcq_assign_exact": 1, "skcq_assign_grid": 6, "skcq_update": 1, "skcq_reseed": 1, "skcq_reseed_noalloc": 1, "skcq_reseed_candidates": 1,
     "skcq_finalize": 1, "skcq_flip_check": 1, "skcq_apply_flip": 1, "skcq_scatter_labels": 1,
     "skcq_row_zero_mask": 1, "skcq_spherical_scales": 1, "skcq_centroids_to_bf16": 1, "skcq_copy_remainder": 1,
     "skcq_ssvq_fold": 1, "skcq_quantize_centroids": 1, "skcq_quantize_scales": 3, "skcq_reconstruct": 1,

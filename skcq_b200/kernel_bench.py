@@ -72,13 +72,47 @@ def assign_case(metric: int, bs: int, K: int, blocks: int, rows: int, reps: int,
     _lib.poll_device_error()
     ms = sum(a.elapsed_time(b) for a, b in ev) / reps
     elems = float(rows) * K * blocks
-    return {
+    res = {
         "case": "assign", "metric": "cosine" if metric == 0 else "l2", "bs": bs, "K": K, "blocks": blocks,
         "rows": rows, "kp": pts.kp, "ms_per_launch": ms, "elements_per_s": elems / (ms / 1e3),
         "algorithmic_tflops": 2 * bs * elems / (ms / 1e3) / 1e12,
         "issued_tf32_tflops": 2 * pts.kp * elems / (ms / 1e3) / 1e12,
         "a_bytes": A.numel() * 4, "b_bytes": B.numel() * 4,
     }
+    if metric == _engine.L2 and 2 <= bs <= 4 and k_pad >= _engine.GRID_MIN_K:
+        # the centroid grid (plus the tensor-core search of uncertified points)
+        # against the tensor-core pass above, on the same points and centroids
+        lab_g = torch.empty_like(labels)
+
+        def grid():
+            _engine.assign_call(pts, B, C, cnorm, k_pad, k_dev, None, lab_g)
+
+        for _ in range(max(warmup, 1)):
+            grid()
+        torch.cuda.synchronize()
+        times = []
+        for _ in range(reps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            grid()
+            b.record()
+            torch.cuda.synchronize()
+            times.append(a.elapsed_time(b))
+        _engine.GRID_STATS.update(enabled=True, points=0.0, fallback=0.0)
+        try:
+            grid()
+        finally:
+            _engine.GRID_STATS["enabled"] = False
+        launch()
+        torch.cuda.synchronize()
+        _lib.poll_device_error()
+        same = (lab_g[:, :rows] == labels[:, :rows]).float().mean().item()
+        gms = sum(times) / len(times)
+        res["grid"] = {"ms_per_call": gms, "speedup_vs_tensor_pass": ms / gms, "cells_per_coordinate":
+                       _engine.grid_cells(bs, k_pad), "fallback_share":
+                       _engine.GRID_STATS["fallback"] / max(_engine.GRID_STATS["points"], 1.0),
+                       "labels_equal_tensor_pass": same}
+    return res
 
 
 def _hbm_peak() -> float:
@@ -312,8 +346,11 @@ def main() -> None:
     ap.add_argument("--rows", type=int, default=98304)
     ap.add_argument("--reps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=1)
+    ap.add_argument("--grid", choices=["on", "off"], default="on",
+                    help="centroid-grid search for low-dimensional euclidean problems (off: tensor-core pass)")
     a = ap.parse_args()
     _lib.load()
+    _engine.GRID = a.grid == "on"
     metric = _engine.COSINE if a.metric == "cosine" else _engine.L2
     if a.kernel == "assign":
         res = assign_case(metric, a.bs, a.K, a.blocks, a.rows, a.reps, a.warmup)
