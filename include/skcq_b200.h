@@ -122,16 +122,18 @@ int skcq_assign(int metric, const float* A, const float* B, const float* X, cons
  * (boundaries at quantiles of the centroids). Each point is scored against
  * the centroids of its cell neighbourhood and certified when every other
  * centroid provably scores lower (distance bound plus the fp32 rounding
- * bound). Certified points get labels[b][i] and unres[b][i] = 0; the others
- * unres[b][i] = 1 and their labels are left as they were (search them over
- * all centroids). Requires 2 <= bs <= 4, 2 <= G <= 256, bs * (G - 1) <= 1024,
- * G^bs <= 2^20; scratch (256-byte aligned) of
+ * bound); a point left uncertified is searched again over the boxes of
+ * radius 2 .. ring_max cells around its own cell (ring_max 0: no such
+ * search; at most 3). Certified points get labels[b][i] and unres[b][i] = 0;
+ * the others unres[b][i] = 1 and their labels are left as they were (search
+ * them over all centroids). Requires 2 <= bs <= 4, 2 <= G <= 256,
+ * bs * (G - 1) <= 1024, G^bs <= 2^20; scratch (256-byte aligned) of
  * skcq_assign_grid_scratch_bytes(nblk, n_pad, k_pad, bs, G) bytes. cnorm as
  * skcq_pack_centroids writes it. */
 size_t skcq_assign_grid_scratch_bytes(int nblk, int n_pad, int k_pad, int bs, int G);
 int skcq_assign_grid(const float* X, const float* C, const float* cnorm, int nblk, int n_pad, int k_pad, int bs,
-                     const int32_t* n, const int32_t* k, const int32_t* active, int G, int32_t* labels,
-                     uint8_t* unres, void* scratch, size_t scratch_bytes, void* stream);
+                     const int32_t* n, const int32_t* k, const int32_t* active, int G, int ring_max,
+                     int32_t* labels, uint8_t* unres, void* scratch, size_t scratch_bytes, void* stream);
 
 /* Same contract as skcq_assign, computed with fp32 FMAs on CUDA cores over all
  * centroids (the reference formula everywhere). Used to cross-check. */

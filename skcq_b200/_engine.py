@@ -482,6 +482,9 @@ class IncrementalAssign:
 # cannot certify go to the tensor-core pass. False: always the tensor-core pass.
 GRID = True
 GRID_MIN_K = 8192
+# Largest box radius (cells) of the grid's second search of uncertified points
+# (0: they go straight to the tensor-core pass).
+GRID_RING = 3
 
 
 def grid_cells(bs: int, k: int) -> int:
@@ -524,7 +527,7 @@ def _grid_assign_run(pts: PointSet, B, C, cnorm, k_pad: int, k_dev, active, labe
     unres = torch.zeros(pts.nblk, pts.n_pad, dtype=torch.uint8, device=dev)
     act = active if active is not None else torch.ones(pts.nblk, dtype=torch.int32, device=dev)
     call("skcq_assign_grid", ptr(pts.X), ptr(C), ptr(cnorm), pts.nblk, pts.n_pad, k_pad, pts.bs, ptr(pts.n),
-         ptr(k_dev), ptr(act), G, ptr(labels), ptr(unres), ptr(scratch), nbytes, s)
+         ptr(k_dev), ptr(act), G, GRID_RING, ptr(labels), ptr(unres), ptr(scratch), nbytes, s)
     ulist = torch.empty(pts.nblk, pts.n_pad, dtype=torch.int32, device=dev)
     ucount = torch.zeros(pts.nblk, dtype=torch.int32, device=dev)
     lbytes = 4 * pts.nblk * -(-pts.n_pad // 4096)

@@ -49,7 +49,7 @@ _SIGS: dict[str, list] = {
     "skcq_assign": [I, P, P, P, P, P, I, I, I, I, P, P, P, P, P],
     "skcq_assign_exact": [I, P, P, P, I, I, I, I, P, P, P, P, P],
     "skcq_assign_grid_scratch_bytes": [I, I, I, I, I],
-    "skcq_assign_grid": [P, P, P, I, I, I, I, P, P, P, I, P, P, P, C.c_size_t, P],
+    "skcq_assign_grid": [P, P, P, I, I, I, I, P, P, P, I, I, P, P, P, C.c_size_t, P],
     "skcq_update": [P, P, I, I, I, I, P, P, P, P, P, P, P],
     "skcq_reseed_scratch_bytes": [I, I],
     "skcq_reseed": [I, P, P, P, I, I, I, I, P, P, P, P, P, P, P, P],

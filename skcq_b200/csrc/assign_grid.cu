@@ -311,6 +311,7 @@ struct GridSearchArgs {
   GridScratch sc;
   int32_t* labels;
   uint8_t* unres;
+  int ring_max;  // largest box radius of the ring search (grid_ring_kernel)
 };
 
 constexpr size_t GR_SEARCH_SMEM =
@@ -446,11 +447,11 @@ __global__ void __launch_bounds__(GR_WARPS * 32) grid_search_kernel(GridSearchAr
 
 // 4. Points the super-cell search left uncertified: one warp per point
 // searches the box of fine cells [q - r, q + r] around the point's own cell q
-// for r = GR_SUP .. GR_RING_MAX (lanes split the box's runs of cells, then a
+// for r = GR_SUP .. ring_max (lanes split the box's runs of cells, then a
 // warp reduction keeps the largest score, lowest index among equals) and
 // stops at the first box it certifies. The rest stay flagged. Warps stride
 // over the problem's points 32 at a time and take the flagged ones.
-constexpr int GR_RING_MAX = 3;
+constexpr int GR_RING_MAX = 3;  // largest ring_max accepted
 
 template <int BS>
 __global__ void __launch_bounds__(GR_WARPS * 32) grid_ring_kernel(GridSearchArgs a) {
@@ -482,7 +483,7 @@ __global__ void __launch_bounds__(GR_WARPS * 32) grid_ring_kernel(GridSearchArgs
         x[d] = a.X[((int64_t)b * a.n_pad + pi) * BS + d];
         q[d] = grid_coord(sb + d * nbd, nbd, x[d]);
       }
-      for (int r = GR_SUP; r <= GR_RING_MAX; ++r) {
+      for (int r = GR_SUP; r <= a.ring_max; ++r) {
         int lo[BS], hi[BS];
         int nruns = 1;
 #pragma unroll
@@ -557,13 +558,16 @@ extern "C" size_t skcq_assign_grid_scratch_bytes(int nblk, int n_pad, int k_pad,
 
 extern "C" int skcq_assign_grid(const float* X, const float* C, const float* cnorm, int nblk, int n_pad, int k_pad,
                                 int bs, const int32_t* n, const int32_t* k, const int32_t* active, int G,
-                                int32_t* labels, uint8_t* unres, void* scratch, size_t scratch_bytes, void* stream) {
+                                int ring_max, int32_t* labels, uint8_t* unres, void* scratch, size_t scratch_bytes,
+                                void* stream) {
   SKCQ_REQUIRE(X && C && cnorm && n && k && labels && unres && scratch, SKCQ_ERR_INVALID,
                "assign_grid: null pointer");
   SKCQ_REQUIRE(grid_args_ok(bs, G), SKCQ_ERR_INVALID, "assign_grid: block size %d / %d cells per coordinate", bs, G);
   SKCQ_REQUIRE(nblk > 0 && nblk <= 65535 && n_pad >= 0 && k_pad >= 0, SKCQ_ERR_INVALID,
                "assign_grid: %d problems, n_pad %d, k_pad %d", nblk, n_pad, k_pad);
   SKCQ_REQUIRE(((uintptr_t)scratch & 255) == 0, SKCQ_ERR_INVALID, "assign_grid: scratch not 256-byte aligned");
+  SKCQ_REQUIRE(ring_max == 0 || (ring_max >= GR_SUP && ring_max <= GR_RING_MAX), SKCQ_ERR_INVALID,
+               "assign_grid: ring radius %d outside {0, %d .. %d}", ring_max, GR_SUP, GR_RING_MAX);
   const GridShape g = grid_shape(bs, G);
   GridScratch sc;
   const size_t need = grid_layout(nblk, n_pad, k_pad, bs, g, static_cast<char*>(scratch), &sc);
@@ -589,21 +593,21 @@ extern "C" int skcq_assign_grid(const float* X, const float* C, const float* cno
     }
     configured_dev = dev;
   }
-  GridSearchArgs args{X, n_pad, k_pad, g, n, k, active, sc, labels, unres};
+  GridSearchArgs args{X, n_pad, k_pad, g, n, k, active, sc, labels, unres, ring_max};
   const dim3 sgrid(ceil_div(g.nsc, GR_WARPS), nblk);
   const dim3 rgrid(min(ceil_div(ceil_div(n_pad, 32), GR_WARPS), 64), nblk);
   switch (bs) {
     case 2:
       grid_search_kernel<2><<<sgrid, GR_WARPS * 32, GR_SEARCH_SMEM, s>>>(args);
-      grid_ring_kernel<2><<<rgrid, GR_WARPS * 32, 0, s>>>(args);
+      if (ring_max) grid_ring_kernel<2><<<rgrid, GR_WARPS * 32, 0, s>>>(args);
       break;
     case 3:
       grid_search_kernel<3><<<sgrid, GR_WARPS * 32, GR_SEARCH_SMEM, s>>>(args);
-      grid_ring_kernel<3><<<rgrid, GR_WARPS * 32, 0, s>>>(args);
+      if (ring_max) grid_ring_kernel<3><<<rgrid, GR_WARPS * 32, 0, s>>>(args);
       break;
     default:
       grid_search_kernel<4><<<sgrid, GR_WARPS * 32, GR_SEARCH_SMEM, s>>>(args);
-      grid_ring_kernel<4><<<rgrid, GR_WARPS * 32, 0, s>>>(args);
+      if (ring_max) grid_ring_kernel<4><<<rgrid, GR_WARPS * 32, 0, s>>>(args);
       break;
   }
   return check_launch("assign_grid");

@@ -49,7 +49,7 @@ extern "C" int skcq_last_error(char* buf, size_t len) {
   return SKCQ_OK;
 }
 
-extern "C" int skcq_abi_version(void) { return 9; }
+extern "C" int skcq_abi_version(void) { return 10; }
 
 extern "C" int skcq_packed_width(int metric, int bs) {
   if (bs <= 0) return skcq::set_error(SKCQ_ERR_INVALID, "block size must be positive (got %d)", bs);

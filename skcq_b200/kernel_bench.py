@@ -87,17 +87,26 @@ def assign_case(metric: int, bs: int, K: int, blocks: int, rows: int, reps: int,
         def grid():
             _engine.assign_call(pts, B, C, cnorm, k_pad, k_dev, None, lab_g)
 
-        for _ in range(max(warmup, 1)):
-            grid()
-        torch.cuda.synchronize()
-        times = []
-        for _ in range(reps):
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record()
-            grid()
-            b.record()
-            torch.cuda.synchronize()
-            times.append(a.elapsed_time(b))
+        ring_default = _engine.GRID_RING
+        by_ring = {}
+        try:
+            for ring in (0, 2, 3):  # largest box radius of the second search of uncertified points
+                _engine.GRID_RING = ring
+                for _ in range(max(warmup, 1)):
+                    grid()
+                torch.cuda.synchronize()
+                times = []
+                for _ in range(reps):
+                    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    a.record()
+                    grid()
+                    b.record()
+                    torch.cuda.synchronize()
+                    times.append(a.elapsed_time(b))
+                by_ring[ring] = sum(times) / len(times)
+        finally:
+            _engine.GRID_RING = ring_default
+        times = [by_ring[ring_default]]
         _engine.GRID_STATS.update(enabled=True, points=0.0, fallback=0.0)
         try:
             grid()
@@ -111,7 +120,8 @@ def assign_case(metric: int, bs: int, K: int, blocks: int, rows: int, reps: int,
         res["grid"] = {"ms_per_call": gms, "speedup_vs_tensor_pass": ms / gms, "cells_per_coordinate":
                        _engine.grid_cells(bs, k_pad), "fallback_share":
                        _engine.GRID_STATS["fallback"] / max(_engine.GRID_STATS["points"], 1.0),
-                       "labels_equal_tensor_pass": same}
+                       "labels_equal_tensor_pass": same, "ring_max": ring_default,
+                       "ms_per_call_by_ring_max": by_ring}
     return res
 
 

@@ -125,7 +125,7 @@ def test_grid_abi_certifies_flags_and_checks():
     labels = torch.full((nblk, pts.n_pad), -3, dtype=torch.int32, device="cuda")
     active = torch.tensor([1, 0, 1], dtype=torch.int32, device="cuda")
     call("skcq_assign_grid", ptr(pts.X), ptr(C2), ptr(cn2), nblk, pts.n_pad, k_pad, bs, ptr(pts.n), ptr(k_dev),
-         ptr(active), G, ptr(labels), ptr(unres), ptr(scratch), nbytes, stream())
+         ptr(active), G, 3, ptr(labels), ptr(unres), ptr(scratch), nbytes, stream())
     _lib.poll_device_error()
     torch.cuda.synchronize()
     u0 = unres[0, :n]
@@ -138,8 +138,11 @@ def test_grid_abi_certifies_flags_and_checks():
     assert (unres[2, :n] == 1).all() and (labels[2] == -3).all()
     with pytest.raises(RuntimeError):
         call("skcq_assign_grid", ptr(pts.X), ptr(C), ptr(cnorm), nblk, pts.n_pad, k_pad, 5, ptr(pts.n), ptr(k_dev),
-             None, G, ptr(labels), ptr(unres), ptr(scratch), nbytes, stream())
+             None, G, 3, ptr(labels), ptr(unres), ptr(scratch), nbytes, stream())
     with pytest.raises(RuntimeError):
         call("skcq_assign_grid", ptr(pts.X), ptr(C), ptr(cnorm), nblk, pts.n_pad, k_pad, bs, ptr(pts.n), ptr(k_dev),
-             None, G, ptr(labels), ptr(unres), ptr(scratch), nbytes - 256, stream())
+             None, G, 3, ptr(labels), ptr(unres), ptr(scratch), nbytes - 256, stream())
+    with pytest.raises(RuntimeError):
+        call("skcq_assign_grid", ptr(pts.X), ptr(C), ptr(cnorm), nblk, pts.n_pad, k_pad, bs, ptr(pts.n), ptr(k_dev),
+             None, G, 1, ptr(labels), ptr(unres), ptr(scratch), nbytes, stream())
     assert lib.skcq_assign_grid_scratch_bytes(nblk, pts.n_pad, k_pad, bs, 1) == 0
