@@ -104,3 +104,61 @@ def test_row_sharded_fit_matches_single_process_nccl(tmp_path):
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     mp.spawn(_worker, args=(2, _free_port(), "nccl", str(tmp_path)), nprocs=2, join=True)
     _check(str(tmp_path), "nccl", 2)
+
+
+def _worker_grid(rank: int, world: int, port: int, out_dir: str) -> None:
+    """A euclidean bs=4 codebook with K = 8192, whose assignments take the
+    centroid grid: the row-sharded fit against the single-process one."""
+    import torch.distributed as dist
+
+    from skcq_b200 import codebook as cb
+    from skcq_b200 import distributed as D
+    from skcq_b200.codebook.events import KmeansDoneEvent
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(0)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        g = torch.Generator().manual_seed(21)
+        E, out_dim, in_dim = 16, 1024, 8
+        z = torch.randn(E * out_dim, in_dim, generator=g)
+        chi2 = torch.randn(5, E * out_dim, in_dim, generator=g).square().sum(0)
+        w = (z / torch.sqrt(chi2 / 5.0) * 0.02).cuda()
+
+        def make():
+            return cb.EuclideanCodebook(cb.EuclideanCodebookConfig(block_size=4, K=8192, max_iters=6,
+                                                                   norm_threshold=1e-9, skip_zeros=False))
+
+        torch.manual_seed(7)
+        ref = make()
+        ref_done = []
+        ref.on(KmeansDoneEvent, ref_done.append)
+        ref_cwr = ref.fit(w)
+        r0, r1 = D.expert_row_range(E, out_dim, world, rank)
+        torch.manual_seed(7)
+        sh = make()
+        done = []
+        sh.on(KmeansDoneEvent, done.append)
+        with D.row_sharded():
+            cwr = sh.fit(w[r0:r1])
+        res = {
+            "cent": (sh.centroids.float() - ref.centroids.float()).abs().max().item(),
+            "idx": (cwr.idxs == ref_cwr.idxs[:, r0:r1]).float().mean().item(),
+            "iters": [d.iters_run for d in done] == [d.iters_run for d in ref_done],
+        }
+        torch.save(res, os.path.join(out_dir, f"grid{rank}.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_row_sharded_grid_fit_matches_single_process_gloo(tmp_path):
+    """The centroid-grid assignment inside a row-sharded fit (each rank grids
+    its own points against the shared centroids)."""
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    import torch.multiprocessing as mp
+
+    mp.spawn(_worker_grid, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    for r in range(2):
+        res = torch.load(os.path.join(str(tmp_path), f"grid{r}.pt"))
+        assert res["cent"] < 1e-5 and res["idx"] > 0.999 and res["iters"], res
