@@ -83,3 +83,28 @@ def test_exchange_layout_and_argument_checks_without_gpu():
     with pytest.raises(RuntimeError, match="null pointer"):
         _lib.call("skcq_list_points", None, 1, 256, None, None, None, None, None, 0, None)
     assert _lib.load().skcq_moved_lists_scratch_bytes(3, 8192, 4096) == 3 * (2 + 1) * 4
+
+
+def test_grid_cell_counts_stay_within_the_kernel_limits():
+    """The engine's cells-per-coordinate choice for the centroid grid
+    (about one centroid per cell) is accepted by the library for every block
+    size and centroid count it can be given, and the library rejects shapes
+    outside its limits (bs in 2..4, 2 <= G <= 256, bs (G - 1) <= 1024,
+    G^bs <= 2^20)."""
+    from skcq_b200 import _engine, _lib
+
+    lib = _lib.load()
+    for bs in (2, 3, 4):
+        for k in (_engine.GRID_MIN_K, 16384, 65536, 1 << 20):
+            G = _engine.grid_cells(bs, k)
+            assert 2 <= G <= 256 and bs * (G - 1) <= 1024 and G ** bs <= (1 << 20), (bs, k, G)
+            assert lib.skcq_assign_grid_scratch_bytes(4, 98304, k, bs, G) > 0, (bs, k, G)
+    assert _engine.grid_cells(4, 65536) == 16  # one centroid per cell at the layer's second residual
+    assert lib.skcq_assign_grid_scratch_bytes(4, 1024, 8192, 5, 8) == 0  # block size 5
+    assert lib.skcq_assign_grid_scratch_bytes(4, 1024, 8192, 4, 33) == 0  # 33^4 cells > 2^20
+    assert lib.skcq_assign_grid_scratch_bytes(4, 1024, 8192, 2, 257) == 0
+    assert lib.skcq_assign_grid_scratch_bytes(4, 1024, 8192, 4, 1) == 0
+    # the layout grows with every dimension it holds
+    a = lib.skcq_assign_grid_scratch_bytes(2, 98304, 65536, 4, 16)
+    assert lib.skcq_assign_grid_scratch_bytes(4, 98304, 65536, 4, 16) > a
+    assert lib.skcq_assign_grid_scratch_bytes(2, 2 * 98304, 65536, 4, 16) > a
