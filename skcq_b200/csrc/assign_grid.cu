@@ -453,8 +453,24 @@ __global__ void __launch_bounds__(GR_WARPS * 32) grid_search_kernel(GridSearchAr
 // over the problem's points 32 at a time and take the flagged ones.
 constexpr int GR_RING_MAX = 3;  // largest ring_max accepted
 
+// Score one candidate with the reference formula (exact_score, euclidean) and
+// keep it when it beats (best, bid): larger score, or equal with a lower index.
 template <int BS>
-__global__ void __launch_bounds__(GR_WARPS * 32) grid_ring_kernel(GridSearchArgs a) {
+__device__ __forceinline__ void grid_ring_take(const float (&x)[BS], float4 cv, float cn, int id, float& best,
+                                               int& bid) {
+  const float cc[4] = {cv.x, cv.y, cv.z, cv.w};
+  float dot = 0.f;
+#pragma unroll
+  for (int d = 0; d < BS; ++d) dot = __fmaf_rn(x[d], cc[d], dot);
+  const float s = -__fadd_rn(__fmul_rn(dot, -2.0f), cn);
+  if (s > best || (s == best && id < bid)) {
+    best = s;
+    bid = id;
+  }
+}
+
+template <int BS>
+__global__ void __launch_bounds__(GR_WARPS * 32, 4) grid_ring_kernel(GridSearchArgs a) {
   __shared__ float sb[GR_MAX_BND];
   const int b = blockIdx.y;
   if (a.active && !a.active[b]) return;
@@ -494,30 +510,43 @@ __global__ void __launch_bounds__(GR_WARPS * 32) grid_ring_kernel(GridSearchArgs
         }
         float best = -INFINITY;
         int bid = -1;
-        for (int run = lane; run < nruns; run += 32) {
-          int rr = run;
-          int64_t base = 0, mul = G;
+        // lane l takes runs l, l + 32, ...: the bounds of four of them are
+        // loaded together, then their candidates two at a time, so several
+        // L2 reads are in flight per lane
+        for (int run0 = lane; run0 < nruns; run0 += 4 * 32) {
+          int st[4], en[4];
 #pragma unroll
-          for (int d = 1; d < BS; ++d) {
-            const int w = hi[d] - lo[d] + 1;
-            base += (int64_t)(lo[d] + rr % w) * mul;
-            rr /= w;
-            mul *= G;
-          }
-          const int64_t c_lo = base + lo[0], c_hi = base + hi[0];
-          const int st = c_lo ? cpos[c_lo - 1] : 0, en = cpos[c_hi];
-          for (int t = st; t < en; ++t) {
-            const float4 cv = a.sc.csort[cbase + t];
-            const float cc[4] = {cv.x, cv.y, cv.z, cv.w};
-            float dot = 0.f;
+          for (int u = 0; u < 4; ++u) {
+            const int run = run0 + 32 * u;
+            st[u] = 0;
+            en[u] = 0;
+            if (run < nruns) {
+              int rr = run;
+              int64_t base = 0, mul = G;
 #pragma unroll
-            for (int d = 0; d < BS; ++d) dot = __fmaf_rn(x[d], cc[d], dot);
-            const float s = -__fadd_rn(__fmul_rn(dot, -2.0f), a.sc.csn[cbase + t]);  // exact_score, euclidean
-            const int id = a.sc.cid[cbase + t];
-            if (s > best || (s == best && id < bid)) {
-              best = s;
-              bid = id;
+              for (int d = 1; d < BS; ++d) {
+                const int w = hi[d] - lo[d] + 1;
+                base += (int64_t)(lo[d] + rr % w) * mul;
+                rr /= w;
+                mul *= G;
+              }
+              const int64_t c_lo = base + lo[0], c_hi = base + hi[0];
+              st[u] = c_lo ? cpos[c_lo - 1] : 0;
+              en[u] = cpos[c_hi];
             }
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            int t = st[u];
+            for (; t + 1 < en[u]; t += 2) {
+              const float4 c0 = a.sc.csort[cbase + t], c1 = a.sc.csort[cbase + t + 1];
+              const float n0 = a.sc.csn[cbase + t], n1 = a.sc.csn[cbase + t + 1];
+              const int i0 = a.sc.cid[cbase + t], i1 = a.sc.cid[cbase + t + 1];
+              grid_ring_take<BS>(x, c0, n0, i0, best, bid);
+              grid_ring_take<BS>(x, c1, n1, i1, best, bid);
+            }
+            if (t < en[u])
+              grid_ring_take<BS>(x, a.sc.csort[cbase + t], a.sc.csn[cbase + t], a.sc.cid[cbase + t], best, bid);
           }
         }
 #pragma unroll
